@@ -1,0 +1,408 @@
+"""Benchmark of the MoE-layer hot path: DeepSeek-V3 MoE layer, bf16, on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference]
+
+Workload (one "step" = one MoE layer over the whole token batch):
+  M = 32768 tokens in total, E = 256 experts, top_k = 8, hidden K = 7168,
+  moe_intermediate N = 2048; grouped_topk routing with sigmoid scores +
+  e_score_correction_bias ~N(0, 0.01), per-group top-2 sum, n_group = 8,
+  topk_group = 4, renormalise, routed scale 2.5; inputs ~N(0, 1), weights
+  ~N(0, 1/sqrt(fan_in)), random-initialised (synthetic data).
+At N = 1 the whole layer runs on one GPU. At N > 1 (one process per GPU,
+torchrun) the experts are split evenly over the ranks (expert parallel) and
+each rank holds M / N tokens: route -> NCCL all-to-all dispatch -> local
+expert path -> NCCL all-to-all combine (strong scaling, M fixed).
+
+Reported: tokens/s of the whole job (max over ranks of the CUDA-event time),
+a roofline entry for the dominant kernel (the tcgen05 gate/up GEMM, timed
+with CUDA events on its launch stream), an end-to-end figure through the
+public API with host buffers, the oracle timed on the host cores as a CPU
+baseline, and the SM clocks sampled during the timed region.
+
+--impl reference times the reference's CPU implementation of the path (its
+v0 algorithm, restated by the numpy oracle because the reference itself is
+Python that cannot be installed on the GPU host) on a bounded sample of the
+same workload, on all host cores.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "MoE-layer tokens/s, DeepSeek-V3 shape (E=256, top-8, K=7168, N=2048), bf16"
+UNIT = "tokens/s"
+DSV3 = dict(E=256, topk=8, K=7168, N=2048, n_group=8, topk_group=4, scale=2.5)
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["native", "reference"], default="native")
+    ap.add_argument("--tokens", type=int, default=32768, help="total tokens per step (all ranks)")
+    ap.add_argument("--skewed", action="store_true", help="bias +2.0 on 16 hot experts")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------------------- helpers
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def committed_traffic(kernel: str):
+    """Per-launch DRAM bytes from the committed ncu summary (profiles/traffic.json), scaled to this workload."""
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    d = json.loads(p.read_text()).get(kernel)
+    return d
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(prefix="clocks_", suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50",
+                 "-i", str(self.idx)], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        time.sleep(0.1)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in Path(self.path).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[4:8]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def make_inputs(M_local, rank, dev, skewed):
+    import torch
+
+    gen = torch.Generator(device=dev).manual_seed(1000 + rank)
+    x = torch.randn(M_local, DSV3["K"], generator=gen, device=dev).to(torch.bfloat16)
+    g = torch.randn(M_local, DSV3["E"], generator=gen, device=dev)
+    bgen = torch.Generator(device=dev).manual_seed(44)
+    bias = torch.randn(DSV3["E"], generator=bgen, device=dev) * 0.01
+    if skewed:
+        hot = torch.randperm(DSV3["E"], generator=torch.Generator().manual_seed(44))[:16]
+        bias[hot.to(dev)] += 2.0
+    return x, g, bias
+
+
+def make_weights(E_local, e0, dev):
+    """Expert weights ~N(0, 1/sqrt(fan_in)) in bf16; expert e's values depend only on e."""
+    import torch
+
+    K, N = DSV3["K"], DSV3["N"]
+    w1 = torch.empty(E_local, 2 * N, K, dtype=torch.bfloat16, device=dev)
+    w2 = torch.empty(E_local, K, N, dtype=torch.bfloat16, device=dev)
+    for i in range(E_local):
+        gen = torch.Generator(device=dev).manual_seed(43_000 + e0 + i)
+        w1[i].copy_(torch.randn(2 * N, K, generator=gen, device=dev) / K ** 0.5)
+        w2[i].copy_(torch.randn(K, N, generator=gen, device=dev) / N ** 0.5)
+    return w1, w2
+
+
+# ----------------------------------------------------------------------------- CPU (oracle) timing
+def cpu_oracle_tokens_per_s(sample_tokens: int, seed: int = 7):
+    """Time the oracle (v0 restated in numpy) on `sample_tokens` tokens of the DSv3 layer.
+
+    Expert weights come from a pool of 8 distinct fp32 weight sets (1.4 GB, larger
+    than any host last-level cache), assigned by expert id modulo 8, so every
+    expert's weights stream from host memory as they would for 256 resident experts.
+    Returns (tokens/s, seconds, cores).
+    """
+    import numpy as np
+
+    from oracle.fused_moe import silu
+    from oracle.grouped_topk import grouped_topk_ref
+
+    K, N, E, k = DSV3["K"], DSV3["N"], DSV3["E"], DSV3["topk"]
+    rng = np.random.default_rng(seed)
+    pool1 = [rng.standard_normal((2 * N, K), dtype=np.float32) / np.sqrt(K) for _ in range(8)]
+    pool2 = [rng.standard_normal((K, N), dtype=np.float32) / np.sqrt(N) for _ in range(8)]
+    x = rng.standard_normal((sample_tokens, K), dtype=np.float32)
+    g = rng.standard_normal((sample_tokens, E), dtype=np.float32)
+    bias = (rng.standard_normal(E, dtype=np.float32) * 0.01).astype(np.float32)
+    # warm the BLAS thread pool
+    _ = pool1[0][:64] @ x[:1].T
+    t0 = time.perf_counter()
+    w, ids = grouped_topk_ref(g, k, True, DSV3["n_group"], DSV3["topk_group"], "sigmoid", DSV3["scale"], bias,
+                              "top2sum")
+    out = np.zeros((sample_tokens, K), np.float32)
+    flat = ids.reshape(-1)
+    tok = np.repeat(np.arange(sample_tokens), k)
+    fw = w.reshape(-1)
+    for e in np.unique(flat):
+        rows = np.nonzero(flat == e)[0]
+        gu = x[tok[rows]] @ pool1[e % 8].T
+        act = silu(gu[:, :N]) * gu[:, N:]
+        y = act @ pool2[e % 8].T
+        np.add.at(out, tok[rows], y * fw[rows, None])
+    dt = time.perf_counter() - t0
+    return sample_tokens / dt, dt, len(os.sched_getaffinity(0))
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return  # the reference CPU path runs once, on rank 0
+    sample = 64
+    vals = []
+    for _ in range(max(0, args.warmup)):
+        cpu_oracle_tokens_per_s(8)
+    secs = []
+    for _ in range(args.steps):
+        v, dt, cores = cpu_oracle_tokens_per_s(sample)
+        vals.append(v)
+        secs.append(dt)
+    value = statistics.median(vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * statistics.median(secs),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"DeepSeek-V3 MoE layer sample of {sample} tokens (of {args.tokens})",
+                   "experts": DSV3["E"], "top_k": DSV3["topk"], "hidden": DSV3["K"],
+                   "intermediate": DSV3["N"], "routing": "sigmoid+bias, top-2 group sum, 4 of 8 groups, x2.5"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": f"{sample} tokens per step, numpy oracle (fp32) on {cores} host threads"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- GPU run
+def run_native(args):
+    import torch
+    import torch.distributed as dist
+
+    import kernelswift_competition_submission_b200 as pkg
+    from kernelswift_competition_submission_b200 import ops
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+    E, k, K, N = DSV3["E"], DSV3["topk"], DSV3["K"], DSV3["N"]
+    M_total = args.tokens
+    if M_total % world:
+        raise SystemExit("--tokens must divide by the GPU count")
+    M = M_total // world
+    x, g, bias = make_inputs(M, rank, dev, args.skewed)
+
+    if world == 1:
+        w1, w2 = make_weights(E, 0, dev)
+        out = torch.empty(M, K, dtype=torch.bfloat16, device=dev)
+        ws = torch.empty(ops.fused_moe_workspace_bytes(M, E, k, K, N), dtype=torch.uint8, device=dev)
+
+        def step(events=None):
+            w, ids = ops.grouped_topk(x, g, k, True, DSV3["n_group"], DSV3["topk_group"], "sigmoid", DSV3["scale"],
+                                      e_score_correction_bias=bias)
+            ops.fused_moe_staged(x, w1, w2, w, ids, out=out, workspace=ws, events=events)
+            return ids
+
+        layer = None
+        launches_per_step = 6  # grouped_topk, align count, align scatter, gemm1, gemm2, combine
+    else:
+        from kernelswift_competition_submission_b200.ep import ExpertParallelMoE
+
+        E_local = E // world
+        w1, w2 = make_weights(E_local, rank * E_local, dev)
+        layer = ExpertParallelMoE(w1, w2, num_experts=E, topk=k, num_expert_group=DSV3["n_group"],
+                                  topk_group=DSV3["topk_group"], scoring_func="sigmoid",
+                                  routed_scaling_factor=DSV3["scale"], e_score_correction_bias=bias)
+
+        def step(events=None):
+            return layer.forward(x, g, events=events)
+
+        launches_per_step = layer.kernel_launches_per_step
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+
+    stage_events = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for i in range(args.steps):
+        step(stage_events[i])
+    t1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    ms_local = t0.elapsed_time(t1)
+    gemm1_ms = [ev[1].elapsed_time(ev[2]) for ev in stage_events]
+    gemm2_ms = [ev[2].elapsed_time(ev[3]) for ev in stage_events]
+    ms = ms_local
+    if world > 1:
+        t = torch.tensor([ms_local], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_per_step = ms / args.steps
+    value = M_total * args.steps / (ms / 1e3)
+
+    # pairs and distinct experts of this rank's expert path (from the last step's routing)
+    if world == 1:
+        w_last, ids_last = ops.grouped_topk(x, g, k, True, DSV3["n_group"], DSV3["topk_group"], "sigmoid",
+                                            DSV3["scale"], e_score_correction_bias=bias)
+        pairs_local = M * k
+        distinct = int(torch.unique(ids_last).numel())
+    else:
+        pairs_local = layer.last_local_pairs
+        distinct = layer.last_local_experts
+
+    peaks = measured_peaks()
+    g1 = statistics.mean(gemm1_ms)
+    g1_flops = 4.0 * pairs_local * K * N
+    achieved = g1_flops / (g1 / 1e3) / 1e12
+    peak = peaks["bf16_tflops_sustained"]
+    tr = committed_traffic("moe_gemm1_silu")
+    traffic = None
+    if tr is not None:
+        traffic = tr["bytes_per_pair"] * pairs_local + tr.get("bytes_fixed", 0)
+    layer_flops = 6.0 * M_total * k * K * N
+    layer_bytes = distinct * 3 * K * N * 2 + M * K * 2 * 2 + M * k * 8 + M * E * 4
+
+    result = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"DeepSeek-V3 MoE layer, {M_total} tokens" + (" (skewed routing)" if args.skewed else ""),
+                   "tokens": M_total, "experts": E, "top_k": k, "hidden": K, "intermediate": N,
+                   "routing": "sigmoid+bias, top-2 group sum, 4 of 8 groups, x2.5",
+                   "parallelism": "single GPU" if world == 1 else f"expert parallel ep{world}",
+                   "l2": "inputs larger than L2 (x 470 MB, weights 22.5 GB); no flush"},
+        "roofline": {"kernel": "moe_gemm1_silu (tcgen05 gate/up GEMM + SiLU*mul)", "bound": "tensor",
+                     "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                     "peak_source": f"{peaks['source']} bf16_tflops_sustained",
+                     "traffic": traffic, "flops_per_launch": g1_flops, "ms_per_launch": g1,
+                     "gemm2_ms_per_launch": statistics.mean(gemm2_ms)},
+        "layer": {"tflops": layer_flops / (ms_per_step / 1e3) / 1e12, "flops_per_step": layer_flops,
+                  "alg_bytes_rank0": layer_bytes,
+                  "roofline_frac": (max(layer_flops / world / (peak * 1e12),
+                                        layer_bytes / (peaks["hbm_gbs"] * 1e9)) / (ms_per_step / 1e3))},
+        "clocks": clocks,
+        "gpu_launches": launches_per_step * args.steps,
+    }
+
+    # ---------------- end to end through the public API, host buffers
+    e2e = None
+    if world == 1:
+        xh = x.cpu().pin_memory()
+        gh = g.cpu().pin_memory()
+        oh = torch.empty(M, K, dtype=torch.bfloat16).pin_memory()
+        xd = torch.empty_like(x)
+        gd = torch.empty_like(g)
+        torch.cuda.synchronize()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        n = max(1, args.e2e_steps)
+        a.record()
+        for _ in range(n):
+            xd.copy_(xh, non_blocking=True)
+            gd.copy_(gh, non_blocking=True)
+            o = pkg.moe_layer(xd, gd, w1, w2, topk=k, renormalize=True, num_expert_group=DSV3["n_group"],
+                              topk_group=DSV3["topk_group"], scoring_func="sigmoid",
+                              routed_scaling_factor=DSV3["scale"], e_score_correction_bias=bias)
+            oh.copy_(o, non_blocking=True)
+        b.record()
+        torch.cuda.synchronize()
+        e2e_ms = a.elapsed_time(b) / n
+        e2e = {"value": M / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": xh.numel() * 2 + gh.numel() * 4,
+               "d2h_bytes_per_step": oh.numel() * 2, "ms_per_step": e2e_ms}
+    else:
+        e2e = layer.e2e(x, g, steps=max(1, args.e2e_steps))
+    result["e2e"] = e2e
+    pkg.check_device_status(dev)
+
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, dt, cores = cpu_oracle_tokens_per_s(64)
+        result["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
+                                  "sample": f"64 tokens of the layer, numpy oracle (fp32), {dt:.1f} s"}
+    if world > 1:
+        layer.close()
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_native(args)
+
+
+if __name__ == "__main__":
+    main()

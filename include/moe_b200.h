@@ -1,0 +1,170 @@
+/*
+ * moe_b200.h — C ABI of the B200 (sm_100a) MoE-layer hot path.
+ *
+ * The reference (kernelswift_competition_submission) exposes this path only as
+ * Python modules: `grouped_topk/v1/grouped_topk.py` (ModelNew.forward ->
+ * _grouped_topk_kernel) and `fused_moe/v1/fused_moe.py` (ModelNew.forward ->
+ * _moe_expert_kernel + _moe_reduce_kernel). Each entry point below replaces one
+ * of those launches; the Python layer of this project (ctypes) binds them the
+ * way the reference's ModelNew binds its Triton kernels.
+ *
+ * Conventions
+ *   - All data pointers are DEVICE pointers on the current CUDA device; sizes
+ *     are element counts; `stream` is a cudaStream_t passed as void* (NULL =
+ *     legacy default stream).
+ *   - Every function returns an int status (MOE_OK = 0). Argument errors are
+ *     detected on the host before any launch. Device-side failures (a bounded
+ *     wait that gave up) are recorded in the optional `status` word, a device
+ *     int the caller zeroes and reads after synchronising.
+ *   - No function allocates device memory; scratch comes from the caller's
+ *     workspace (see moe_fused_workspace_bytes).
+ *   - Inputs are never written.
+ */
+#ifndef MOE_B200_H
+#define MOE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MOE_API __attribute__((visibility("default")))
+#else
+#define MOE_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define MOE_OK 0
+#define MOE_ERR_INVALID_ARG 1 /* null pointer, negative size, unknown enum value */
+#define MOE_ERR_BAD_SHAPE 2   /* shape outside what the kernels support */
+#define MOE_ERR_UNSUPPORTED 3 /* dtype or rule not implemented */
+#define MOE_ERR_NOT_SM100 4   /* current device is not compute capability 10.x */
+#define MOE_ERR_WORKSPACE 5   /* workspace smaller than required */
+#define MOE_ERR_CUDA 6        /* a CUDA runtime call failed */
+#define MOE_ERR_TIMEOUT 7     /* a bounded device-side wait gave up */
+
+/* scoring_func */
+#define MOE_SCORING_SOFTMAX 0
+#define MOE_SCORING_SIGMOID 1
+/* group_score_mode */
+#define MOE_GROUP_SCORE_MAX 0      /* reference v0 rule: best expert of the group */
+#define MOE_GROUP_SCORE_TOP2_SUM 1 /* DeepSeek-V3 rule: sum of the group's two best */
+/* element types of hidden_states / w1 / w2 / out */
+#define MOE_DTYPE_BF16 0
+#define MOE_DTYPE_FP16 1
+
+/* Human-readable name of a status code (static string). */
+MOE_API const char* moe_status_string(int status);
+
+/* Library ABI version (major * 100 + minor). */
+MOE_API int moe_abi_version(void);
+
+/* MOE_OK when the current device is sm_100 (B200/GB200), else MOE_ERR_NOT_SM100
+ * or MOE_ERR_CUDA. */
+MOE_API int moe_check_device(void);
+
+/*
+ * grouped_topk routing.
+ * Replaces grouped_topk/v1/grouped_topk.py:210-235 (ModelNew.forward launching
+ * _grouped_topk_kernel); the rule is grouped_topk/v0/grouped_topk.py:91-132.
+ *
+ *   gating_output            fp32 [num_tokens, num_experts], row-major
+ *   e_score_correction_bias  fp32 [num_experts] or NULL (NULL = reference v0 rule)
+ *   topk_weights (out)       fp32 [num_tokens, topk]
+ *   topk_ids (out)           int32 [num_tokens, topk], sorted by score descending,
+ *                            ties broken by the lowest expert index
+ * Ranking uses scores (+ bias when given); weights are the scores without the
+ * bias, renormalised when `renormalize`, then multiplied by
+ * routed_scaling_factor. Supports num_experts <= 512, num_expert_group <= 32,
+ * topk <= 32 and topk <= topk_group * (num_experts / num_expert_group).
+ * The fused_moe routing of fused_moe/v0/fused_moe.py:134-139 is the special
+ * case num_expert_group = topk_group = 1, softmax, scale 1.
+ */
+MOE_API int moe_grouped_topk(const float* gating_output, const float* e_score_correction_bias,
+                     int64_t num_tokens, int num_experts, int topk, int renormalize,
+                     int num_expert_group, int topk_group, int scoring_func, int group_score_mode,
+                     float routed_scaling_factor, float* topk_weights, int32_t* topk_ids,
+                     void* stream);
+
+/*
+ * Token -> expert align stage (counting sort of (token, slot) pairs).
+ * Replaces the per-expert boolean masks of fused_moe/v0/fused_moe.py:143-159
+ * and the routing recomputation inside fused_moe/v1/fused_moe.py:182-197.
+ *
+ *   topk_ids      int32 [num_pairs]   (num_pairs = num_tokens * topk, row-major)
+ *   counts (out)  int32 [num_experts]
+ *   block_start (out) int32 [num_experts + 1]  prefix sum of ceil(count / block_m)
+ *   sorted_pairs (out) int32 [sorted_capacity]  pair id per padded row, -1 in padding;
+ *                 rows of expert e are [block_start[e] * block_m, block_start[e+1] * block_m)
+ *   scratch       int32 [num_experts + 1] device scratch (overwritten)
+ * sorted_capacity must be >= moe_align_capacity(num_pairs, num_experts, block_m).
+ * Order of pairs inside one expert's segment is unspecified.
+ */
+MOE_API int64_t moe_align_capacity(int64_t num_pairs, int num_experts, int block_m);
+MOE_API int moe_align(const int32_t* topk_ids, int64_t num_pairs, int num_experts, int block_m,
+              int32_t* counts, int32_t* block_start, int32_t* sorted_pairs, int64_t sorted_capacity,
+              int32_t* scratch, void* stream);
+
+/*
+ * Expert computation of fused_moe for given routing.
+ * Replaces fused_moe/v1/fused_moe.py:305-341 (ModelNew.forward after routing:
+ * _moe_expert_kernel + _moe_reduce_kernel); the math is
+ * fused_moe/v0/fused_moe.py:141-167:
+ *   out[t] = sum_j topk_weights[t, j] * (silu(x[t] W1g^T) * (x[t] W1u^T)) W2^T,
+ *   with expert e = topk_ids[t, j], W1g = w1[e, :N, :], W1u = w1[e, N:, :], W2 = w2[e].
+ *
+ *   dtype          MOE_DTYPE_BF16 or MOE_DTYPE_FP16 (x, w1, w2, out)
+ *   hidden_states  [num_tokens, hidden_size]
+ *   w1             [num_experts, 2 * intermediate_size, hidden_size]
+ *   w2             [num_experts, hidden_size, intermediate_size]
+ *   topk_weights   fp32 [num_tokens, topk]
+ *   topk_ids       int32 [num_tokens, topk], values in [0, num_experts)
+ *   out            [num_tokens, hidden_size]
+ *   workspace      device buffer of >= moe_fused_workspace_bytes(...) bytes, 256-B aligned
+ *   status         optional device int (NULL allowed); a device-side timeout writes
+ *                  MOE_ERR_TIMEOUT there
+ * Requires hidden_size % 64 == 0 and intermediate_size % 64 == 0, all pointers
+ * 16-byte aligned. GEMMs run on tcgen05 tensor cores with TMA-fed operands and
+ * TMEM accumulators; SiLU*mul is fused into the gate/up GEMM epilogue.
+ */
+MOE_API size_t moe_fused_workspace_bytes(int64_t num_tokens, int num_experts, int topk, int hidden_size,
+                                 int intermediate_size);
+MOE_API int moe_fused_experts(int dtype, const void* hidden_states, const void* w1, const void* w2,
+                      const float* topk_weights, const int32_t* topk_ids, int64_t num_tokens,
+                      int num_experts, int topk, int hidden_size, int intermediate_size, void* out,
+                      void* workspace, size_t workspace_bytes, int* status, void* stream);
+
+/*
+ * The four stages of moe_fused_experts as separate calls on the same workspace
+ * (same arguments as moe_fused_experts), in this order:
+ *   moe_expert_align_gather  align stage + gather of each pair's token row into
+ *                            expert-sorted order (workspace)
+ *   moe_expert_gemm1         tcgen05 gate/up GEMM, SiLU*mul epilogue -> act (workspace)
+ *   moe_expert_gemm2         tcgen05 down GEMM, per-pair rows -> slot buffer (workspace)
+ *   moe_expert_combine       top-k weighted sum of the slot rows -> out
+ * moe_fused_experts(...) is exactly these four calls. They exist so a caller
+ * can interleave its own work (events, communication) between stages.
+ */
+MOE_API int moe_expert_align_gather(int dtype, const void* hidden_states, const int32_t* topk_ids,
+                                    int64_t num_tokens, int num_experts, int topk, int hidden_size,
+                                    int intermediate_size, void* workspace, size_t workspace_bytes,
+                                    void* stream);
+MOE_API int moe_expert_gemm1(int dtype, const void* w1, int64_t num_tokens, int num_experts, int topk,
+                             int hidden_size, int intermediate_size, void* workspace,
+                             size_t workspace_bytes, int* status, void* stream);
+MOE_API int moe_expert_gemm2(int dtype, const void* w2, int64_t num_tokens, int num_experts, int topk,
+                             int hidden_size, int intermediate_size, void* workspace,
+                             size_t workspace_bytes, int* status, void* stream);
+MOE_API int moe_expert_combine(int dtype, const float* topk_weights, const int32_t* topk_ids,
+                               int64_t num_tokens, int num_experts, int topk, int hidden_size,
+                               int intermediate_size, void* out, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOE_B200_H */

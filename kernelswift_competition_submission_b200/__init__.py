@@ -1,0 +1,27 @@
+"""B200-native (sm_100a) MoE-layer hot path: grouped_topk routing -> fused_moe.
+
+Public API (mirrors the reference's task signatures):
+
+    from kernelswift_competition_submission_b200 import grouped_topk, fused_moe
+    w, ids = grouped_topk(hidden_states, gating_output, topk, renormalize,
+                          num_expert_group, topk_group, scoring_func,
+                          routed_scaling_factor, e_score_correction_bias)
+    out = fused_moe(hidden_states, w1, w2, w, ids)
+
+Drop-in task modules with the reference harness contract (``ModelNew``,
+``get_inputs``, ``get_init_inputs``) live in ``tasks/``; the expert-parallel
+layer is in ``ep``.
+"""
+
+from .ops import (  # noqa: F401
+    check_device_status,
+    fused_moe,
+    fused_moe_workspace_bytes,
+    grouped_topk,
+    moe_align,
+    moe_layer,
+    softmax_topk,
+)
+
+__all__ = ["grouped_topk", "fused_moe", "softmax_topk", "moe_align", "moe_layer", "fused_moe_workspace_bytes",
+           "check_device_status"]

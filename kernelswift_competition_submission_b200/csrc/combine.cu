@@ -1,0 +1,61 @@
+// Top-k combine: out[t] = sum_j topk_weights[t, j] * y[t * topk + j], accumulated in
+// fp32 and rounded once to the output type. This is the weighted reduction of
+// fused_moe/v0/fused_moe.py:165-167 and the E-reduction kernel of
+// fused_moe/v1/fused_moe.py:221-252, reduced over the topk slots instead of all
+// experts (the reference's own pending idea, fused_moe/README.md "partial[TOP_K,T,H]").
+// Each thread owns 8 consecutive hidden elements (one 16-byte vector) of a token;
+// slot rows of a token are contiguous, so every load and store is coalesced.
+#include "common.cuh"
+#include "moe_internal.h"
+
+namespace moe {
+namespace {
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+combine_kernel(const uint4* __restrict__ y, const float* __restrict__ w, const int32_t* __restrict__ ids, int64_t M,
+               int topk, int E, int vecs_per_row, uint4* __restrict__ out) {
+  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t t = gid / vecs_per_row;
+  const int v = (int)(gid - t * vecs_per_row);
+  if (t >= M) return;
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int j = 0; j < topk; ++j) {
+    const int e = __ldg(ids + t * topk + j);
+    if (e < 0 || e >= E) continue;
+    const float wj = __ldg(w + t * topk + j);
+    const uint4 q = __ldg(y + (t * topk + j) * vecs_per_row + v);
+    const uint32_t u[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = ElemTraits<T>::unpack2(u[i]);
+      acc[2 * i] = fmaf(wj, f.x, acc[2 * i]);
+      acc[2 * i + 1] = fmaf(wj, f.y, acc[2 * i + 1]);
+    }
+  }
+  uint4 o;
+  o.x = ElemTraits<T>::pack2(acc[0], acc[1]);
+  o.y = ElemTraits<T>::pack2(acc[2], acc[3]);
+  o.z = ElemTraits<T>::pack2(acc[4], acc[5]);
+  o.w = ElemTraits<T>::pack2(acc[6], acc[7]);
+  out[t * vecs_per_row + v] = o;
+}
+
+}  // namespace
+
+cudaError_t launch_combine(int dtype, const void* y_slots, const float* topk_weights, const int32_t* topk_ids,
+                           int64_t M, int topk, int E, int K, void* out, cudaStream_t st) {
+  if (M == 0) return cudaSuccess;
+  const int vpr = K / 8;
+  const int64_t threads = M * vpr;
+  const unsigned blocks = (unsigned)ceil_div(threads, 256);
+  if (dtype == MOE_DTYPE_BF16)
+    combine_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(static_cast<const uint4*>(y_slots), topk_weights, topk_ids,
+                                                          M, topk, E, vpr, static_cast<uint4*>(out));
+  else
+    combine_kernel<__half><<<blocks, 256, 0, st>>>(static_cast<const uint4*>(y_slots), topk_weights, topk_ids, M,
+                                                   topk, E, vpr, static_cast<uint4*>(out));
+  return cudaGetLastError();
+}
+
+}  // namespace moe

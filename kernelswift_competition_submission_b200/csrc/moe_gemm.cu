@@ -1,0 +1,361 @@
+// Grouped expert GEMMs on sm_100a tensor cores (tcgen05 + TMEM + TMA).
+//
+// One persistent, warp-specialised kernel template serves both expert GEMMs of
+// fused_moe/v0/fused_moe.py:160-163:
+//   GEMM1_SILU : act[r, n]  = silu(x_r . w1[e, n]) * (x_r . w1[e, N + n])     (:160-162)
+//   GEMM2      : y[pair(r)] = act_r . w2[e]^T                                  (:163)
+// Rows r come from the align stage: pairs grouped by expert e in m-blocks of
+// 128 rows (block_start[e] .. block_start[e+1]).
+//
+// Tile = 128 rows x BN output columns, K consumed 64 elements (128 bytes) per
+// pipeline stage:
+//   warp 0      TMA producer: one elected lane loads the A box (128 x 64) and the
+//               B box(es) (BN x 64) of each stage, 128-byte swizzle, completion
+//               counted in bytes on the stage's `full` mbarrier.
+//   warp 1      MMA issuer: one lane issues 4 x tcgen05.mma (M=128, N=BN, K=16)
+//               per stage into a TMEM accumulator and commits the stage's
+//               `empty` mbarrier; after the last stage of a tile it commits
+//               `tmem_full` of that accumulator.
+//   warp 2      TMEM allocator (2 accumulators x BN fp32 columns).
+//   warps 4-7   epilogue: warp w reads TMEM lanes 32(w-4)..+31 (one row per
+//               thread) with tcgen05.ld, applies SiLU*mul (GEMM1) or the
+//               pair scatter (GEMM2), stores to global and releases the
+//               accumulator, so the epilogue of tile i overlaps the MMAs of i+1.
+// For GEMM1 the B tile stacks the gate rows [n0, n0+BN/2) over the up rows
+// [N+n0, N+n0+BN/2) of the same expert, so gate and up of column n land in
+// the same accumulator row and SiLU*mul needs no extra pass or weight copy.
+//
+// Tile order: expert-major, then n-block, then m-block fastest, so concurrently
+// running CTAs share the expert's B tile through L2.
+// All mbarrier waits are bounded (common.cuh); on a timeout every role stops,
+// the producer waits (bounded) for its copies in flight, the MMA warp waits for
+// its MMAs, and TMEM is freed before the CTA exits.
+#include "common.cuh"
+#include "moe_internal.h"
+
+#include <mutex>
+
+namespace moe {
+namespace {
+
+enum { MODE_GEMM1_SILU = 0, MODE_GEMM2 = 1 };
+
+constexpr int kThreads = 256;
+constexpr int kBK = 64;                    // K elements per stage (128 bytes of 16-bit data)
+constexpr int kATileBytes = kBlockM * kBK * 2;
+
+template <int BN, int STAGES>
+struct SmemLayout {
+  static constexpr int kBTileBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kATileBytes + kBTileBytes;
+  static constexpr int kBarOffset = STAGES * kStageBytes;
+  static constexpr int kNumBars = 2 * STAGES + 5;
+  static constexpr int kMiscOffset = kBarOffset + kNumBars * 8;
+  static constexpr int kBlockStartOffset = kMiscOffset + 16;
+  static int bytes(int E) { return 1024 + kBlockStartOffset + 4 * (E + 1); }
+};
+
+__device__ __forceinline__ void decode_tile(const int* s_bs, int E, int NB, int tile, int& e, int& nb, int& mb) {
+  int lo = 0, hi = E - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (s_bs[mid] * NB <= tile) lo = mid; else hi = mid - 1;
+  }
+  e = lo;
+  const int nblk = s_bs[lo + 1] - s_bs[lo];
+  const int local = tile - s_bs[lo] * NB;
+  nb = local / nblk;
+  mb = s_bs[lo] + (local - nb * nblk);
+}
+
+template <typename T, int MODE, int BN, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+moe_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                const int32_t* __restrict__ block_start, int E, int k_red, int n_out, int NB,
+                T* __restrict__ out, const int32_t* __restrict__ sorted_pairs, int* status) {
+  using L = SmemLayout<BN, STAGES>;
+  constexpr int BH = (MODE == MODE_GEMM1_SILU) ? BN / 2 : BN;   // rows per B box
+  constexpr uint32_t kTmemCols = 2 * BN;
+  constexpr uint32_t kIdesc = idesc_f16(kBlockM, BN, ElemTraits<T>::kFmt);
+  constexpr uint32_t kStageTx = L::kStageBytes;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* tmem_full = bars + 2 * STAGES;
+  uint64_t* tmem_empty = bars + 2 * STAGES + 2;
+  uint64_t* mma_done = bars + 2 * STAGES + 4;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + L::kMiscOffset);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(smem + L::kMiscOffset + 4);
+  int* s_bs = reinterpret_cast<int*>(smem + L::kBlockStartOffset);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  for (int i = threadIdx.x; i <= E; i += kThreads) s_bs[i] = __ldg(block_start + i);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    for (int a = 0; a < 2; ++a) { mbar_init(&tmem_full[a], 1); mbar_init(&tmem_empty[a], 128); }
+    mbar_init(mma_done, 1);
+    *s_abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) { tma_prefetch_desc(&map_a); tma_prefetch_desc(&map_b); }
+  if (warp == 2) { tmem_alloc(s_tmem, kTmemCols); tmem_relinquish(); }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *s_tmem;
+
+  const int total_tiles = s_bs[E] * NB;
+  const int num_kb = (k_red + kBK - 1) / kBK;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------ TMA producer
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, issued_parity = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+        int e, nb, mb;
+        decode_tile(s_bs, E, NB, tile, e, nb, mb);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, status, s_abort)) { ok = false; break; }
+          uint8_t* a_dst = smem + stage * L::kStageBytes;
+          uint8_t* b_dst = a_dst + kATileBytes;
+          mbar_arrive_expect_tx(&full[stage], kStageTx);
+          tma_load_2d(&map_a, &full[stage], a_dst, kb * kBK, mb * kBlockM);
+          if constexpr (MODE == MODE_GEMM1_SILU) {
+            tma_load_3d(&map_b, &full[stage], b_dst, kb * kBK, nb * BH, 2 * e);
+            tma_load_3d(&map_b, &full[stage], b_dst + BH * kBK * 2, kb * kBK, nb * BH, 2 * e + 1);
+          } else {
+            tma_load_3d(&map_b, &full[stage], b_dst, kb * kBK, nb * BN, e);
+          }
+          issued_mask |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      if (!ok) {
+        // drain: wait (bounded, ignoring the abort flag) for the last copy issued into each stage
+        for (int s = 0; s < STAGES; ++s)
+          if ((issued_mask >> s) & 1u) mbar_wait(&full[s], (issued_parity >> s) & 1u, nullptr, nullptr);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------ MMA issuer
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+        if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1, status, s_abort)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, status, s_abort)) { ok = false; break; }
+          tc_fence_after();
+          const uint8_t* a_src = smem + stage * L::kStageBytes;
+          const uint64_t a_desc = smem_desc_sw128(a_src);
+          const uint64_t b_desc = smem_desc_sw128(a_src + kATileBytes);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            // +32 bytes along K inside the 128-byte swizzled row = +2 in the address field
+            umma_f16(d_tmem, a_desc + 2 * k, b_desc + 2 * k, kIdesc, (kb | k) != 0);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        umma_commit(&tmem_full[acc]);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      }
+      // all MMAs issued by this thread complete before TMEM is freed
+      umma_commit(mma_done);
+      mbar_wait(mma_done, 0, nullptr, nullptr);
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------ epilogue
+    const int ew = warp - 4;
+    const int row = ew * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
+      int e, nb, mb;
+      decode_tile(s_bs, E, NB, tile, e, nb, mb);
+      // warp-uniform decision: tcgen05.ld below is .sync.aligned
+      if (!__all_sync(0xffffffffu, mbar_wait(&tmem_full[acc], acc_phase, status, s_abort))) break;
+      tc_fence_after();
+      const uint32_t t_row = tmem_base + ((uint32_t)(ew * 32) << 16) + (uint32_t)(acc * BN);
+      const int64_t grow = (int64_t)mb * kBlockM + row;
+      if constexpr (MODE == MODE_GEMM1_SILU) {
+        T* dst = out + grow * (int64_t)n_out + (int64_t)nb * BH;
+#pragma unroll 1
+        for (int c = 0; c < BH / 32; ++c) {
+          uint32_t g[32], u[32];
+          tmem_ld32(t_row + c * 32, g);
+          tmem_ld32(t_row + BH + c * 32, u);
+          tmem_wait_ld();
+          uint32_t packed[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float g0 = __uint_as_float(g[2 * i]), g1 = __uint_as_float(g[2 * i + 1]);
+            const float u0 = __uint_as_float(u[2 * i]), u1 = __uint_as_float(u[2 * i + 1]);
+            const float a0 = g0 / (1.0f + __expf(-g0)) * u0;
+            const float a1 = g1 / (1.0f + __expf(-g1)) * u1;
+            packed[i] = ElemTraits<T>::pack2(a0, a1);
+          }
+          uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            d4[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+        }
+      } else {
+        const int pair = __ldg(sorted_pairs + grow);
+        T* dst = out + (int64_t)(pair < 0 ? 0 : pair) * n_out + (int64_t)nb * BN;
+        const int cols = min(BN, n_out - nb * BN);
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld32(t_row + c * 32, v);
+          tmem_wait_ld();
+          if (pair >= 0 && c * 32 < cols) {
+            uint32_t packed[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              packed[i] = ElemTraits<T>::pack2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
+            uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              d4[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tmem_empty[acc]);
+      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// K-major operand map with a 64-element (128-byte) inner box and 128-byte swizzle.
+bool make_map(CUtensorMap* m, int dtype, const void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
+              uint32_t box_rows) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return false;
+  cuuint64_t gdim[3], gstr[2];
+  cuuint32_t box[3] = {kBK, box_rows, 1}, estr[3] = {1, 1, 1};
+  for (int i = 0; i < rank; ++i) gdim[i] = dims[i];
+  for (int i = 0; i < rank - 1; ++i) gstr[i] = strides_bytes[i];
+  const CUtensorMapDataType dt =
+      dtype == MOE_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  return enc(m, dt, rank, const_cast<void*>(base), gdim, gstr, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+constexpr int kStages = 4;
+
+template <typename T, int MODE, int BN>
+cudaError_t launch_gemm_t(const CUtensorMap& ma, const CUtensorMap& mb, const int32_t* block_start, int E, int k_red,
+                          int n_out, int NB, int64_t rows_cap, void* out, const int32_t* sorted_pairs, int* status,
+                          cudaStream_t st) {
+  using L = SmemLayout<BN, kStages>;
+  auto kern = moe_gemm_kernel<T, MODE, BN, kStages>;
+  const int smem = L::bytes(E);
+  cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (err != cudaSuccess) return err;
+  const int64_t tiles_cap = (rows_cap / kBlockM) * NB;
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(num_sms(), tiles_cap));
+  kern<<<grid, kThreads, smem, st>>>(ma, mb, block_start, E, k_red, n_out, NB, static_cast<T*>(out), sorted_pairs,
+                                     status);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_gemm1_silu(int dtype, const void* x_sorted, int64_t rows_cap, const void* w1, int E, int K, int N,
+                              const int32_t* block_start, void* act, int* status, cudaStream_t st) {
+  const int BN = (N % 128 == 0) ? 256 : 128;
+  const int BH = BN / 2;
+  CUtensorMap ma, mbm;
+  const uint64_t a_dims[2] = {(uint64_t)K, (uint64_t)rows_cap};
+  const uint64_t a_str[1] = {(uint64_t)K * 2};
+  const uint64_t b_dims[3] = {(uint64_t)K, (uint64_t)N, (uint64_t)2 * E};
+  const uint64_t b_str[2] = {(uint64_t)K * 2, (uint64_t)N * K * 2};
+  if (!make_map(&ma, dtype, x_sorted, 2, a_dims, a_str, kBlockM)) return cudaErrorInvalidValue;
+  if (!make_map(&mbm, dtype, w1, 3, b_dims, b_str, (uint32_t)BH)) return cudaErrorInvalidValue;
+  const int NB = N / BH;
+  if (dtype == MOE_DTYPE_BF16) {
+    if (BN == 256)
+      return launch_gemm_t<__nv_bfloat16, MODE_GEMM1_SILU, 256>(ma, mbm, block_start, E, K, N, NB, rows_cap, act,
+                                                                nullptr, status, st);
+    return launch_gemm_t<__nv_bfloat16, MODE_GEMM1_SILU, 128>(ma, mbm, block_start, E, K, N, NB, rows_cap, act,
+                                                              nullptr, status, st);
+  }
+  if (BN == 256)
+    return launch_gemm_t<__half, MODE_GEMM1_SILU, 256>(ma, mbm, block_start, E, K, N, NB, rows_cap, act, nullptr,
+                                                       status, st);
+  return launch_gemm_t<__half, MODE_GEMM1_SILU, 128>(ma, mbm, block_start, E, K, N, NB, rows_cap, act, nullptr,
+                                                     status, st);
+}
+
+cudaError_t launch_gemm2_scatter(int dtype, const void* act, int64_t rows_cap, const void* w2, int E, int K, int N,
+                                 const int32_t* block_start, const int32_t* sorted_pairs, int64_t num_pairs,
+                                 void* y_slots, int* status, cudaStream_t st) {
+  (void)num_pairs;
+  const int BN = (K >= 256) ? 256 : 128;
+  CUtensorMap ma, mbm;
+  const uint64_t a_dims[2] = {(uint64_t)N, (uint64_t)rows_cap};
+  const uint64_t a_str[1] = {(uint64_t)N * 2};
+  const uint64_t b_dims[3] = {(uint64_t)N, (uint64_t)K, (uint64_t)E};
+  const uint64_t b_str[2] = {(uint64_t)N * 2, (uint64_t)K * N * 2};
+  if (!make_map(&ma, dtype, act, 2, a_dims, a_str, kBlockM)) return cudaErrorInvalidValue;
+  if (!make_map(&mbm, dtype, w2, 3, b_dims, b_str, (uint32_t)BN)) return cudaErrorInvalidValue;
+  const int NB = (int)ceil_div(K, BN);
+  if (dtype == MOE_DTYPE_BF16) {
+    if (BN == 256)
+      return launch_gemm_t<__nv_bfloat16, MODE_GEMM2, 256>(ma, mbm, block_start, E, N, K, NB, rows_cap, y_slots,
+                                                           sorted_pairs, status, st);
+    return launch_gemm_t<__nv_bfloat16, MODE_GEMM2, 128>(ma, mbm, block_start, E, N, K, NB, rows_cap, y_slots,
+                                                         sorted_pairs, status, st);
+  }
+  if (BN == 256)
+    return launch_gemm_t<__half, MODE_GEMM2, 256>(ma, mbm, block_start, E, N, K, NB, rows_cap, y_slots, sorted_pairs,
+                                                  status, st);
+  return launch_gemm_t<__half, MODE_GEMM2, 128>(ma, mbm, block_start, E, N, K, NB, rows_cap, y_slots, sorted_pairs,
+                                                status, st);
+}
+
+}  // namespace moe

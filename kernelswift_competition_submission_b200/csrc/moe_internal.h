@@ -1,0 +1,48 @@
+// Internal launch helpers shared by the C-ABI translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace moe {
+
+constexpr int kBlockM = 128;  // rows per m-block of the grouped GEMMs (one TMEM lane per row)
+
+// Metadata of the align stage. counts, cursor and done must be zero before the
+// launch; launch_align zeroes them itself.
+struct AlignMeta {
+  int32_t* counts;       // [E]     pairs per expert
+  int32_t* cursor;       // [E]     scratch: rows handed out per expert
+  int32_t* block_start;  // [E + 1] prefix sum of ceil(counts / block_m)
+  int32_t* done;         // [1]     scratch: CTAs finished counting
+};
+// Contiguous layout used by the fused path: [counts | cursor | done | block_start];
+// the first 2E + 1 ints are the ones zeroed before each launch.
+inline int64_t align_meta_ints(int E) { return 3 * (int64_t)E + 2; }
+inline AlignMeta align_meta_contiguous(int32_t* meta, int E) {
+  return AlignMeta{meta, meta + E, meta + 2 * E + 1, meta + 2 * E};
+}
+
+// Launches the align stage. When x_src != nullptr the scatter also copies each
+// pair's token row of `row_bytes` bytes from x_src into x_sorted at the pair's
+// padded row (x_sorted row pitch = row_bytes).
+cudaError_t launch_align(const int32_t* topk_ids, int64_t num_pairs, int topk, int E, int block_m, AlignMeta m,
+                         bool meta_contiguous, int32_t* sorted_pairs, int64_t sorted_capacity, const void* x_src,
+                         void* x_sorted, int64_t row_bytes, cudaStream_t st);
+
+// Weighted sum over the topk slots: out[t] = sum_j w[t, j] * y[t * topk + j]   (elem = bf16 / fp16).
+// Slots whose expert id is outside [0, E) contribute nothing (as in the reference's expert loop).
+cudaError_t launch_combine(int dtype, const void* y_slots, const float* topk_weights, const int32_t* topk_ids,
+                           int64_t M, int topk, int E, int K, void* out, cudaStream_t st);
+
+// Grouped GEMMs (sm_100a tcgen05). Rows come in m-blocks of kBlockM grouped by expert
+// (block_start from the align stage, total read on device).
+cudaError_t launch_gemm1_silu(int dtype, const void* x_sorted, int64_t rows_cap, const void* w1, int E, int K, int N,
+                              const int32_t* block_start, void* act, int* status, cudaStream_t st);
+cudaError_t launch_gemm2_scatter(int dtype, const void* act, int64_t rows_cap, const void* w2, int E, int K, int N,
+                                 const int32_t* block_start, const int32_t* sorted_pairs, int64_t num_pairs,
+                                 void* y_slots, int* status, cudaStream_t st);
+
+int num_sms();
+
+}  // namespace moe

@@ -1,0 +1,251 @@
+"""Functional MoE-layer ops backed by the sm_100a C-ABI library.
+
+These are the call signatures the reference's tasks are built around:
+
+* ``grouped_topk(hidden_states, gating_output, topk, renormalize,
+  num_expert_group, topk_group, scoring_func="softmax",
+  routed_scaling_factor=1.0, e_score_correction_bias=None)`` — the rule of
+  ``grouped_topk/v0/grouped_topk.py:91-132`` (``Model.forward``), plus the
+  DeepSeek-V3 bias and per-group top-2 sum.
+* ``fused_moe(hidden_states, w1, w2, topk_weights, topk_ids)`` — the expert
+  path of ``fused_moe/v0/fused_moe.py:141-167``.
+* ``softmax_topk(router_logits, top_k, renormalize)`` — the routing block of
+  ``fused_moe/v0/fused_moe.py:134-139``.
+
+Device memory, streams and output allocation come from PyTorch; every kernel
+launch goes through ``libmoe_b200.so`` on torch's current CUDA stream. There is
+no CPU or PyTorch fallback: CPU tensors, a missing library or a non-sm_100
+device raise.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+_DTYPES = {torch.bfloat16: _lib.MOE_DTYPE_BF16, torch.float16: _lib.MOE_DTYPE_FP16}
+_status_words: dict[int, torch.Tensor] = {}
+
+
+def _ptr(t: torch.Tensor | None):
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require_cuda(name: str, *ts: torch.Tensor) -> torch.device:
+    dev = None
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError(f"{name}: tensors must be on a CUDA device (got {t.device}); there is no CPU path")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError(f"{name}: all tensors must be on the same device")
+    return dev
+
+
+def status_word(device: torch.device) -> torch.Tensor:
+    """Per-device int32 the kernels write MOE_ERR_TIMEOUT into if a bounded wait gives up."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    t = _status_words.get(idx)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        _status_words[idx] = t
+    return t
+
+
+def check_device_status(device: torch.device | None = None) -> None:
+    """Synchronise and raise if a kernel recorded a device-side failure; resets the word."""
+    device = device or torch.device("cuda", torch.cuda.current_device())
+    w = status_word(device)
+    code = int(w.item())
+    if code:
+        w.zero_()
+        _lib.check(code, "device status")
+
+
+def grouped_topk(
+    hidden_states: torch.Tensor,
+    gating_output: torch.Tensor,
+    topk: int,
+    renormalize: bool,
+    num_expert_group: int,
+    topk_group: int,
+    scoring_func: str = "softmax",
+    routed_scaling_factor: float = 1.0,
+    e_score_correction_bias: torch.Tensor | None = None,
+    group_score: str | None = None,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Grouped top-k routing; returns (topk_weights fp32 [M, topk], topk_ids int32 [M, topk]).
+
+    ``group_score`` defaults to "max" (the reference v0 rule) without a bias and
+    to "top2sum" (DeepSeek-V3) with one; either may be forced.
+    """
+    if hidden_states is not None and hidden_states.size(0) != gating_output.size(0):
+        raise AssertionError("hidden_states.size(0) != gating_output.size(0)")  # v0 :96
+    if scoring_func == "softmax":
+        sf = _lib.MOE_SCORING_SOFTMAX
+    elif scoring_func == "sigmoid":
+        sf = _lib.MOE_SCORING_SIGMOID
+    else:
+        raise ValueError(f"Unsupported scoring_func: {scoring_func}")
+    if group_score is None:
+        group_score = "max" if e_score_correction_bias is None else "top2sum"
+    gm = {"max": _lib.MOE_GROUP_SCORE_MAX, "top2sum": _lib.MOE_GROUP_SCORE_TOP2_SUM}[group_score]
+    dev = _require_cuda("grouped_topk", gating_output, e_score_correction_bias)
+    g = gating_output
+    if g.dtype != torch.float32:
+        g = g.float()
+    g = g.contiguous()
+    bias = None
+    if e_score_correction_bias is not None:
+        bias = e_score_correction_bias.to(torch.float32).contiguous()
+    M, E = g.shape
+    w = torch.empty(M, topk, dtype=torch.float32, device=dev)
+    ids = torch.empty(M, topk, dtype=torch.int32, device=dev)
+    lib = _lib.load()
+    _lib.check(
+        lib.moe_grouped_topk(_ptr(g), _ptr(bias), M, E, topk, int(bool(renormalize)), num_expert_group, topk_group,
+                             sf, gm, float(routed_scaling_factor), _ptr(w), _ptr(ids), _stream(dev)),
+        "moe_grouped_topk")
+    return w, ids
+
+
+def softmax_topk(router_logits: torch.Tensor, top_k: int, renormalize: bool = True):
+    """Mixtral routing (fused_moe/v0/fused_moe.py:134-139): one group, softmax, no scale."""
+    return grouped_topk(None, router_logits, top_k, renormalize, 1, 1, "softmax", 1.0)
+
+
+def moe_align(topk_ids: torch.Tensor, num_experts: int, block_m: int = 128):
+    """Counting sort of the (token, slot) pairs by expert (the align stage, exposed for tests).
+
+    Returns (counts int32 [E], block_start int32 [E+1], sorted_pairs int32 [capacity]).
+    """
+    dev = _require_cuda("moe_align", topk_ids)
+    ids = topk_ids.to(torch.int32).contiguous().view(-1)
+    lib = _lib.load()
+    P = ids.numel()
+    cap = lib.moe_align_capacity(P, num_experts, block_m)
+    counts = torch.empty(num_experts, dtype=torch.int32, device=dev)
+    block_start = torch.empty(num_experts + 1, dtype=torch.int32, device=dev)
+    sorted_pairs = torch.empty(max(cap, 1), dtype=torch.int32, device=dev)
+    scratch = torch.empty(num_experts + 1, dtype=torch.int32, device=dev)
+    _lib.check(
+        lib.moe_align(_ptr(ids), P, num_experts, block_m, _ptr(counts), _ptr(block_start), _ptr(sorted_pairs), cap,
+                      _ptr(scratch), _stream(dev)),
+        "moe_align")
+    return counts, block_start, sorted_pairs[:cap]
+
+
+def fused_moe_workspace_bytes(num_tokens: int, num_experts: int, topk: int, hidden_size: int,
+                              intermediate_size: int) -> int:
+    return int(_lib.load().moe_fused_workspace_bytes(num_tokens, num_experts, topk, hidden_size, intermediate_size))
+
+
+def fused_moe(
+    hidden_states: torch.Tensor,
+    w1: torch.Tensor,
+    w2: torch.Tensor,
+    topk_weights: torch.Tensor,
+    topk_ids: torch.Tensor,
+    *,
+    activation: str = "silu",
+    out: torch.Tensor | None = None,
+    workspace: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Expert path of the MoE layer for given routing.
+
+    hidden_states [M, K] (bf16/fp16), w1 [E, 2N, K], w2 [E, K, N] in the same
+    dtype, topk_weights [M, k] (any float dtype; used in fp32), topk_ids [M, k].
+    Returns out [M, K] = sum_j w[:, j] * (silu(x W1g^T) * (x W1u^T)) W2^T.
+    """
+    if activation != "silu":
+        raise ValueError(f"Unsupported activation: {activation}")
+    dev = _require_cuda("fused_moe", hidden_states, w1, w2, topk_weights, topk_ids)
+    dt = hidden_states.dtype
+    if dt not in _DTYPES:
+        raise TypeError(f"fused_moe: hidden_states dtype {dt} not supported (bf16 or fp16)")
+    if w1.dtype != dt or w2.dtype != dt:
+        raise TypeError("fused_moe: w1/w2 must have the dtype of hidden_states")
+    M, K = hidden_states.shape
+    E, twoN, K1 = w1.shape
+    N = twoN // 2
+    if K1 != K or tuple(w2.shape) != (E, K, N) or twoN != 2 * N:
+        raise ValueError(f"fused_moe: shape mismatch x{tuple(hidden_states.shape)} w1{tuple(w1.shape)} "
+                         f"w2{tuple(w2.shape)}")
+    k = topk_ids.shape[1]
+    if tuple(topk_weights.shape) != (M, k) or topk_ids.shape[0] != M:
+        raise ValueError("fused_moe: topk_weights / topk_ids must be [M, topk]")
+    x = hidden_states.contiguous()
+    w1c = w1.contiguous()
+    w2c = w2.contiguous()
+    tw = topk_weights.to(torch.float32).contiguous()
+    ti = topk_ids.to(torch.int32).contiguous()
+    if out is None:
+        out = torch.empty(M, K, dtype=dt, device=dev)
+    lib = _lib.load()
+    need = int(lib.moe_fused_workspace_bytes(M, E, k, K, N))
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=dev)
+    _lib.check(
+        lib.moe_fused_experts(_DTYPES[dt], _ptr(x), _ptr(w1c), _ptr(w2c), _ptr(tw), _ptr(ti), M, E, k, K, N,
+                              _ptr(out), _ptr(workspace), workspace.numel(), _ptr(status_word(dev)), _stream(dev)),
+        "moe_fused_experts")
+    return out
+
+
+def fused_moe_staged(hidden_states, w1, w2, topk_weights, topk_ids, *, out=None, workspace=None, events=None):
+    """``fused_moe`` issued as its four C-ABI stages (same kernels, same order).
+
+    ``events``: optional list of 5 ``torch.cuda.Event`` recorded on the current
+    stream before align, before GEMM1, before GEMM2, before combine and after
+    combine, so a caller can time each stage on the stream it runs on.
+    """
+    dev = _require_cuda("fused_moe_staged", hidden_states, w1, w2, topk_weights, topk_ids)
+    dt = _DTYPES[hidden_states.dtype]
+    M, K = hidden_states.shape
+    E, twoN, _ = w1.shape
+    N = twoN // 2
+    k = topk_ids.shape[1]
+    lib = _lib.load()
+    need = int(lib.moe_fused_workspace_bytes(M, E, k, K, N))
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=dev)
+    if out is None:
+        out = torch.empty(M, K, dtype=hidden_states.dtype, device=dev)
+    st = _stream(dev)
+    ws, wsn, status = _ptr(workspace), workspace.numel(), _ptr(status_word(dev))
+    tw = topk_weights.to(torch.float32).contiguous()
+    ti = topk_ids.to(torch.int32).contiguous()
+    ev = events or [None] * 5
+    if ev[0] is not None:
+        ev[0].record()
+    _lib.check(lib.moe_expert_align_gather(dt, _ptr(hidden_states), _ptr(ti), M, E, k, K, N, ws, wsn, st),
+               "moe_expert_align_gather")
+    if ev[1] is not None:
+        ev[1].record()
+    _lib.check(lib.moe_expert_gemm1(dt, _ptr(w1), M, E, k, K, N, ws, wsn, status, st), "moe_expert_gemm1")
+    if ev[2] is not None:
+        ev[2].record()
+    _lib.check(lib.moe_expert_gemm2(dt, _ptr(w2), M, E, k, K, N, ws, wsn, status, st), "moe_expert_gemm2")
+    if ev[3] is not None:
+        ev[3].record()
+    _lib.check(lib.moe_expert_combine(dt, _ptr(tw), _ptr(ti), M, E, k, K, N, _ptr(out), ws, wsn, st),
+               "moe_expert_combine")
+    if ev[4] is not None:
+        ev[4].record()
+    return out
+
+
+def moe_layer(hidden_states, gating_output, w1, w2, *, topk, renormalize=True, num_expert_group=1, topk_group=1,
+              scoring_func="softmax", routed_scaling_factor=1.0, e_score_correction_bias=None):
+    """grouped_topk routing feeding fused_moe: the whole MoE layer on the GPU."""
+    w, ids = grouped_topk(hidden_states, gating_output, topk, renormalize, num_expert_group, topk_group,
+                          scoring_func, routed_scaling_factor, e_score_correction_bias)
+    return fused_moe(hidden_states, w1, w2, w, ids)

@@ -1,0 +1,80 @@
+"""CPU: the drop-in task modules satisfy the reference harness's loading contract.
+
+The reference harness (bench/auto_bench.py:74-98, 143-178) executes only
+imports, class/function definitions and literal assignments at module level,
+then builds ``ModelNew(*get_init_inputs())`` and copies the v0 weights with
+``load_state_dict``. This test applies the same filtering rule (restated here)
+and checks the parameter names/shapes, and that a CPU forward fails loudly
+instead of silently running a fallback.
+"""
+import ast
+import types
+
+import pytest
+import torch
+
+from kernelswift_competition_submission_b200 import build
+
+TASKS = build.PKG / "tasks"
+
+
+def _is_literal(node):
+    if isinstance(node, ast.Constant):
+        return True
+    if isinstance(node, (ast.Tuple, ast.List, ast.Set)):
+        return all(_is_literal(e) for e in node.elts)
+    if isinstance(node, ast.Dict):
+        return all((k is None or _is_literal(k)) and _is_literal(v) for k, v in zip(node.keys, node.values))
+    if isinstance(node, ast.UnaryOp):
+        return _is_literal(node.operand)
+    return False
+
+
+def load_like_harness(path):
+    tree = ast.parse(path.read_text())
+    keep = []
+    for n in tree.body:
+        if isinstance(n, (ast.Import, ast.ImportFrom, ast.ClassDef, ast.FunctionDef, ast.AsyncFunctionDef)):
+            keep.append(n)
+        elif isinstance(n, ast.Assign) and _is_literal(n.value):
+            keep.append(n)
+    tree.body = keep
+    mod = types.ModuleType("_task_" + path.stem)
+    mod.__file__ = str(path)
+    exec(compile(ast.fix_missing_locations(tree), str(path), "exec"), mod.__dict__)
+    return mod
+
+
+def test_grouped_topk_task_module():
+    m = load_like_harness(TASKS / "grouped_topk.py")
+    model = m.ModelNew(*m.get_init_inputs())
+    assert model.state_dict() == {} or len(model.state_dict()) == 0
+    h, g = m.get_inputs()
+    assert h.device.type == "cpu" and g.shape == (83, 256) and g.dtype == torch.float32
+    with pytest.raises(RuntimeError, match="CUDA device"):
+        model(h, g)
+
+
+def test_fused_moe_task_module_state_dict_contract():
+    m = load_like_harness(TASKS / "fused_moe.py")
+    model = m.ModelNew(*m.get_init_inputs())
+    sd = model.state_dict()
+    assert set(sd) == {"w1", "w2"}
+    assert tuple(sd["w1"].shape) == (8, 128, 128) and tuple(sd["w2"].shape) == (8, 128, 64)
+    h, lg = m.get_inputs()
+    assert h.dtype == torch.float16 and h.device.type == "cpu"
+    with pytest.raises(RuntimeError, match="CUDA device"):
+        model(h, lg)
+
+
+def test_weight_cache_invalidates_on_update():
+    m = load_like_harness(TASKS / "fused_moe.py")
+    model = m.ModelNew(4, 2, 64, 64)
+    a1, _ = model._prepared_weights(torch.float16)
+    a2, _ = model._prepared_weights(torch.float16)
+    assert a1 is a2
+    with torch.no_grad():
+        model.w1.add_(1.0)
+    a3, _ = model._prepared_weights(torch.float16)
+    assert a3 is not a1
+    torch.testing.assert_close(a3.float(), model.w1.detach().half().float())

@@ -1,0 +1,29 @@
+"""fp32 PyTorch restatement of the reference's v0 expert path, for full-size GPU parity checks.
+
+Same steps as ``fused_moe/v0/fused_moe.py:141-167`` (and as ``oracle.fused_moe``),
+computed in fp32 on the GPU for a sample of token rows, so DeepSeek-V3-sized
+weights (22.5 GB) need not be copied to the host. TF32 is disabled.
+"""
+import torch
+
+
+def experts_rows_fp32(x, w1, w2, topk_weights, topk_ids, rows):
+    """out[rows] in fp32; x [M,K], w1 [E,2N,K], w2 [E,K,N] (any float dtype, on GPU)."""
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        rows = torch.as_tensor(rows, device=x.device, dtype=torch.long)
+        xs = x[rows].float()
+        ids = topk_ids[rows].long()
+        ws = topk_weights[rows].float()
+        N = w1.shape[1] // 2
+        out = torch.zeros(len(rows), x.shape[1], dtype=torch.float32, device=x.device)
+        for e in torch.unique(ids).tolist():
+            r, j = torch.nonzero(ids == e, as_tuple=True)
+            gu = xs[r] @ w1[e].float().T
+            act = torch.nn.functional.silu(gu[:, :N]) * gu[:, N:]
+            y = act @ w2[e].float().T
+            out.index_add_(0, r, y * ws[r, j][:, None])
+        return out
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
