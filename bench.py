@@ -52,6 +52,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["native", "reference"], default="native")
     ap.add_argument("--tokens", type=int, default=32768, help="total tokens per step (all ranks)")
+    ap.add_argument("--experts", type=int, default=256,
+                    help="number of experts (256 = DeepSeek-V3; fewer only for small profiling cases)")
     ap.add_argument("--skewed", action="store_true", help="bias +2.0 on 16 hot experts")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=5)
@@ -243,6 +245,9 @@ def run_native(args):
         from datetime import timedelta
 
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+    DSV3["E"] = args.experts
+    if args.experts % DSV3["n_group"]:
+        raise SystemExit("--experts must divide by 8 groups")
     E, k, K, N = DSV3["E"], DSV3["topk"], DSV3["K"], DSV3["N"]
     M_total = args.tokens
     if M_total % world:
@@ -336,7 +341,8 @@ def run_native(args):
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"DeepSeek-V3 MoE layer, {M_total} tokens" + (" (skewed routing)" if args.skewed else ""),
+        "config": {"workload": f"DeepSeek-V3 MoE layer, {M_total} tokens" + (" (skewed routing)" if args.skewed else "")
+                   + ("" if E == 256 else f" (reduced to {E} experts)"),
                    "tokens": M_total, "experts": E, "top_k": k, "hidden": K, "intermediate": N,
                    "routing": "sigmoid+bias, top-2 group sum, 4 of 8 groups, x2.5",
                    "parallelism": "single GPU" if world == 1 else f"expert parallel ep{world}",
