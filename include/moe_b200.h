@@ -45,6 +45,7 @@ extern "C" {
 #define MOE_ERR_WORKSPACE 5   /* workspace smaller than required */
 #define MOE_ERR_CUDA 6        /* a CUDA runtime call failed */
 #define MOE_ERR_TIMEOUT 7     /* a bounded device-side wait gave up */
+#define MOE_ERR_SCRATCH_LIMIT 8 /* request exceeds the fixed scratch of moe_align_noalloc */
 
 /* scoring_func */
 #define MOE_SCORING_SOFTMAX 0
@@ -107,6 +108,38 @@ MOE_API int64_t moe_align_capacity(int64_t num_pairs, int num_experts, int block
 MOE_API int moe_align(const int32_t* topk_ids, int64_t num_pairs, int num_experts, int block_m,
               int32_t* counts, int32_t* block_start, int32_t* sorted_pairs, int64_t sorted_capacity,
               int32_t* scratch, void* stream);
+
+/*
+ * moe_align_noalloc: moe_align for callers that cannot allocate device memory.
+ * No counterpart in the reference (its align step is the per-expert Python
+ * loop of fused_moe/v0/fused_moe.py:155-159, which allocates freely).
+ *
+ * Who needs it: a caller whose device memory is owned by someone else, e.g.
+ * an inference engine that reserves nearly all of HBM up front for its own
+ * pools and does not allow side allocations, or a foreign-language binding
+ * that has no handle on the host framework's allocator, cannot produce the
+ * `scratch` buffer moe_align asks for. This entry point needs only the
+ * inputs and outputs: its scratch (one int per expert plus one counter) is a
+ * fixed array inside the library.
+ *
+ * Same arguments, outputs and ordering rules as moe_align, minus `scratch`.
+ * Limits and behaviour:
+ *   - num_experts <= MOE_NOALLOC_MAX_EXPERTS (1024); larger requests return
+ *     MOE_ERR_SCRATCH_LIMIT before anything is enqueued.
+ *   - The scratch array (4100 bytes) is held by every GPU that loads this
+ *     library until the process exits.
+ *   - The first call on a device looks up the array's device address with
+ *     cudaGetSymbolAddress (with that device current) and caches it; make that
+ *     first call before any stream capture.
+ *   - All calls share the one array. Each call zeroes what must start at zero
+ *     on its own stream, but calls that overlap on the GPU (different streams,
+ *     not ordered by events) race on it: serialise them.
+ *   - Calls no cudaMalloc, cudaFree or other allocating routine.
+ */
+#define MOE_NOALLOC_MAX_EXPERTS 1024
+MOE_API int moe_align_noalloc(const int32_t* topk_ids, int64_t num_pairs, int num_experts, int block_m,
+                              int32_t* counts, int32_t* block_start, int32_t* sorted_pairs,
+                              int64_t sorted_capacity, void* stream);
 
 /*
  * Expert computation of fused_moe for given routing.

@@ -22,6 +22,8 @@ MOE_ERR_NOT_SM100 = 4
 MOE_ERR_WORKSPACE = 5
 MOE_ERR_CUDA = 6
 MOE_ERR_TIMEOUT = 7
+MOE_ERR_SCRATCH_LIMIT = 8
+MOE_NOALLOC_MAX_EXPERTS = 1024
 
 MOE_SCORING_SOFTMAX = 0
 MOE_SCORING_SIGMOID = 1
@@ -44,6 +46,7 @@ SIGNATURES = {
     "moe_grouped_topk": (_i32, [_c_p, _c_p, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _f32, _c_p, _c_p, _c_p]),
     "moe_align_capacity": (_i64, [_i64, _i32, _i32]),
     "moe_align": (_i32, [_c_p, _i64, _i32, _i32, _c_p, _c_p, _c_p, _i64, _c_p, _c_p]),
+    "moe_align_noalloc": (_i32, [_c_p, _i64, _i32, _i32, _c_p, _c_p, _c_p, _i64, _c_p]),
     "moe_fused_workspace_bytes": (_sz, [_i64, _i32, _i32, _i32, _i32]),
     "moe_fused_experts": (_i32, [_i32, _c_p, _c_p, _c_p, _c_p, _c_p, _i64, _i32, _i32, _i32, _i32, _c_p, _c_p, _sz,
                                  _c_p, _c_p]),

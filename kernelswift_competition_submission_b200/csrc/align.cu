@@ -17,6 +17,7 @@
 #include "moe_internal.h"
 
 #include <algorithm>
+#include <mutex>
 
 namespace moe {
 namespace {
@@ -188,6 +189,59 @@ extern "C" int moe_align(const int32_t* topk_ids, int64_t num_pairs, int num_exp
     return MOE_ERR_INVALID_ARG;
   if (num_pairs > INT32_MAX) return MOE_ERR_BAD_SHAPE;
   if (sorted_capacity < moe_align_capacity(num_pairs, num_experts, block_m)) return MOE_ERR_WORKSPACE;
+  moe::AlignMeta m{counts, scratch, block_start, scratch + num_experts};
+  const cudaError_t err = moe::launch_align(topk_ids, num_pairs, 1, num_experts, block_m, m, false, sorted_pairs,
+                                            sorted_capacity, nullptr, nullptr, 0, static_cast<cudaStream_t>(stream));
+  return err == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
+}
+
+// ---------------------------------------------------------------------------
+// moe_align_noalloc: the align stage for callers that cannot hand this library
+// any device memory of their own.
+//
+// Its only scratch (one cursor per expert plus the CTA completion counter) is
+// the fixed array below, sized for MOE_NOALLOC_MAX_EXPERTS experts (4100 bytes).
+// Every GPU that loads this library holds it until the process exits. Host code
+// must not pass `g_noalloc_align_scratch` itself to a kernel (on the host that
+// name is only a stand-in); the device address is looked up once per device
+// with cudaGetSymbolAddress, on the first call made while that device is
+// current, and cached.
+namespace {
+
+static __device__ __align__(256) int32_t g_noalloc_align_scratch[MOE_NOALLOC_MAX_EXPERTS + 1];
+
+constexpr int kNoAllocMaxDevices = 64;
+int32_t* g_noalloc_scratch_ptr[kNoAllocMaxDevices];
+std::mutex g_noalloc_mutex;
+
+int noalloc_scratch(int32_t** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) return MOE_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_align_scratch) != cudaSuccess || p == nullptr) return MOE_ERR_CUDA;
+    g_noalloc_scratch_ptr[dev] = static_cast<int32_t*>(p);
+  }
+  *out = g_noalloc_scratch_ptr[dev];
+  return MOE_OK;
+}
+
+}  // namespace
+
+extern "C" int moe_align_noalloc(const int32_t* topk_ids, int64_t num_pairs, int num_experts, int block_m,
+                                 int32_t* counts, int32_t* block_start, int32_t* sorted_pairs,
+                                 int64_t sorted_capacity, void* stream) {
+  if (num_experts > MOE_NOALLOC_MAX_EXPERTS) return MOE_ERR_SCRATCH_LIMIT;
+  if (num_pairs < 0 || num_experts <= 0 || block_m <= 0 || block_m > 4096) return MOE_ERR_INVALID_ARG;
+  if (!counts || !block_start || (num_pairs > 0 && (!topk_ids || !sorted_pairs))) return MOE_ERR_INVALID_ARG;
+  if (num_pairs > INT32_MAX) return MOE_ERR_BAD_SHAPE;
+  if (sorted_capacity < moe_align_capacity(num_pairs, num_experts, block_m)) return MOE_ERR_WORKSPACE;
+  int32_t* scratch = nullptr;
+  const int rc = noalloc_scratch(&scratch);
+  if (rc != MOE_OK) return rc;
+  // cursor = scratch[0, E), done = scratch[E]; launch_align zeroes both (and counts)
+  // on `stream` before its kernels run, so the previous call's contents never leak in.
   moe::AlignMeta m{counts, scratch, block_start, scratch + num_experts};
   const cudaError_t err = moe::launch_align(topk_ids, num_pairs, 1, num_experts, block_m, m, false, sorted_pairs,
                                             sorted_capacity, nullptr, nullptr, 0, static_cast<cudaStream_t>(stream));

@@ -60,6 +60,7 @@ extern "C" const char* moe_status_string(int status) {
     case MOE_ERR_WORKSPACE: return "workspace too small";
     case MOE_ERR_CUDA: return "CUDA runtime error";
     case MOE_ERR_TIMEOUT: return "device-side wait timed out";
+    case MOE_ERR_SCRATCH_LIMIT: return "request exceeds the fixed scratch of the no-allocation entry point";
     default: return "unknown status";
   }
 }
