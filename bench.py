@@ -322,8 +322,7 @@ def run_native(args):
         pairs_local = M * k
         distinct = int(torch.unique(ids_last).numel())
     else:
-        pairs_local = layer.last_local_pairs
-        distinct = layer.last_local_experts
+        pairs_local, distinct = layer.local_work()
 
     peaks = measured_peaks()
     g1 = statistics.mean(gemm1_ms)
