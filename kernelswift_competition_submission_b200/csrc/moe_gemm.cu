@@ -33,7 +33,6 @@
 #include "common.cuh"
 #include "moe_internal.h"
 
-#include <mutex>
 
 namespace moe {
 namespace {
@@ -251,40 +250,6 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
 }
 
 // ---------------------------------------------------------------- host side
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn get_encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  });
-  return fn;
-}
-
-// K-major operand map with a 64-element (128-byte) inner box and 128-byte swizzle.
-bool make_map(CUtensorMap* m, int dtype, const void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
-              uint32_t box_rows) {
-  EncodeTiledFn enc = get_encode_fn();
-  if (!enc) return false;
-  cuuint64_t gdim[3], gstr[2];
-  cuuint32_t box[3] = {kBK, box_rows, 1}, estr[3] = {1, 1, 1};
-  for (int i = 0; i < rank; ++i) gdim[i] = dims[i];
-  for (int i = 0; i < rank - 1; ++i) gstr[i] = strides_bytes[i];
-  const CUtensorMapDataType dt =
-      dtype == MOE_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  return enc(m, dt, rank, const_cast<void*>(base), gdim, gstr, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 constexpr int kStages = 4;
 
 template <typename T, int MODE, int BN>
@@ -314,8 +279,8 @@ cudaError_t launch_gemm1_silu(int dtype, const void* x_sorted, int64_t rows_cap,
   const uint64_t a_str[1] = {(uint64_t)K * 2};
   const uint64_t b_dims[3] = {(uint64_t)K, (uint64_t)N, (uint64_t)2 * E};
   const uint64_t b_str[2] = {(uint64_t)K * 2, (uint64_t)N * K * 2};
-  if (!make_map(&ma, dtype, x_sorted, 2, a_dims, a_str, kBlockM)) return cudaErrorInvalidValue;
-  if (!make_map(&mbm, dtype, w1, 3, b_dims, b_str, (uint32_t)BH)) return cudaErrorInvalidValue;
+  if (!make_kmajor_map(&ma, dtype, x_sorted, 2, a_dims, a_str, kBlockM)) return cudaErrorInvalidValue;
+  if (!make_kmajor_map(&mbm, dtype, w1, 3, b_dims, b_str, (uint32_t)BH)) return cudaErrorInvalidValue;
   const int NB = N / BH;
   if (dtype == MOE_DTYPE_BF16) {
     if (BN == 256)
@@ -341,8 +306,8 @@ cudaError_t launch_gemm2_scatter(int dtype, const void* act, int64_t rows_cap, c
   const uint64_t a_str[1] = {(uint64_t)N * 2};
   const uint64_t b_dims[3] = {(uint64_t)N, (uint64_t)K, (uint64_t)E};
   const uint64_t b_str[2] = {(uint64_t)N * 2, (uint64_t)K * N * 2};
-  if (!make_map(&ma, dtype, act, 2, a_dims, a_str, kBlockM)) return cudaErrorInvalidValue;
-  if (!make_map(&mbm, dtype, w2, 3, b_dims, b_str, (uint32_t)BN)) return cudaErrorInvalidValue;
+  if (!make_kmajor_map(&ma, dtype, act, 2, a_dims, a_str, kBlockM)) return cudaErrorInvalidValue;
+  if (!make_kmajor_map(&mbm, dtype, w2, 3, b_dims, b_str, (uint32_t)BN)) return cudaErrorInvalidValue;
   const int NB = (int)ceil_div(K, BN);
   if (dtype == MOE_DTYPE_BF16) {
     if (BN == 256)

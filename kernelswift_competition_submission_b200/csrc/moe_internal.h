@@ -1,6 +1,7 @@
 // Internal launch helpers shared by the C-ABI translation units.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -35,13 +36,25 @@ cudaError_t launch_align(const int32_t* topk_ids, int64_t num_pairs, int topk, i
 cudaError_t launch_combine(int dtype, const void* y_slots, const float* topk_weights, const int32_t* topk_ids,
                            int64_t M, int topk, int E, int K, void* out, cudaStream_t st);
 
-// Grouped GEMMs (sm_100a tcgen05). Rows come in m-blocks of kBlockM grouped by expert
-// (block_start from the align stage, total read on device).
+// Grouped GEMMs, one CTA per tile (sm_100a tcgen05.mma.cta_group::1, token-major 128 x 256
+// tiles). Rows come in m-blocks of kBlockM grouped by expert (align with block_m = kBlockM;
+// block_start read on the device).
 cudaError_t launch_gemm1_silu(int dtype, const void* x_sorted, int64_t rows_cap, const void* w1, int E, int K, int N,
                               const int32_t* block_start, void* act, int* status, cudaStream_t st);
 cudaError_t launch_gemm2_scatter(int dtype, const void* act, int64_t rows_cap, const void* w2, int E, int K, int N,
                                  const int32_t* block_start, const int32_t* sorted_pairs, int64_t num_pairs,
                                  void* y_slots, int* status, cudaStream_t st);
+
+// Grouped GEMMs on SM pairs (sm_100a tcgen05.mma.cta_group::2, swap-AB). Rows are the
+// (token, slot) pairs grouped by expert without padding: expert e owns rows
+// [expert_off[e], expert_off[e+1]) (the align stage with block_m = 1); P rows in total.
+cudaError_t launch_pair_gemm1_silu(int dtype, const void* x_sorted, int64_t P, const void* w1, int E, int K, int N,
+                                   const int32_t* expert_off, void* act, int* status, cudaStream_t st);
+cudaError_t launch_pair_gemm2_scatter(int dtype, const void* act, int64_t P, const void* w2, int E, int K, int N,
+                                      const int32_t* expert_off, const int32_t* sorted_pairs, void* y_slots,
+                                      int* status, cudaStream_t st);
+bool make_kmajor_map(CUtensorMap* m, int dtype, const void* base, int rank, const uint64_t* dims,
+                     const uint64_t* strides_bytes, uint32_t box_rows);
 
 int num_sms();
 
