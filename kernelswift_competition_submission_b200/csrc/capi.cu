@@ -27,30 +27,15 @@ int device_is_sm100() {
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-// GEMM path, chosen from shapes alone (the routing is device data): when the
-// average expert receives at least this many (token, slot) pairs, the
-// token-major 1-CTA kernels (128-row m-blocks, tiles 128 x 256) run; below it
-// the swap-AB CTA-pair kernels (weights as the 256-row operand, tokens padded
-// only to 32) avoid padding every expert to 128 rows.
-#ifndef MOE_TOKEN_MAJOR_MIN_PAIRS
-#define MOE_TOKEN_MAJOR_MIN_PAIRS 256
-#endif
-inline bool use_token_major(int64_t P, int E) { return P >= (int64_t)MOE_TOKEN_MAJOR_MIN_PAIRS * E; }
-
 struct FusedLayout {
   size_t meta, sorted, x_sorted, act, y_slots, total;
   int64_t cap;
-  bool token_major;
-  int block_m;
 };
 
 FusedLayout fused_layout(int64_t M, int E, int topk, int K, int N) {
   FusedLayout l;
   const int64_t P = M * topk;
-  l.token_major = use_token_major(P, E);
-  l.block_m = l.token_major ? kBlockM : 1;
-  // token-major: each expert's rows padded to whole 128-row m-blocks; pair path: no padding
-  l.cap = l.token_major ? moe_align_capacity(P, E, kBlockM) : std::max<int64_t>(P, 1);
+  l.cap = moe_align_capacity(P, E, kBlockM);  // each expert's rows padded to whole 128-row m-blocks
   size_t off = 0;
   l.meta = off;     off = align_up(off + sizeof(int32_t) * (size_t)align_meta_ints(E), 256);
   l.sorted = off;   off = align_up(off + sizeof(int32_t) * (size_t)l.cap, 256);
@@ -155,7 +140,7 @@ extern "C" int moe_expert_align_gather(int dtype, const void* hidden_states, con
   if ((rc = workspace_views(workspace, workspace_bytes, num_tokens, num_experts, topk, hidden_size,
                             intermediate_size, &w)) != MOE_OK)
     return rc;
-  return cuda_status(launch_align(topk_ids, num_tokens * topk, topk, num_experts, w.l.block_m, w.am, true, w.sorted,
+  return cuda_status(launch_align(topk_ids, num_tokens * topk, topk, num_experts, kBlockM, w.am, true, w.sorted,
                                   w.l.cap, hidden_states, w.x_sorted, (int64_t)hidden_size * 2,
                                   static_cast<cudaStream_t>(stream)));
 }
@@ -172,12 +157,8 @@ extern "C" int moe_expert_gemm1(int dtype, const void* w1, int64_t num_tokens, i
   if ((rc = workspace_views(workspace, workspace_bytes, num_tokens, num_experts, topk, hidden_size,
                             intermediate_size, &w)) != MOE_OK)
     return rc;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (w.l.token_major)
-    return cuda_status(launch_gemm1_silu(dtype, w.x_sorted, w.l.cap, w1, num_experts, hidden_size, intermediate_size,
-                                         w.am.block_start, w.act, status, st));
-  return cuda_status(launch_pair_gemm1_silu(dtype, w.x_sorted, num_tokens * topk, w1, num_experts, hidden_size,
-                                            intermediate_size, w.am.block_start, w.act, status, st));
+  return cuda_status(launch_gemm1_silu(dtype, w.x_sorted, w.l.cap, w1, num_experts, hidden_size, intermediate_size,
+                                       w.am.block_start, w.act, status, static_cast<cudaStream_t>(stream)));
 }
 
 extern "C" int moe_expert_gemm2(int dtype, const void* w2, int64_t num_tokens, int num_experts, int topk,
@@ -192,12 +173,9 @@ extern "C" int moe_expert_gemm2(int dtype, const void* w2, int64_t num_tokens, i
   if ((rc = workspace_views(workspace, workspace_bytes, num_tokens, num_experts, topk, hidden_size,
                             intermediate_size, &w)) != MOE_OK)
     return rc;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (w.l.token_major)
-    return cuda_status(launch_gemm2_scatter(dtype, w.act, w.l.cap, w2, num_experts, hidden_size, intermediate_size,
-                                            w.am.block_start, w.sorted, num_tokens * topk, w.y_slots, status, st));
-  return cuda_status(launch_pair_gemm2_scatter(dtype, w.act, num_tokens * topk, w2, num_experts, hidden_size,
-                                               intermediate_size, w.am.block_start, w.sorted, w.y_slots, status, st));
+  return cuda_status(launch_gemm2_scatter(dtype, w.act, w.l.cap, w2, num_experts, hidden_size, intermediate_size,
+                                          w.am.block_start, w.sorted, num_tokens * topk, w.y_slots, status,
+                                          static_cast<cudaStream_t>(stream)));
 }
 
 extern "C" int moe_expert_combine(int dtype, const float* topk_weights, const int32_t* topk_ids, int64_t num_tokens,
@@ -232,20 +210,14 @@ extern "C" int moe_fused_experts(int dtype, const void* hidden_states, const voi
     return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int64_t P = num_tokens * topk;
-  cudaError_t err = launch_align(topk_ids, P, topk, num_experts, w.l.block_m, w.am, true, w.sorted, w.l.cap,
+  cudaError_t err = launch_align(topk_ids, P, topk, num_experts, kBlockM, w.am, true, w.sorted, w.l.cap,
                                  hidden_states, w.x_sorted, (int64_t)hidden_size * 2, st);
   if (err == cudaSuccess)
-    err = w.l.token_major ? launch_gemm1_silu(dtype, w.x_sorted, w.l.cap, w1, num_experts, hidden_size,
-                                              intermediate_size, w.am.block_start, w.act, status, st)
-                          : launch_pair_gemm1_silu(dtype, w.x_sorted, P, w1, num_experts, hidden_size,
-                                                   intermediate_size, w.am.block_start, w.act, status, st);
+    err = launch_gemm1_silu(dtype, w.x_sorted, w.l.cap, w1, num_experts, hidden_size, intermediate_size,
+                            w.am.block_start, w.act, status, st);
   if (err == cudaSuccess)
-    err = w.l.token_major ? launch_gemm2_scatter(dtype, w.act, w.l.cap, w2, num_experts, hidden_size,
-                                                 intermediate_size, w.am.block_start, w.sorted, P, w.y_slots, status,
-                                                 st)
-                          : launch_pair_gemm2_scatter(dtype, w.act, P, w2, num_experts, hidden_size,
-                                                      intermediate_size, w.am.block_start, w.sorted, w.y_slots,
-                                                      status, st);
+    err = launch_gemm2_scatter(dtype, w.act, w.l.cap, w2, num_experts, hidden_size, intermediate_size,
+                               w.am.block_start, w.sorted, P, w.y_slots, status, st);
   if (err == cudaSuccess)
     err = launch_combine(dtype, w.y_slots, topk_weights, topk_ids, num_tokens, topk, num_experts, hidden_size, out,
                          st);

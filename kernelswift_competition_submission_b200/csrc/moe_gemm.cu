@@ -43,11 +43,18 @@ constexpr int kThreads = 256;
 constexpr int kBK = 64;                    // K elements per stage (128 bytes of 16-bit data)
 constexpr int kATileBytes = kBlockM * kBK * 2;
 
+// Epilogue staging: each epilogue warp owns a [32 rows][64 columns] 16-bit tile
+// with a 144-byte row pitch (128 + 16), so the per-row 16-byte writes and the
+// per-segment 16-byte reads are both free of bank conflicts.
+constexpr int kEpiPitch = 144;
+constexpr int kEpiWarpBytes = 32 * kEpiPitch;
+
 template <int BN, int STAGES>
 struct SmemLayout {
   static constexpr int kBTileBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kATileBytes + kBTileBytes;
-  static constexpr int kBarOffset = STAGES * kStageBytes;
+  static constexpr int kEpiOffset = STAGES * kStageBytes;
+  static constexpr int kBarOffset = kEpiOffset + 4 * kEpiWarpBytes;
   static constexpr int kNumBars = 2 * STAGES + 5;
   static constexpr int kMiscOffset = kBarOffset + kNumBars * 8;
   static constexpr int kBlockStartOffset = kMiscOffset + 16;
@@ -180,8 +187,15 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
     }
   } else if (warp >= 4) {
     // ------------------------------------------------ epilogue
+    // Each warp owns TMEM lanes 32*ew .. +31 (= tile rows). Per group of 64 output
+    // columns: tcgen05.ld two 32-column chunks (one row per thread), convert, stage
+    // in the warp's shared tile, then store whole 128-byte row segments: lane l
+    // writes 16-byte chunk (l & 7) of row 4*i + (l >> 3), so one warp store covers
+    // four full segments instead of 32 half-sectors.
     const int ew = warp - 4;
-    const int row = ew * 32 + lane;
+    uint8_t* stage = smem + L::kEpiOffset + ew * kEpiWarpBytes;
+    const int st_r = lane >> 3, st_c = lane & 7;
+    constexpr int kGroups = (MODE == MODE_GEMM1_SILU ? BH : BN) / 64;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
@@ -191,52 +205,61 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
       if (!__all_sync(0xffffffffu, mbar_wait(&tmem_full[acc], acc_phase, status, s_abort))) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(ew * 32) << 16) + (uint32_t)(acc * BN);
-      const int64_t grow = (int64_t)mb * kBlockM + row;
-      if constexpr (MODE == MODE_GEMM1_SILU) {
-        T* dst = out + grow * (int64_t)n_out + (int64_t)nb * BH;
+      const int64_t row0 = (int64_t)mb * kBlockM + ew * 32;  // first tile row of this warp
+      int my_pair = 0;
+      if constexpr (MODE == MODE_GEMM2) my_pair = __ldg(sorted_pairs + row0 + lane);
 #pragma unroll 1
-        for (int c = 0; c < BH / 32; ++c) {
-          uint32_t g[32], u[32];
-          tmem_ld32(t_row + c * 32, g);
-          tmem_ld32(t_row + BH + c * 32, u);
-          tmem_wait_ld();
+      for (int g = 0; g < kGroups; ++g) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int c = 2 * g + h;  // 32-column chunk
           uint32_t packed[16];
+          if constexpr (MODE == MODE_GEMM1_SILU) {
+            uint32_t gt[32], up[32];
+            tmem_ld32(t_row + c * 32, gt);
+            tmem_ld32(t_row + BH + c * 32, up);
+            tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float g0 = __uint_as_float(g[2 * i]), g1 = __uint_as_float(g[2 * i + 1]);
-            const float u0 = __uint_as_float(u[2 * i]), u1 = __uint_as_float(u[2 * i + 1]);
-            const float a0 = g0 / (1.0f + __expf(-g0)) * u0;
-            const float a1 = g1 / (1.0f + __expf(-g1)) * u1;
-            packed[i] = ElemTraits<T>::pack2(a0, a1);
-          }
-          uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-            d4[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
-        }
-      } else {
-        const int pair = __ldg(sorted_pairs + grow);
-        T* dst = out + (int64_t)(pair < 0 ? 0 : pair) * n_out + (int64_t)nb * BN;
-        const int cols = min(BN, n_out - nb * BN);
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t v[32];
-          tmem_ld32(t_row + c * 32, v);
-          tmem_wait_ld();
-          if (pair >= 0 && c * 32 < cols) {
-            uint32_t packed[16];
+            for (int i = 0; i < 16; ++i) {
+              const float g0 = __uint_as_float(gt[2 * i]), g1 = __uint_as_float(gt[2 * i + 1]);
+              const float u0 = __uint_as_float(up[2 * i]), u1 = __uint_as_float(up[2 * i + 1]);
+              packed[i] = ElemTraits<T>::pack2(g0 / (1.0f + __expf(-g0)) * u0, g1 / (1.0f + __expf(-g1)) * u1);
+            }
+          } else {
+            uint32_t v[32];
+            tmem_ld32(t_row + c * 32, v);
+            tmem_wait_ld();
 #pragma unroll
             for (int i = 0; i < 16; ++i)
               packed[i] = ElemTraits<T>::pack2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
-            uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+          }
+          uint4* srow = reinterpret_cast<uint4*>(stage + lane * kEpiPitch + h * 64);
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-              d4[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+          for (int i = 0; i < 4; ++i)
+            srow[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+        }
+        if (g == kGroups - 1) {
+          // accumulator fully read: release it to the MMA warp before the last stores
+          tc_fence_before();
+          mbar_arrive(&tmem_empty[acc]);
+        }
+        __syncwarp();
+#pragma unroll
+        for (int it = 0; it < 8; ++it) {
+          const int r = 4 * it + st_r;
+          const uint4 val = *reinterpret_cast<const uint4*>(stage + r * kEpiPitch + st_c * 16);
+          if constexpr (MODE == MODE_GEMM1_SILU) {
+            T* dst = out + (row0 + r) * (int64_t)n_out + (int64_t)nb * BH + g * 64 + st_c * 8;
+            *reinterpret_cast<uint4*>(dst) = val;
+          } else {
+            const int pair = __shfl_sync(0xffffffffu, my_pair, r);
+            const int col = nb * BN + g * 64;
+            if (pair >= 0 && col < n_out)
+              *reinterpret_cast<uint4*>(out + (int64_t)pair * n_out + col + st_c * 8) = val;
           }
         }
+        __syncwarp();
       }
-      tc_fence_before();
-      mbar_arrive(&tmem_empty[acc]);
       if (++acc == 2) { acc = 0; acc_phase ^= 1; }
     }
   }

@@ -45,14 +45,6 @@ cudaError_t launch_gemm2_scatter(int dtype, const void* act, int64_t rows_cap, c
                                  const int32_t* block_start, const int32_t* sorted_pairs, int64_t num_pairs,
                                  void* y_slots, int* status, cudaStream_t st);
 
-// Grouped GEMMs on SM pairs (sm_100a tcgen05.mma.cta_group::2, swap-AB). Rows are the
-// (token, slot) pairs grouped by expert without padding: expert e owns rows
-// [expert_off[e], expert_off[e+1]) (the align stage with block_m = 1); P rows in total.
-cudaError_t launch_pair_gemm1_silu(int dtype, const void* x_sorted, int64_t P, const void* w1, int E, int K, int N,
-                                   const int32_t* expert_off, void* act, int* status, cudaStream_t st);
-cudaError_t launch_pair_gemm2_scatter(int dtype, const void* act, int64_t P, const void* w2, int E, int K, int N,
-                                      const int32_t* expert_off, const int32_t* sorted_pairs, void* y_slots,
-                                      int* status, cudaStream_t st);
 bool make_kmajor_map(CUtensorMap* m, int dtype, const void* base, int rank, const uint64_t* dims,
                      const uint64_t* strides_bytes, uint32_t box_rows);
 
