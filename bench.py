@@ -287,6 +287,7 @@ def run_native(args):
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
+        layer.profile = True  # per-phase CUDA events (negligible cost) for the breakdown below
 
     stage_events = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
     sampler = ClockSampler(local_rank)
@@ -323,6 +324,8 @@ def run_native(args):
         distinct = int(torch.unique(ids_last).numel())
     else:
         pairs_local, distinct = layer.local_work()
+        layer.profile = False
+        phases = layer.phase_breakdown()
 
     peaks = measured_peaks()
     g1 = statistics.mean(gemm1_ms)
@@ -358,6 +361,9 @@ def run_native(args):
         "clocks": clocks,
         "gpu_launches": launches_per_step * args.steps,
     }
+    if world > 1:
+        result["ep_phases_ms_rank0"] = phases
+        result["ep_local_pairs_rank0"] = pairs_local
 
     # ---------------- end to end through the public API, host buffers
     e2e = None

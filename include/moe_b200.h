@@ -196,6 +196,38 @@ MOE_API int moe_expert_combine(int dtype, const float* topk_weights, const int32
                                int intermediate_size, void* out, void* workspace,
                                size_t workspace_bytes, void* stream);
 
+/*
+ * Expert-parallel dispatch / combine (the reference has no multi-device code;
+ * these serve the expert-parallel form of the layer, experts split evenly over
+ * `world` ranks: rank d owns experts [d * experts_per_rank, (d+1) * experts_per_rank)).
+ * A token is sent once to each rank owning one of its top-k experts.
+ *
+ *   moe_ep_send_capacity  upper bound on rows one rank sends: num_tokens * min(topk, world)
+ *   moe_ep_plan           per-destination row counts: offsets int32 [world + 1] (row
+ *                         offset of each destination block in the send buffer) and
+ *                         counts int64 [world] (all-to-all split sizes);
+ *                         scratch int32 [2 * world + 1]
+ *   moe_ep_pack           copies each token's hidden row into its destination blocks of
+ *                         send_x [capacity, hidden_size]; send_meta int32 [capacity, 2*topk]
+ *                         holds the k expert ids in the destination's numbering (-1 when
+ *                         the destination does not own that slot's expert) followed by the
+ *                         k weights as fp32 bits; tok_rows int32 [num_tokens, world] records
+ *                         the send row of each (token, destination) or -1. Same scratch
+ *                         and offsets as the moe_ep_plan call before it, same stream.
+ *   moe_ep_combine        out[t] = sum over d with tok_rows[t, d] >= 0 of
+ *                         returned_rows[tok_rows[t, d]] (fp32 accumulation)
+ * Requires world <= 64, topk <= 32, hidden_size % 8 == 0.
+ */
+MOE_API int64_t moe_ep_send_capacity(int64_t num_tokens, int topk, int world);
+MOE_API int moe_ep_plan(const int32_t* topk_ids, int64_t num_tokens, int topk, int experts_per_rank,
+                        int world, int32_t* scratch, int32_t* offsets, int64_t* counts, void* stream);
+MOE_API int moe_ep_pack(int dtype, const void* hidden_states, const int32_t* topk_ids,
+                        const float* topk_weights, int64_t num_tokens, int hidden_size, int topk,
+                        int experts_per_rank, int world, int32_t* scratch, const int32_t* offsets,
+                        void* send_x, int32_t* send_meta, int32_t* tok_rows, void* stream);
+MOE_API int moe_ep_combine(int dtype, const void* returned_rows, const int32_t* tok_rows,
+                           int64_t num_tokens, int hidden_size, int world, void* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -54,6 +54,10 @@ SIGNATURES = {
     "moe_expert_gemm1": (_i32, [_i32, _c_p, _i64, _i32, _i32, _i32, _i32, _c_p, _sz, _c_p, _c_p]),
     "moe_expert_gemm2": (_i32, [_i32, _c_p, _i64, _i32, _i32, _i32, _i32, _c_p, _sz, _c_p, _c_p]),
     "moe_expert_combine": (_i32, [_i32, _c_p, _c_p, _i64, _i32, _i32, _i32, _i32, _c_p, _c_p, _sz, _c_p]),
+    "moe_ep_send_capacity": (_i64, [_i64, _i32, _i32]),
+    "moe_ep_plan": (_i32, [_c_p, _i64, _i32, _i32, _i32, _c_p, _c_p, _c_p, _c_p]),
+    "moe_ep_pack": (_i32, [_i32, _c_p, _c_p, _c_p, _i64, _i32, _i32, _i32, _i32, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p]),
+    "moe_ep_combine": (_i32, [_i32, _c_p, _c_p, _i64, _i32, _i32, _c_p, _c_p]),
 }
 
 _lib = None

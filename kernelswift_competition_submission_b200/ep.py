@@ -19,6 +19,10 @@ form of its MoE path (``grouped_topk`` routing feeding ``fused_moe``,
 5. send the partial rows back with the reverse splits and sum them per token in
    fp32.
 
+On CUDA tensors steps 2 and 5 are the library's kernels (``moe_ep_plan``,
+``moe_ep_pack``, ``moe_ep_combine``); on CPU tensors (the gloo tests) the
+same plan is restated with torch ops (``plan_dispatch``).
+
 Collectives go through ``torch.distributed`` (NCCL over NVLink/NVSwitch on
 B200; gloo in the CPU tests); no kernel waits on another rank. Every rank takes
 the same collective steps in the same order, including for empty splits.
@@ -82,10 +86,14 @@ class ExpertParallelMoE:
                              e_score_correction_bias=e_score_correction_bias)
         self.route_fn = route_fn or self._route_cuda
         self.expert_fn = expert_fn or self._experts_cuda
-        self.kernel_launches_per_step = 6  # routing, align count, align scatter, GEMM1, GEMM2, combine
-        self.last_local_pairs = 0
-        self.last_local_experts = 0
+        # routing, EP count, EP pack, align count, align scatter, GEMM1, GEMM2, combine, EP combine
+        self.kernel_launches_per_step = 9
         self._ws = None
+        # per-phase CUDA events of each forward when `profile` is set (bench breakdown)
+        self.profile = False
+        self.phase_log = []
+        self._on_cuda = False
+        self._marks = []
 
     # ------------------------------------------------------------------ default (CUDA) stages
     def _route_cuda(self, x, gating):
@@ -110,33 +118,108 @@ class ExpertParallelMoE:
         return fused_moe_staged(x, self.w1, self.w2, w, ids, workspace=self._ws, events=events)
 
     # ------------------------------------------------------------------ forward
+    def _mark(self, name):
+        if self.profile and self._on_cuda:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            self._marks.append((name, ev))
+
     def forward(self, x: torch.Tensor, gating: torch.Tensor, events=None) -> torch.Tensor:
         M, K = x.shape
+        self._on_cuda = x.is_cuda
+        self._marks = []
+        self._mark("start")
         w, ids = self.route_fn(x, gating)
-        send_tok, send_counts, send_ids, send_w = plan_dispatch(ids, w, self.E_local, self.world)
+        self._mark("route")
+        if x.is_cuda:
+            send_x, send_meta, send_counts, tok_rows = self._dispatch_cuda(x, w, ids)
+        else:  # CPU tensors (gloo tests): the same plan restated with torch ops
+            send_tok, send_counts, send_ids, send_w = plan_dispatch(ids, w, self.E_local, self.world)
+            send_x = x.index_select(0, send_tok)
+            send_meta = torch.cat([send_ids, send_w.view(torch.int32)], dim=1).contiguous()
         recv_counts = torch.empty_like(send_counts)
         dist.all_to_all_single(recv_counts, send_counts, group=self.group)
         s_split = send_counts.tolist()
         r_split = recv_counts.tolist()
-        R = int(sum(r_split))
-        send_x = x.index_select(0, send_tok)
-        send_meta = torch.cat([send_ids, send_w.view(torch.int32)], dim=1).contiguous()
+        S, R = int(sum(s_split)), int(sum(r_split))
+        send_x, send_meta = send_x[:S], send_meta[:S]
         recv_x = torch.empty(R, K, dtype=x.dtype, device=x.device)
         recv_meta = torch.empty(R, 2 * self.topk, dtype=torch.int32, device=x.device)
+        self._mark("plan")
         dist.all_to_all_single(recv_x, send_x, output_split_sizes=r_split, input_split_sizes=s_split,
                                group=self.group)
         dist.all_to_all_single(recv_meta, send_meta, output_split_sizes=r_split, input_split_sizes=s_split,
                                group=self.group)
         recv_ids = recv_meta[:, : self.topk].contiguous()
         recv_w = recv_meta[:, self.topk:].contiguous().view(torch.float32)
+        self._mark("dispatch")
         partial = self.expert_fn(recv_x, recv_w, recv_ids, events=events)
-        back = torch.empty(int(send_tok.numel()), K, dtype=partial.dtype, device=x.device)
+        self._mark("experts")
+        back = torch.empty(S, K, dtype=partial.dtype, device=x.device)
         dist.all_to_all_single(back, partial.contiguous(), output_split_sizes=s_split, input_split_sizes=r_split,
                                group=self.group)
-        out = torch.zeros(M, K, dtype=torch.float32, device=x.device)
-        out.index_add_(0, send_tok, back.float())
+        self._mark("combine_a2a")
+        if x.is_cuda:
+            out = self._combine_cuda(back, tok_rows, M, K, x.dtype)
+        else:
+            out = torch.zeros(M, K, dtype=torch.float32, device=x.device)
+            out.index_add_(0, send_tok, back.float())
+            out = out.to(x.dtype)
+        self._mark("reduce")
         self._last_recv_ids = recv_ids
-        return out.to(x.dtype)
+        if self.profile and self._marks:
+            self.phase_log.append(self._marks)
+        return out
+
+    # ------------------------------------------------------------------ CUDA dispatch / combine
+    def _dispatch_cuda(self, x, w, ids):
+        """Count, scan and pack with the library's EP kernels (one host-visible output: the counts)."""
+        from . import _lib
+        from .ops import _DTYPES, _ptr, _stream
+
+        M, K = x.shape
+        lib = _lib.load()
+        cap = max(1, int(lib.moe_ep_send_capacity(M, self.topk, self.world)))
+        dev = x.device
+        key = (cap, K, x.dtype)
+        if getattr(self, "_buf_key", None) != key:
+            self._buf_key = key
+            self._send_x = torch.empty(cap, K, dtype=x.dtype, device=dev)
+            self._send_meta = torch.empty(cap, 2 * self.topk, dtype=torch.int32, device=dev)
+            self._scratch = torch.empty(2 * self.world + 1, dtype=torch.int32, device=dev)
+            self._offsets = torch.empty(self.world + 1, dtype=torch.int32, device=dev)
+            self._counts = torch.empty(self.world, dtype=torch.int64, device=dev)
+        tok_rows = torch.empty(M, self.world, dtype=torch.int32, device=dev)
+        xc = x.contiguous()
+        ids32 = ids.to(torch.int32).contiguous()
+        w32 = w.to(torch.float32).contiguous()
+        st = _stream(dev)
+        _lib.check(lib.moe_ep_plan(_ptr(ids32), M, self.topk, self.E_local, self.world, _ptr(self._scratch),
+                                   _ptr(self._offsets), _ptr(self._counts), st), "moe_ep_plan")
+        _lib.check(lib.moe_ep_pack(_DTYPES[x.dtype], _ptr(xc), _ptr(ids32), _ptr(w32), M, K, self.topk, self.E_local,
+                                   self.world, _ptr(self._scratch), _ptr(self._offsets), _ptr(self._send_x),
+                                   _ptr(self._send_meta), _ptr(tok_rows), st), "moe_ep_pack")
+        return self._send_x, self._send_meta, self._counts, tok_rows
+
+    def _combine_cuda(self, back, tok_rows, M, K, dtype):
+        from . import _lib
+        from .ops import _DTYPES, _ptr, _stream
+
+        out = torch.empty(M, K, dtype=dtype, device=back.device)
+        if back.numel() == 0:
+            back = torch.empty(1, K, dtype=dtype, device=back.device)  # valid pointer; no row is read
+        _lib.check(_lib.load().moe_ep_combine(_DTYPES[dtype], _ptr(back), _ptr(tok_rows), M, K, self.world, _ptr(out),
+                                              _stream(back.device)), "moe_ep_combine")
+        return out
+
+    def phase_breakdown(self):
+        """Mean ms per phase over the profiled forwards (synchronises)."""
+        torch.cuda.synchronize()
+        acc = {}
+        for marks in self.phase_log:
+            for (n0, e0), (n1, e1) in zip(marks, marks[1:]):
+                acc.setdefault(n1, []).append(e0.elapsed_time(e1))
+        return {k: sum(v) / len(v) for k, v in acc.items()}
 
     __call__ = forward
 
