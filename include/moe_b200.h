@@ -56,6 +56,7 @@ extern "C" {
 /* element types of hidden_states / w1 / w2 / out */
 #define MOE_DTYPE_BF16 0
 #define MOE_DTYPE_FP16 1
+#define MOE_DTYPE_FP32 2 /* FP8 quantiser inputs only */
 
 /* Human-readable name of a status code (static string). */
 MOE_API const char* moe_status_string(int status);
@@ -195,6 +196,45 @@ MOE_API int moe_expert_combine(int dtype, const float* topk_weights, const int32
                                int64_t num_tokens, int num_experts, int topk, int hidden_size,
                                int intermediate_size, void* out, void* workspace,
                                size_t workspace_bytes, void* stream);
+
+/*
+ * FP8 (e4m3) block quantisation, the w8a8 recipe of the FP8 layer configuration
+ * (no counterpart in the reference, whose path is fp16/bf16/fp32 only):
+ *   scale = amax(|block|) / 448 (1.0 for an all-zero block), q = e4m3(x / scale),
+ *   rounded to nearest even, saturating at +-448.
+ *   moe_quantize_rows_fp8    per row, per 128 columns (activations, per token):
+ *                            x [num_rows, cols] -> q uint8 [num_rows, cols],
+ *                            scales fp32 [num_rows, cols / 128]
+ *   moe_quantize_blocks_fp8  per 128 x 128 block of each [rows, cols] matrix
+ *                            (expert weights): w [batch, rows, cols] -> q uint8
+ *                            [batch, rows, cols], scales fp32 [batch, rows/128, cols/128]
+ * dtype: MOE_DTYPE_BF16, MOE_DTYPE_FP16 or MOE_DTYPE_FP32. cols (and rows) % 128 == 0.
+ */
+MOE_API int moe_quantize_rows_fp8(int dtype, const void* x, int64_t num_rows, int cols, void* q,
+                                  float* scales, void* stream);
+MOE_API int moe_quantize_blocks_fp8(int dtype, const void* w, int64_t batch, int rows, int cols, void* q,
+                                    float* scales, void* stream);
+
+/*
+ * Expert computation of the FP8 w8a8 configuration (DeepSeek-V3 recipe; no
+ * counterpart in the reference, which has no FP8 code): the math of
+ * moe_fused_experts on dequantised operands.
+ *   hidden_states  bf16 [num_tokens, hidden_size]; quantised here per token per 128
+ *   w1_q, w1_scale e4m3 [E, 2N, K] and fp32 [E, 2N/128, K/128] (moe_quantize_blocks_fp8)
+ *   w2_q, w2_scale e4m3 [E, K, N]  and fp32 [E, K/128, N/128]
+ *   out            bf16 [num_tokens, hidden_size]
+ * The SiLU*mul output is quantised per row per 128 before the down projection.
+ * e4m3 tiles stream from HBM at one byte per element and are dequantised to
+ * bf16 in shared memory for the tcgen05 MMA (fp32 accumulate). Requires
+ * hidden_size % 128 == 0 and intermediate_size % 128 == 0, both <= 16384.
+ */
+MOE_API size_t moe_fused_workspace_bytes_fp8(int64_t num_tokens, int num_experts, int topk, int hidden_size,
+                                             int intermediate_size);
+MOE_API int moe_fused_experts_fp8(const void* hidden_states, const void* w1_q, const float* w1_scale,
+                                  const void* w2_q, const float* w2_scale, const float* topk_weights,
+                                  const int32_t* topk_ids, int64_t num_tokens, int num_experts, int topk,
+                                  int hidden_size, int intermediate_size, void* out, void* workspace,
+                                  size_t workspace_bytes, int* status, void* stream);
 
 /*
  * Expert-parallel dispatch / combine (the reference has no multi-device code;

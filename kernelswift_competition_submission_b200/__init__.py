@@ -16,12 +16,15 @@ layer is in ``ep``.
 from .ops import (  # noqa: F401
     check_device_status,
     fused_moe,
+    fused_moe_fp8,
     fused_moe_workspace_bytes,
     grouped_topk,
     moe_align,
     moe_layer,
+    quantize_rows_fp8,
+    quantize_weights_fp8,
     softmax_topk,
 )
 
-__all__ = ["grouped_topk", "fused_moe", "softmax_topk", "moe_align", "moe_layer", "fused_moe_workspace_bytes",
-           "check_device_status"]
+__all__ = ["grouped_topk", "fused_moe", "fused_moe_fp8", "softmax_topk", "moe_align", "moe_layer",
+           "fused_moe_workspace_bytes", "quantize_rows_fp8", "quantize_weights_fp8", "check_device_status"]

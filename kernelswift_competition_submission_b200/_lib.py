@@ -31,6 +31,7 @@ MOE_GROUP_SCORE_MAX = 0
 MOE_GROUP_SCORE_TOP2_SUM = 1
 MOE_DTYPE_BF16 = 0
 MOE_DTYPE_FP16 = 1
+MOE_DTYPE_FP32 = 2
 
 _c_p = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -54,6 +55,11 @@ SIGNATURES = {
     "moe_expert_gemm1": (_i32, [_i32, _c_p, _i64, _i32, _i32, _i32, _i32, _c_p, _sz, _c_p, _c_p]),
     "moe_expert_gemm2": (_i32, [_i32, _c_p, _i64, _i32, _i32, _i32, _i32, _c_p, _sz, _c_p, _c_p]),
     "moe_expert_combine": (_i32, [_i32, _c_p, _c_p, _i64, _i32, _i32, _i32, _i32, _c_p, _c_p, _sz, _c_p]),
+    "moe_quantize_rows_fp8": (_i32, [_i32, _c_p, _i64, _i32, _c_p, _c_p, _c_p]),
+    "moe_quantize_blocks_fp8": (_i32, [_i32, _c_p, _i64, _i32, _i32, _c_p, _c_p, _c_p]),
+    "moe_fused_workspace_bytes_fp8": (_sz, [_i64, _i32, _i32, _i32, _i32]),
+    "moe_fused_experts_fp8": (_i32, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _i64, _i32, _i32, _i32, _i32, _c_p,
+                                     _c_p, _sz, _c_p, _c_p]),
     "moe_ep_send_capacity": (_i64, [_i64, _i32, _i32]),
     "moe_ep_plan": (_i32, [_c_p, _i64, _i32, _i32, _i32, _c_p, _c_p, _c_p, _c_p]),
     "moe_ep_pack": (_i32, [_i32, _c_p, _c_p, _c_p, _i64, _i32, _i32, _i32, _i32, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p]),

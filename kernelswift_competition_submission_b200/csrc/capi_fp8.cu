@@ -1,0 +1,94 @@
+// C-ABI entry of the FP8 w8a8 expert path: quantise the token rows (per token
+// per 128) -> align -> gather e4m3 rows and scales -> FP8 GEMM1 (+ SiLU*mul +
+// per-row e4m3 quantisation of act) -> FP8 GEMM2 -> top-k combine.
+#include "common.cuh"
+#include "moe_internal.h"
+
+#include <algorithm>
+
+namespace moe {
+namespace {
+
+inline size_t up256(size_t v) { return (v + 255) / 256 * 256; }
+
+struct F8Layout2 {
+  size_t meta, sorted, xq, xs, xq_s, xs_s, actq, acts, y, total;
+  int64_t cap;
+};
+
+F8Layout2 fp8_layout(int64_t M, int E, int topk, int K, int N) {
+  F8Layout2 l;
+  const int64_t P = M * topk;
+  l.cap = moe_align_capacity(P, E, kBlockM);
+  size_t o = 0;
+  l.meta = o;  o = up256(o + 4 * (size_t)align_meta_ints(E));
+  l.sorted = o; o = up256(o + 4 * (size_t)l.cap);
+  l.xq = o;    o = up256(o + (size_t)M * K);
+  l.xs = o;    o = up256(o + 4 * (size_t)M * (K / 128));
+  l.xq_s = o;  o = up256(o + (size_t)l.cap * K);
+  l.xs_s = o;  o = up256(o + 4 * (size_t)l.cap * (K / 128));
+  l.actq = o;  o = up256(o + (size_t)l.cap * N);
+  l.acts = o;  o = up256(o + 4 * (size_t)l.cap * (N / 128));
+  l.y = o;     o = up256(o + 2 * (size_t)P * K);
+  l.total = o;
+  return l;
+}
+
+}  // namespace
+}  // namespace moe
+
+extern "C" size_t moe_fused_workspace_bytes_fp8(int64_t num_tokens, int num_experts, int topk, int hidden_size,
+                                                int intermediate_size) {
+  if (num_tokens < 0 || num_experts <= 0 || topk <= 0 || hidden_size <= 0 || intermediate_size <= 0) return 0;
+  return moe::fp8_layout(num_tokens, num_experts, topk, hidden_size, intermediate_size).total;
+}
+
+extern "C" int moe_fused_experts_fp8(const void* hidden_states, const void* w1_q, const float* w1_scale,
+                                     const void* w2_q, const float* w2_scale, const float* topk_weights,
+                                     const int32_t* topk_ids, int64_t num_tokens, int num_experts, int topk,
+                                     int hidden_size, int intermediate_size, void* out, void* workspace,
+                                     size_t workspace_bytes, int* status, void* stream) {
+  using namespace moe;
+  const int64_t M = num_tokens;
+  const int E = num_experts, K = hidden_size, N = intermediate_size;
+  if (M < 0 || E <= 0 || topk <= 0 || K <= 0 || N <= 0) return MOE_ERR_INVALID_ARG;
+  if (E > 1024 || topk > 64) return MOE_ERR_BAD_SHAPE;
+  if (K % 128 != 0 || N % 128 != 0) return MOE_ERR_BAD_SHAPE;
+  if (K > 16384 || N > 16384) return MOE_ERR_BAD_SHAPE;  // a tile stages at most 128 K-block scales
+  const int64_t P = M * topk;
+  if (P > INT32_MAX / 2) return MOE_ERR_BAD_SHAPE;
+  if (M == 0) return MOE_OK;
+  if (!hidden_states || !w1_q || !w1_scale || !w2_q || !w2_scale || !topk_weights || !topk_ids || !out || !workspace)
+    return MOE_ERR_INVALID_ARG;
+  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (!a16(hidden_states) || !a16(w1_q) || !a16(w2_q) || !a16(out) || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return MOE_ERR_INVALID_ARG;
+  const int dev_ok = moe_check_device();
+  if (dev_ok != MOE_OK) return dev_ok;
+  const F8Layout2 l = fp8_layout(M, E, topk, K, N);
+  if (workspace_bytes < l.total) return MOE_ERR_WORKSPACE;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int32_t* meta = reinterpret_cast<int32_t*>(ws + l.meta);
+  int32_t* sorted = reinterpret_cast<int32_t*>(ws + l.sorted);
+  const AlignMeta am = align_meta_contiguous(meta, E);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+  cudaError_t err = launch_quantize_rows(MOE_DTYPE_BF16, hidden_states, M, K, ws + l.xq,
+                                         reinterpret_cast<float*>(ws + l.xs), st);
+  if (err == cudaSuccess)
+    err = launch_align(topk_ids, P, topk, E, kBlockM, am, true, sorted, l.cap, nullptr, nullptr, 0, st);
+  if (err == cudaSuccess)
+    err = launch_gather_rows(ws + l.xq, K, sorted, am.block_start, E, topk, l.cap, ws + l.xq_s, st);
+  if (err == cudaSuccess)
+    err = launch_gather_rows(ws + l.xs, 4 * (int64_t)(K / 128), sorted, am.block_start, E, topk, l.cap, ws + l.xs_s,
+                             st);
+  if (err == cudaSuccess)
+    err = launch_fp8_gemm1(ws + l.xq_s, reinterpret_cast<const float*>(ws + l.xs_s), l.cap, w1_q, w1_scale, E, K, N,
+                           am.block_start, am.counts, ws + l.actq, reinterpret_cast<float*>(ws + l.acts), status, st);
+  if (err == cudaSuccess)
+    err = launch_fp8_gemm2(ws + l.actq, reinterpret_cast<const float*>(ws + l.acts), l.cap, w2_q, w2_scale, E, K, N,
+                           am.block_start, am.counts, sorted, ws + l.y, status, st);
+  if (err == cudaSuccess)
+    err = launch_combine(MOE_DTYPE_BF16, ws + l.y, topk_weights, topk_ids, M, topk, E, K, out, st);
+  return err == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
+}

@@ -173,6 +173,24 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, int ab_fmt) {
          | ((uint32_t)(M >> 4) << 24);      // M >> 4
 }
 
+// ---------------------------------------------------------------- named barriers
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+// AND of `pred` over the `threads` threads that reach named barrier `id`.
+__device__ __forceinline__ bool named_bar_and(int id, int threads, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 q, %3, 0;\n\t"
+      "barrier.cta.red.and.pred p, %1, %2, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"(id), "r"(threads), "r"((uint32_t)pred)
+      : "memory");
+  return r != 0;
+}
+
 // ---------------------------------------------------------------- element types
 template <typename T> struct ElemTraits;
 template <> struct ElemTraits<__nv_bfloat16> {

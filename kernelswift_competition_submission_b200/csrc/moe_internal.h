@@ -48,6 +48,23 @@ cudaError_t launch_gemm2_scatter(int dtype, const void* act, int64_t rows_cap, c
 bool make_kmajor_map(CUtensorMap* m, int dtype, const void* base, int rank, const uint64_t* dims,
                      const uint64_t* strides_bytes, uint32_t box_rows);
 
+bool make_fp8_map(CUtensorMap* m, const void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
+                  uint32_t box_rows);
+
+// FP8 path: e4m3 operands dequantised to bf16 in shared memory, tcgen05 bf16 MMA.
+cudaError_t launch_fp8_gemm1(const void* xq_sorted, const float* xs_sorted, int64_t rows_cap, const void* w1q,
+                             const float* w1s, int E, int K, int N, const int32_t* block_start,
+                             const int32_t* expert_counts, void* actq, float* acts, int* status, cudaStream_t st);
+cudaError_t launch_fp8_gemm2(const void* actq, const float* acts, int64_t rows_cap, const void* w2q, const float* w2s,
+                             int E, int K, int N, const int32_t* block_start, const int32_t* expert_counts,
+                             const int32_t* sorted_pairs, void* y_slots, int* status, cudaStream_t st);
+// dst[r] = src[sorted_pairs[r] / topk] (row_bytes each) for the rows the align stage filled.
+cudaError_t launch_gather_rows(const void* src, int64_t row_bytes, const int32_t* sorted_pairs,
+                               const int32_t* block_start, int E, int topk, int64_t cap, void* dst, cudaStream_t st);
+
+// Per row, per 128 columns e4m3 quantisation (dtype bf16 / fp16 / fp32 input).
+cudaError_t launch_quantize_rows(int dtype, const void* x, int64_t M, int K, uint8_t* q, float* s, cudaStream_t st);
+
 int num_sms();
 
 }  // namespace moe

@@ -156,6 +156,10 @@ def fused_moe(
     topk_ids: torch.Tensor,
     *,
     activation: str = "silu",
+    use_fp8_w8a8: bool = False,
+    w1_scale: torch.Tensor | None = None,
+    w2_scale: torch.Tensor | None = None,
+    block_shape=(128, 128),
     out: torch.Tensor | None = None,
     workspace: torch.Tensor | None = None,
 ) -> torch.Tensor:
@@ -164,9 +168,20 @@ def fused_moe(
     hidden_states [M, K] (bf16/fp16), w1 [E, 2N, K], w2 [E, K, N] in the same
     dtype, topk_weights [M, k] (any float dtype; used in fp32), topk_ids [M, k].
     Returns out [M, K] = sum_j w[:, j] * (silu(x W1g^T) * (x W1u^T)) W2^T.
+
+    With ``use_fp8_w8a8`` the weights are e4m3 with fp32 ``w1_scale`` /
+    ``w2_scale`` per 128 x 128 block (``quantize_weights_fp8``) and the token rows
+    are quantised per token per 128 on the fly (``fused_moe_fp8``).
     """
     if activation != "silu":
         raise ValueError(f"Unsupported activation: {activation}")
+    if use_fp8_w8a8:
+        if tuple(block_shape) != (128, 128):
+            raise ValueError("use_fp8_w8a8 supports block_shape (128, 128)")
+        if w1_scale is None or w2_scale is None:
+            raise ValueError("use_fp8_w8a8 needs w1_scale and w2_scale")
+        return fused_moe_fp8(hidden_states, w1, w1_scale, w2, w2_scale, topk_weights, topk_ids, out=out,
+                             workspace=workspace)
     dev = _require_cuda("fused_moe", hidden_states, w1, w2, topk_weights, topk_ids)
     dt = hidden_states.dtype
     if dt not in _DTYPES:
@@ -197,6 +212,75 @@ def fused_moe(
         lib.moe_fused_experts(_DTYPES[dt], _ptr(x), _ptr(w1c), _ptr(w2c), _ptr(tw), _ptr(ti), M, E, k, K, N,
                               _ptr(out), _ptr(workspace), workspace.numel(), _ptr(status_word(dev)), _stream(dev)),
         "moe_fused_experts")
+    return out
+
+
+def _fp8_bytes(t: torch.Tensor) -> torch.Tensor:
+    if t.dtype == torch.float8_e4m3fn:
+        return t.view(torch.uint8)
+    if t.dtype != torch.uint8:
+        raise TypeError(f"expected e4m3 data (torch.float8_e4m3fn or uint8), got {t.dtype}")
+    return t
+
+
+def quantize_rows_fp8(x: torch.Tensor):
+    """Per row, per 128 columns e4m3 quantisation: returns (q float8_e4m3fn [M, K], scales fp32 [M, K/128])."""
+    dev = _require_cuda("quantize_rows_fp8", x)
+    dt = {torch.bfloat16: _lib.MOE_DTYPE_BF16, torch.float16: _lib.MOE_DTYPE_FP16,
+          torch.float32: _lib.MOE_DTYPE_FP32}[x.dtype]
+    x = x.contiguous()
+    M, K = x.shape
+    q = torch.empty(M, K, dtype=torch.uint8, device=dev)
+    s = torch.empty(M, K // 128, dtype=torch.float32, device=dev)
+    _lib.check(_lib.load().moe_quantize_rows_fp8(dt, _ptr(x), M, K, _ptr(q), _ptr(s), _stream(dev)),
+               "moe_quantize_rows_fp8")
+    return q.view(torch.float8_e4m3fn), s
+
+
+def quantize_weights_fp8(w: torch.Tensor):
+    """Per 128 x 128 block e4m3 quantisation of [E, R, C] weights: (q float8_e4m3fn, scales fp32 [E, R/128, C/128])."""
+    dev = _require_cuda("quantize_weights_fp8", w)
+    dt = {torch.bfloat16: _lib.MOE_DTYPE_BF16, torch.float16: _lib.MOE_DTYPE_FP16,
+          torch.float32: _lib.MOE_DTYPE_FP32}[w.dtype]
+    w = w.contiguous()
+    E, R, C = w.shape
+    q = torch.empty(E, R, C, dtype=torch.uint8, device=dev)
+    s = torch.empty(E, R // 128, C // 128, dtype=torch.float32, device=dev)
+    _lib.check(_lib.load().moe_quantize_blocks_fp8(dt, _ptr(w), E, R, C, _ptr(q), _ptr(s), _stream(dev)),
+               "moe_quantize_blocks_fp8")
+    return q.view(torch.float8_e4m3fn), s
+
+
+def fused_moe_fp8(hidden_states, w1_q, w1_scale, w2_q, w2_scale, topk_weights, topk_ids, *, out=None,
+                  workspace=None):
+    """FP8 w8a8 expert path: bf16 tokens (quantised per token per 128 inside), e4m3 weights with
+    fp32 scales per 128 x 128 block (``quantize_weights_fp8``); returns bf16 [M, K]."""
+    dev = _require_cuda("fused_moe_fp8", hidden_states, w1_q, w2_q, w1_scale, w2_scale, topk_weights, topk_ids)
+    if hidden_states.dtype != torch.bfloat16:
+        raise TypeError("fused_moe_fp8: hidden_states must be bf16")
+    x = hidden_states.contiguous()
+    M, K = x.shape
+    w1b, w2b = _fp8_bytes(w1_q.contiguous()), _fp8_bytes(w2_q.contiguous())
+    E, twoN, _ = w1b.shape
+    N = twoN // 2
+    if tuple(w2b.shape) != (E, K, N) or tuple(w1_scale.shape) != (E, twoN // 128, K // 128) or \
+            tuple(w2_scale.shape) != (E, K // 128, N // 128):
+        raise ValueError("fused_moe_fp8: weight / scale shapes do not match")
+    k = topk_ids.shape[1]
+    tw = topk_weights.to(torch.float32).contiguous()
+    ti = topk_ids.to(torch.int32).contiguous()
+    s1 = w1_scale.to(torch.float32).contiguous()
+    s2 = w2_scale.to(torch.float32).contiguous()
+    if out is None:
+        out = torch.empty(M, K, dtype=torch.bfloat16, device=dev)
+    lib = _lib.load()
+    need = int(lib.moe_fused_workspace_bytes_fp8(M, E, k, K, N))
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=dev)
+    _lib.check(
+        lib.moe_fused_experts_fp8(_ptr(x), _ptr(w1b), _ptr(s1), _ptr(w2b), _ptr(s2), _ptr(tw), _ptr(ti), M, E, k, K, N,
+                                  _ptr(out), _ptr(workspace), workspace.numel(), _ptr(status_word(dev)), _stream(dev)),
+        "moe_fused_experts_fp8")
     return out
 
 

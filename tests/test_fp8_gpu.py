@@ -1,0 +1,105 @@
+"""GPU parity of the FP8 w8a8 path: e4m3 quantisers (bit-exact against the oracle) and the
+fused FP8 expert path (atol = rtol = 5e-2 against the fp32-accumulated reference on the same
+operands the kernel multiplies: the dequantised values q * s rounded to bf16).
+
+Why the reference rounds its operands: the SiLU*mul output is re-quantised to e4m3
+(3 mantissa bits); an operand 2**-9 off moves some outputs across a rounding boundary, and a
+one-ulp e4m3 flip is 12.5 % of that element, so exact and bf16-rounded operands disagree by
+more than the kernel's own error. The exact-operand oracle is checked too, on aggregate relative error."""
+import numpy as np
+import pytest
+import torch
+
+from kernelswift_competition_submission_b200 import (check_device_status, fused_moe, fused_moe_fp8, grouped_topk,
+                                                     quantize_rows_fp8, quantize_weights_fp8, softmax_topk)
+from oracle.fp8 import moe_experts_fp8_ref, quantize_blocks_128, quantize_rows_128
+from torch_ref import experts_rows_fp8
+
+pytestmark = pytest.mark.gpu
+TOL8 = 5e-2
+
+
+@pytest.mark.parametrize("M,K,dtype", [(1, 128, torch.bfloat16), (37, 512, torch.bfloat16), (64, 7168, torch.bfloat16),
+                                       (9, 256, torch.float32), (5, 384, torch.float16)])
+def test_quantize_rows_bit_exact(cuda_device, M, K, dtype):
+    gen = torch.Generator().manual_seed(M * K)
+    x = (torch.randn(M, K, generator=gen) * torch.logspace(-3, 2, M)[:, None]).to(dtype)
+    x[0, :128] = 0  # an all-zero block keeps scale 1
+    q, s = quantize_rows_fp8(x.to(cuda_device))
+    rq, rs = quantize_rows_128(x.float().numpy())
+    np.testing.assert_array_equal(s.cpu().numpy(), rs)
+    np.testing.assert_array_equal(q.float().cpu().numpy(), rq)
+
+
+@pytest.mark.parametrize("E,R,C", [(1, 128, 128), (3, 256, 384), (2, 512, 1024)])
+def test_quantize_weights_bit_exact(cuda_device, E, R, C):
+    gen = torch.Generator().manual_seed(E + R + C)
+    w = (torch.randn(E, R, C, generator=gen) / C ** 0.5).to(torch.bfloat16)
+    q, s = quantize_weights_fp8(w.to(cuda_device))
+    rq, rs = quantize_blocks_128(w.float().numpy())
+    np.testing.assert_array_equal(s.cpu().numpy(), rs)
+    np.testing.assert_array_equal(q.float().cpu().numpy(), rq)
+
+
+def _fp8_weights(E, K, N, dev, seed):
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    w1 = (torch.randn(E, 2 * N, K, generator=gen, device=dev) / K ** 0.5).to(torch.bfloat16)
+    w2 = (torch.randn(E, K, N, generator=gen, device=dev) / N ** 0.5).to(torch.bfloat16)
+    w1q, w1s = quantize_weights_fp8(w1)
+    w2q, w2s = quantize_weights_fp8(w2)
+    return w1q, w1s, w2q, w2s
+
+
+@pytest.mark.parametrize("M,E,k,K,N", [(1, 8, 2, 256, 128), (37, 16, 4, 512, 256), (300, 8, 2, 384, 128),
+                                       (129, 4, 1, 256, 384)])
+def test_fused_fp8_oracle(cuda_device, M, E, k, K, N):
+    dev = cuda_device
+    w1q, w1s, w2q, w2s = _fp8_weights(E, K, N, dev, seed=M + E)
+    gen = torch.Generator(device=dev).manual_seed(M)
+    x = torch.randn(M, K, generator=gen, device=dev).to(torch.bfloat16)
+    w, ids = softmax_topk(torch.randn(M, E, generator=gen, device=dev), k)
+    out = fused_moe_fp8(x, w1q, w1s, w2q, w2s, w, ids)
+    args = (x.float().cpu().numpy(), w1q.float().cpu().numpy(), w1s.cpu().numpy(), w2q.float().cpu().numpy(),
+            w2s.cpu().numpy(), w.cpu().numpy(), ids.cpu().numpy())
+    got = out.float().cpu().numpy()
+    np.testing.assert_allclose(got, moe_experts_fp8_ref(*args, operand_rounding="bf16"), atol=TOL8, rtol=TOL8)
+    exact = moe_experts_fp8_ref(*args)
+    rel = np.linalg.norm(got - exact) / np.linalg.norm(exact)
+    assert rel < TOL8, rel  # exact-operand oracle: aggregate relative error within the FP8 tolerance
+    check_device_status(dev)
+
+
+def test_functional_flag_routes_to_fp8(cuda_device):
+    dev = cuda_device
+    w1q, w1s, w2q, w2s = _fp8_weights(8, 256, 128, dev, seed=3)
+    x = torch.randn(20, 256, device=dev).to(torch.bfloat16)
+    w, ids = softmax_topk(torch.randn(20, 8, device=dev), 2)
+    a = fused_moe(x, w1q, w2q, w, ids, use_fp8_w8a8=True, w1_scale=w1s, w2_scale=w2s)
+    b = fused_moe_fp8(x, w1q, w1s, w2q, w2s, w, ids)
+    assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("M", [1, 8, 32, 128])
+def test_dsv3_fp8_config(cuda_device, M, dsv3_fp8_weights):
+    """DeepSeek-V3 FP8 layer: grouped_topk (sigmoid + bias, top-2 group sum, x2.5) feeding the FP8 expert path."""
+    dev = cuda_device
+    w1q, w1s, w2q, w2s = dsv3_fp8_weights
+    gen = torch.Generator(device=dev).manual_seed(200 + M)
+    x = torch.randn(M, 7168, generator=gen, device=dev).to(torch.bfloat16)
+    g = torch.randn(M, 256, generator=gen, device=dev)
+    bias = torch.randn(256, generator=gen, device=dev) * 0.01
+    w, ids = grouped_topk(x, g, 8, True, 8, 4, "sigmoid", 2.5, e_score_correction_bias=bias)
+    out = fused_moe_fp8(x, w1q, w1s, w2q, w2s, w, ids)
+    rows = torch.randperm(M, generator=gen, device=dev)[:8].cpu()
+    ref = experts_rows_fp8(x, w1q, w1s, w2q, w2s, w, ids, rows)
+    torch.testing.assert_close(out[rows.to(dev)].float(), ref, atol=TOL8, rtol=TOL8)
+    check_device_status(dev)
+
+
+@pytest.fixture(scope="module")
+def dsv3_fp8_weights(cuda_device):
+    w = _fp8_weights(256, 7168, 2048, cuda_device, seed=43)
+    torch.cuda.empty_cache()
+    yield w
+    del w
+    torch.cuda.empty_cache()
