@@ -57,6 +57,10 @@ def parse():
     ap.add_argument("--skewed", action="store_true", help="bias +2.0 on 16 hot experts")
     ap.add_argument("--fp8", action="store_true",
                     help="FP8 w8a8 configuration: e4m3 weights with 128x128 block scales, tokens per 128")
+    ap.add_argument("--ep-chunks", type=int, default=None,
+                    help="expert-parallel overlap: token chunks per step (default: the layer's choice)")
+    ap.add_argument("--ep-reserve-sms", type=int, default=None,
+                    help="expert-parallel overlap: SMs the expert GEMMs leave to the all-to-alls")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=5)
     return ap.parse_args()
@@ -304,7 +308,9 @@ def run_native(args):
         w1, w2 = make_weights(E_local, rank * E_local, dev)
         layer = ExpertParallelMoE(w1, w2, num_experts=E, topk=k, num_expert_group=DSV3["n_group"],
                                   topk_group=DSV3["topk_group"], scoring_func="sigmoid",
-                                  routed_scaling_factor=DSV3["scale"], e_score_correction_bias=bias)
+                                  routed_scaling_factor=DSV3["scale"], e_score_correction_bias=bias,
+                                  **{k_: v_ for k_, v_ in (("chunks", args.ep_chunks),
+                                                           ("reserve_sms", args.ep_reserve_sms)) if v_ is not None})
 
         def step(events=None):
             return layer.forward(x, g, events=events)
@@ -328,15 +334,16 @@ def run_native(args):
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record()
     for i in range(args.steps):
-        step(stage_events[i])
+        step(stage_events[i] if world == 1 else None)
     t1.record()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     clocks = sampler.stop()
     ms_local = t0.elapsed_time(t1)
-    gemm1_ms = [ev[1].elapsed_time(ev[2]) for ev in stage_events]
-    gemm2_ms = [ev[2].elapsed_time(ev[3]) for ev in stage_events]
+    if world == 1:
+        gemm1_ms = [ev[1].elapsed_time(ev[2]) for ev in stage_events]
+        gemm2_ms = [ev[2].elapsed_time(ev[3]) for ev in stage_events]
     ms = ms_local
     if world > 1:
         t = torch.tensor([ms_local], device=dev)
@@ -355,6 +362,11 @@ def run_native(args):
         pairs_local, distinct = layer.local_work()
         layer.profile = False
         phases = layer.phase_breakdown()
+        gb = layer.gemm_breakdown()
+        if gb is not None:  # overlapped layer: GEMM times summed over the chunks of a step
+            gemm1_ms, gemm2_ms, pairs_local = [gb[0]], [gb[1]], int(gb[2])
+        else:
+            gemm1_ms, gemm2_ms = [float("nan")], [float("nan")]
 
     peaks = measured_peaks()
     layer_flops = 6.0 * M_total * k * K * N
@@ -363,13 +375,24 @@ def run_native(args):
     if args.fp8:
         layer_bytes += distinct * 3 * (K // 128) * (N // 128) * 4  # fp32 block scales
     if args.fp8:
-        # decode-sized FP8 layers are bound by the e4m3 weight stream: roofline on HBM
+        # whole FP8 expert path (quantise, align, gather, GEMM1, GEMM2, combine) against the
+        # tighter of its two bounds: e4m3 tensor rate (twice the measured bf16 rate, the B200
+        # dense ratio) for prefill-sized batches, the weight stream over HBM for decode sizes
         path_ms = statistics.mean([ev[1].elapsed_time(ev[4]) for ev in stage_events])
-        achieved = layer_bytes / (path_ms / 1e3) / 1e9
-        roof = {"kernel": "FP8 expert path (quantise, align, gather, GEMM1, GEMM2, combine)", "bound": "hbm",
-                "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
-                "peak_source": f"{peaks['source']} hbm_gbs", "traffic": None,
-                "bytes_per_launch": layer_bytes, "ms_per_launch": path_ms}
+        path_flops = 6.0 * pairs_local * K * N
+        peak_f8 = 2.0 * peaks["bf16_tflops_sustained"]
+        if path_flops / (peak_f8 * 1e12) >= layer_bytes / (peaks["hbm_gbs"] * 1e9):
+            achieved = path_flops / (path_ms / 1e3) / 1e12
+            roof = {"kernel": "FP8 expert path (quantise, align, gather, GEMM1, GEMM2, combine)", "bound": "tensor",
+                    "achieved": achieved, "peak": peak_f8, "unit": "TFLOP/s", "frac": achieved / peak_f8,
+                    "peak_source": f"2 x {peaks['source']} bf16_tflops_sustained (e4m3 dense rate)",
+                    "traffic": None, "flops_per_launch": path_flops, "ms_per_launch": path_ms}
+        else:
+            achieved = layer_bytes / (path_ms / 1e3) / 1e9
+            roof = {"kernel": "FP8 expert path (quantise, align, gather, GEMM1, GEMM2, combine)", "bound": "hbm",
+                    "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                    "frac": achieved / peaks["hbm_gbs"], "peak_source": f"{peaks['source']} hbm_gbs",
+                    "traffic": None, "bytes_per_launch": layer_bytes, "ms_per_launch": path_ms}
     else:
         g1 = statistics.mean(gemm1_ms)
         g1_flops = 4.0 * pairs_local * K * N
@@ -389,7 +412,7 @@ def run_native(args):
     result = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "fp8-e4m3 (bf16 MMA)" if args.fp8 else "bf16", "data": "synthetic",
+        "vs_baseline": None, "dtype": "fp8-e4m3" if args.fp8 else "bf16", "data": "synthetic",
         "config": {"workload": f"DeepSeek-V3 MoE layer{' FP8 w8a8' if args.fp8 else ''}, {M_total} tokens"
                    + (" (skewed routing)" if args.skewed else "") + ("" if E == 256 else f" (reduced to {E} experts)"),
                    "tokens": M_total, "experts": E, "top_k": k, "hidden": K, "intermediate": N,
@@ -405,41 +428,68 @@ def run_native(args):
         "gpu_launches": launches_per_step * args.steps,
     }
     if world > 1:
+        result["config"]["ep_overlap"] = {"chunks": layer.chunks, "reserve_sms": layer.reserve_sms}
         result["ep_phases_ms_rank0"] = phases
         result["ep_local_pairs_rank0"] = pairs_local
 
     # ---------------- end to end through the public API, host buffers
-    e2e = None
-    if world == 1:
-        xh = x.cpu().pin_memory()
-        gh = g.cpu().pin_memory()
-        oh = torch.empty(M, K, dtype=torch.bfloat16).pin_memory()
-        xd = torch.empty_like(x)
-        gd = torch.empty_like(g)
-        torch.cuda.synchronize()
-        a = torch.cuda.Event(enable_timing=True)
-        b = torch.cuda.Event(enable_timing=True)
-        n = max(1, args.e2e_steps)
-        a.record()
-        for _ in range(n):
-            xd.copy_(xh, non_blocking=True)
-            gd.copy_(gh, non_blocking=True)
-            if args.fp8:
-                w_, ids_ = pkg.grouped_topk(xd, gd, k, True, DSV3["n_group"], DSV3["topk_group"], "sigmoid",
-                                            DSV3["scale"], e_score_correction_bias=bias)
-                o = pkg.fused_moe(xd, w1q, w2q, w_, ids_, use_fp8_w8a8=True, w1_scale=w1s, w2_scale=w2s)
-            else:
-                o = pkg.moe_layer(xd, gd, w1, w2, topk=k, renormalize=True, num_expert_group=DSV3["n_group"],
-                                  topk_group=DSV3["topk_group"], scoring_func="sigmoid",
-                                  routed_scaling_factor=DSV3["scale"], e_score_correction_bias=bias)
-            oh.copy_(o, non_blocking=True)
-        b.record()
-        torch.cuda.synchronize()
-        e2e_ms = a.elapsed_time(b) / n
-        e2e = {"value": M / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": xh.numel() * 2 + gh.numel() * 4,
-               "d2h_bytes_per_step": oh.numel() * 2, "ms_per_step": e2e_ms}
+    # end to end: batches in pinned host memory through the public API, every step's H2D of
+    # its hidden states + router logits and D2H of its output inside the timed region;
+    # HostPipeline overlaps step i+1's H2D and step i-1's D2H with step i's layer
+    from kernelswift_competition_submission_b200.pipeline import HostPipeline
+
+    if world > 1:
+        def layer_fn(xd, gd):
+            return layer.forward(xd, gd)
+    elif args.fp8:
+        def layer_fn(xd, gd):
+            w_, ids_ = pkg.grouped_topk(xd, gd, k, True, DSV3["n_group"], DSV3["topk_group"], "sigmoid",
+                                        DSV3["scale"], e_score_correction_bias=bias)
+            return pkg.fused_moe(xd, w1q, w2q, w_, ids_, use_fp8_w8a8=True, w1_scale=w1s, w2_scale=w2s)
     else:
-        e2e = layer.e2e(x, g, steps=max(1, args.e2e_steps))
+        def layer_fn(xd, gd):
+            return pkg.moe_layer(xd, gd, w1, w2, topk=k, renormalize=True, num_expert_group=DSV3["n_group"],
+                                 topk_group=DSV3["topk_group"], scoring_func="sigmoid",
+                                 routed_scaling_factor=DSV3["scale"], e_score_correction_bias=bias)
+    xh = x.cpu().pin_memory()
+    gh = g.cpu().pin_memory()
+    ohs = [torch.empty(M, K, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    pipe = HostPipeline(layer_fn, dev)
+    pipe.run([xh, xh], [gh, gh], ohs)  # warm-up: device slots, allocator
+    n = max(2, args.e2e_steps)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    pipe.run([xh] * n, [gh] * n, [ohs[i % 2] for i in range(n)])
+    b.record()
+    torch.cuda.synchronize()
+    e2e_ms = a.elapsed_time(b) / n
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    # the host link alone: one H2D of the step's inputs and one D2H of its output, each timed apart
+    xd_, gd_ = torch.empty_like(x), torch.empty_like(g)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    ev[0].record()
+    xd_.copy_(xh, non_blocking=True)
+    gd_.copy_(gh, non_blocking=True)
+    ev[1].record()
+    ev[2].record()
+    ohs[0].copy_(xd_, non_blocking=True)
+    ev[3].record()
+    torch.cuda.synchronize()
+    h2d_ms, d2h_ms = ev[0].elapsed_time(ev[1]), ev[2].elapsed_time(ev[3])
+    del xd_, gd_
+    e2e = {"value": M_total / (e2e_ms / 1e3), "unit": UNIT,
+           "h2d_bytes_per_step": xh.numel() * xh.element_size() + gh.numel() * gh.element_size(),
+           "d2h_bytes_per_step": ohs[0].numel() * ohs[0].element_size(), "ms_per_step": e2e_ms, "steps": n,
+           "h2d_ms_alone": h2d_ms, "d2h_ms_alone": d2h_ms,
+           "path": "HostPipeline over pinned host batches (H2D/D2H overlapped with the layer)"
+                   + ("; per-rank host bytes, value is the whole job" if world > 1 else "")}
     result["e2e"] = e2e
     pkg.check_device_status(dev)
 

@@ -179,8 +179,10 @@ MOE_API int moe_fused_experts(int dtype, const void* hidden_states, const void* 
  *   moe_expert_gemm1         tcgen05 gate/up GEMM, SiLU*mul epilogue -> act (workspace)
  *   moe_expert_gemm2         tcgen05 down GEMM, per-pair rows -> slot buffer (workspace)
  *   moe_expert_combine       top-k weighted sum of the slot rows -> out
- * moe_fused_experts(...) is exactly these four calls. They exist so a caller
- * can interleave its own work (events, communication) between stages.
+ * moe_fused_experts(...) is exactly these four calls (with max_ctas = 0). They
+ * exist so a caller can interleave its own work (events, communication)
+ * between stages. max_ctas limits the persistent GEMM grid (0 = one CTA per
+ * SM) so that work on other streams, e.g. collectives, can run beside it.
  */
 MOE_API int moe_expert_align_gather(int dtype, const void* hidden_states, const int32_t* topk_ids,
                                     int64_t num_tokens, int num_experts, int topk, int hidden_size,
@@ -188,10 +190,10 @@ MOE_API int moe_expert_align_gather(int dtype, const void* hidden_states, const 
                                     void* stream);
 MOE_API int moe_expert_gemm1(int dtype, const void* w1, int64_t num_tokens, int num_experts, int topk,
                              int hidden_size, int intermediate_size, void* workspace,
-                             size_t workspace_bytes, int* status, void* stream);
+                             size_t workspace_bytes, int* status, int max_ctas, void* stream);
 MOE_API int moe_expert_gemm2(int dtype, const void* w2, int64_t num_tokens, int num_experts, int topk,
                              int hidden_size, int intermediate_size, void* workspace,
-                             size_t workspace_bytes, int* status, void* stream);
+                             size_t workspace_bytes, int* status, int max_ctas, void* stream);
 MOE_API int moe_expert_combine(int dtype, const float* topk_weights, const int32_t* topk_ids,
                                int64_t num_tokens, int num_experts, int topk, int hidden_size,
                                int intermediate_size, void* out, void* workspace,

@@ -52,8 +52,8 @@ SIGNATURES = {
     "moe_fused_experts": (_i32, [_i32, _c_p, _c_p, _c_p, _c_p, _c_p, _i64, _i32, _i32, _i32, _i32, _c_p, _c_p, _sz,
                                  _c_p, _c_p]),
     "moe_expert_align_gather": (_i32, [_i32, _c_p, _c_p, _i64, _i32, _i32, _i32, _i32, _c_p, _sz, _c_p]),
-    "moe_expert_gemm1": (_i32, [_i32, _c_p, _i64, _i32, _i32, _i32, _i32, _c_p, _sz, _c_p, _c_p]),
-    "moe_expert_gemm2": (_i32, [_i32, _c_p, _i64, _i32, _i32, _i32, _i32, _c_p, _sz, _c_p, _c_p]),
+    "moe_expert_gemm1": (_i32, [_i32, _c_p, _i64, _i32, _i32, _i32, _i32, _c_p, _sz, _c_p, _i32, _c_p]),
+    "moe_expert_gemm2": (_i32, [_i32, _c_p, _i64, _i32, _i32, _i32, _i32, _c_p, _sz, _c_p, _i32, _c_p]),
     "moe_expert_combine": (_i32, [_i32, _c_p, _c_p, _i64, _i32, _i32, _i32, _i32, _c_p, _c_p, _sz, _c_p]),
     "moe_quantize_rows_fp8": (_i32, [_i32, _c_p, _i64, _i32, _c_p, _c_p, _c_p]),
     "moe_quantize_blocks_fp8": (_i32, [_i32, _c_p, _i64, _i32, _i32, _c_p, _c_p, _c_p]),

@@ -147,7 +147,7 @@ extern "C" int moe_expert_align_gather(int dtype, const void* hidden_states, con
 
 extern "C" int moe_expert_gemm1(int dtype, const void* w1, int64_t num_tokens, int num_experts, int topk,
                                 int hidden_size, int intermediate_size, void* workspace, size_t workspace_bytes,
-                                int* status, void* stream) {
+                                int* status, int max_ctas, void* stream) {
   using namespace moe;
   int rc = validate_experts(dtype, num_tokens, num_experts, topk, hidden_size, intermediate_size);
   if (rc != MOE_OK || num_tokens == 0) return rc;
@@ -158,12 +158,12 @@ extern "C" int moe_expert_gemm1(int dtype, const void* w1, int64_t num_tokens, i
                             intermediate_size, &w)) != MOE_OK)
     return rc;
   return cuda_status(launch_gemm1_silu(dtype, w.x_sorted, w.l.cap, w1, num_experts, hidden_size, intermediate_size,
-                                       w.am.block_start, w.act, status, static_cast<cudaStream_t>(stream)));
+                                       w.am.block_start, w.act, status, max_ctas, static_cast<cudaStream_t>(stream)));
 }
 
 extern "C" int moe_expert_gemm2(int dtype, const void* w2, int64_t num_tokens, int num_experts, int topk,
                                 int hidden_size, int intermediate_size, void* workspace, size_t workspace_bytes,
-                                int* status, void* stream) {
+                                int* status, int max_ctas, void* stream) {
   using namespace moe;
   int rc = validate_experts(dtype, num_tokens, num_experts, topk, hidden_size, intermediate_size);
   if (rc != MOE_OK || num_tokens == 0) return rc;
@@ -174,7 +174,7 @@ extern "C" int moe_expert_gemm2(int dtype, const void* w2, int64_t num_tokens, i
                             intermediate_size, &w)) != MOE_OK)
     return rc;
   return cuda_status(launch_gemm2_scatter(dtype, w.act, w.l.cap, w2, num_experts, hidden_size, intermediate_size,
-                                          w.am.block_start, w.sorted, num_tokens * topk, w.y_slots, status,
+                                          w.am.block_start, w.sorted, num_tokens * topk, w.y_slots, status, max_ctas,
                                           static_cast<cudaStream_t>(stream)));
 }
 
@@ -214,10 +214,10 @@ extern "C" int moe_fused_experts(int dtype, const void* hidden_states, const voi
                                  hidden_states, w.x_sorted, (int64_t)hidden_size * 2, st);
   if (err == cudaSuccess)
     err = launch_gemm1_silu(dtype, w.x_sorted, w.l.cap, w1, num_experts, hidden_size, intermediate_size,
-                            w.am.block_start, w.act, status, st);
+                            w.am.block_start, w.act, status, 0, st);
   if (err == cudaSuccess)
     err = launch_gemm2_scatter(dtype, w.act, w.l.cap, w2, num_experts, hidden_size, intermediate_size,
-                               w.am.block_start, w.sorted, P, w.y_slots, status, st);
+                               w.am.block_start, w.sorted, P, w.y_slots, status, 0, st);
   if (err == cudaSuccess)
     err = launch_combine(dtype, w.y_slots, topk_weights, topk_ids, num_tokens, topk, num_experts, hidden_size, out,
                          st);

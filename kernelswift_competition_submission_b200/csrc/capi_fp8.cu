@@ -54,7 +54,6 @@ extern "C" int moe_fused_experts_fp8(const void* hidden_states, const void* w1_q
   if (M < 0 || E <= 0 || topk <= 0 || K <= 0 || N <= 0) return MOE_ERR_INVALID_ARG;
   if (E > 1024 || topk > 64) return MOE_ERR_BAD_SHAPE;
   if (K % 128 != 0 || N % 128 != 0) return MOE_ERR_BAD_SHAPE;
-  if (K > 16384 || N > 16384) return MOE_ERR_BAD_SHAPE;  // a tile stages at most 128 K-block scales
   const int64_t P = M * topk;
   if (P > INT32_MAX / 2) return MOE_ERR_BAD_SHAPE;
   if (M == 0) return MOE_OK;
@@ -84,10 +83,10 @@ extern "C" int moe_fused_experts_fp8(const void* hidden_states, const void* w1_q
                              st);
   if (err == cudaSuccess)
     err = launch_fp8_gemm1(ws + l.xq_s, reinterpret_cast<const float*>(ws + l.xs_s), l.cap, w1_q, w1_scale, E, K, N,
-                           am.block_start, am.counts, ws + l.actq, reinterpret_cast<float*>(ws + l.acts), status, st);
+                           am.block_start, ws + l.actq, reinterpret_cast<float*>(ws + l.acts), status, st);
   if (err == cudaSuccess)
     err = launch_fp8_gemm2(ws + l.actq, reinterpret_cast<const float*>(ws + l.acts), l.cap, w2_q, w2_scale, E, K, N,
-                           am.block_start, am.counts, sorted, ws + l.y, status, st);
+                           am.block_start, sorted, ws + l.y, status, st);
   if (err == cudaSuccess)
     err = launch_combine(MOE_DTYPE_BF16, ws + l.y, topk_weights, topk_ids, M, topk, E, K, out, st);
   return err == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;

@@ -278,14 +278,17 @@ constexpr int kStages = 4;
 template <typename T, int MODE, int BN>
 cudaError_t launch_gemm_t(const CUtensorMap& ma, const CUtensorMap& mb, const int32_t* block_start, int E, int k_red,
                           int n_out, int NB, int64_t rows_cap, void* out, const int32_t* sorted_pairs, int* status,
-                          cudaStream_t st) {
+                          int max_ctas, cudaStream_t st) {
   using L = SmemLayout<BN, kStages>;
   auto kern = moe_gemm_kernel<T, MODE, BN, kStages>;
   const int smem = L::bytes(E);
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (err != cudaSuccess) return err;
   const int64_t tiles_cap = (rows_cap / kBlockM) * NB;
-  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(num_sms(), tiles_cap));
+  // persistent grid: one CTA per SM, or fewer when the caller keeps SMs free for
+  // concurrent work (e.g. collectives overlapping the GEMM)
+  const int ctas = (max_ctas > 0 && max_ctas < num_sms()) ? max_ctas : num_sms();
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(ctas, tiles_cap));
   kern<<<grid, kThreads, smem, st>>>(ma, mb, block_start, E, k_red, n_out, NB, static_cast<T*>(out), sorted_pairs,
                                      status);
   return cudaGetLastError();
@@ -294,7 +297,7 @@ cudaError_t launch_gemm_t(const CUtensorMap& ma, const CUtensorMap& mb, const in
 }  // namespace
 
 cudaError_t launch_gemm1_silu(int dtype, const void* x_sorted, int64_t rows_cap, const void* w1, int E, int K, int N,
-                              const int32_t* block_start, void* act, int* status, cudaStream_t st) {
+                              const int32_t* block_start, void* act, int* status, int max_ctas, cudaStream_t st) {
   const int BN = (N % 128 == 0) ? 256 : 128;
   const int BH = BN / 2;
   CUtensorMap ma, mbm;
@@ -308,20 +311,20 @@ cudaError_t launch_gemm1_silu(int dtype, const void* x_sorted, int64_t rows_cap,
   if (dtype == MOE_DTYPE_BF16) {
     if (BN == 256)
       return launch_gemm_t<__nv_bfloat16, MODE_GEMM1_SILU, 256>(ma, mbm, block_start, E, K, N, NB, rows_cap, act,
-                                                                nullptr, status, st);
+                                                                nullptr, status, max_ctas, st);
     return launch_gemm_t<__nv_bfloat16, MODE_GEMM1_SILU, 128>(ma, mbm, block_start, E, K, N, NB, rows_cap, act,
-                                                              nullptr, status, st);
+                                                              nullptr, status, max_ctas, st);
   }
   if (BN == 256)
     return launch_gemm_t<__half, MODE_GEMM1_SILU, 256>(ma, mbm, block_start, E, K, N, NB, rows_cap, act, nullptr,
-                                                       status, st);
+                                                       status, max_ctas, st);
   return launch_gemm_t<__half, MODE_GEMM1_SILU, 128>(ma, mbm, block_start, E, K, N, NB, rows_cap, act, nullptr,
-                                                     status, st);
+                                                     status, max_ctas, st);
 }
 
 cudaError_t launch_gemm2_scatter(int dtype, const void* act, int64_t rows_cap, const void* w2, int E, int K, int N,
                                  const int32_t* block_start, const int32_t* sorted_pairs, int64_t num_pairs,
-                                 void* y_slots, int* status, cudaStream_t st) {
+                                 void* y_slots, int* status, int max_ctas, cudaStream_t st) {
   (void)num_pairs;
   const int BN = (K >= 256) ? 256 : 128;
   CUtensorMap ma, mbm;
@@ -335,15 +338,15 @@ cudaError_t launch_gemm2_scatter(int dtype, const void* act, int64_t rows_cap, c
   if (dtype == MOE_DTYPE_BF16) {
     if (BN == 256)
       return launch_gemm_t<__nv_bfloat16, MODE_GEMM2, 256>(ma, mbm, block_start, E, N, K, NB, rows_cap, y_slots,
-                                                           sorted_pairs, status, st);
+                                                           sorted_pairs, status, max_ctas, st);
     return launch_gemm_t<__nv_bfloat16, MODE_GEMM2, 128>(ma, mbm, block_start, E, N, K, NB, rows_cap, y_slots,
-                                                         sorted_pairs, status, st);
+                                                         sorted_pairs, status, max_ctas, st);
   }
   if (BN == 256)
     return launch_gemm_t<__half, MODE_GEMM2, 256>(ma, mbm, block_start, E, N, K, NB, rows_cap, y_slots, sorted_pairs,
-                                                  status, st);
+                                                  status, max_ctas, st);
   return launch_gemm_t<__half, MODE_GEMM2, 128>(ma, mbm, block_start, E, N, K, NB, rows_cap, y_slots, sorted_pairs,
-                                                status, st);
+                                                status, max_ctas, st);
 }
 
 }  // namespace moe

@@ -39,11 +39,12 @@ cudaError_t launch_combine(int dtype, const void* y_slots, const float* topk_wei
 // Grouped GEMMs, one CTA per tile (sm_100a tcgen05.mma.cta_group::1, token-major 128 x 256
 // tiles). Rows come in m-blocks of kBlockM grouped by expert (align with block_m = kBlockM;
 // block_start read on the device).
+// max_ctas: persistent grid size limit (0 = one CTA per SM).
 cudaError_t launch_gemm1_silu(int dtype, const void* x_sorted, int64_t rows_cap, const void* w1, int E, int K, int N,
-                              const int32_t* block_start, void* act, int* status, cudaStream_t st);
+                              const int32_t* block_start, void* act, int* status, int max_ctas, cudaStream_t st);
 cudaError_t launch_gemm2_scatter(int dtype, const void* act, int64_t rows_cap, const void* w2, int E, int K, int N,
                                  const int32_t* block_start, const int32_t* sorted_pairs, int64_t num_pairs,
-                                 void* y_slots, int* status, cudaStream_t st);
+                                 void* y_slots, int* status, int max_ctas, cudaStream_t st);
 
 bool make_kmajor_map(CUtensorMap* m, int dtype, const void* base, int rank, const uint64_t* dims,
                      const uint64_t* strides_bytes, uint32_t box_rows);
@@ -51,13 +52,15 @@ bool make_kmajor_map(CUtensorMap* m, int dtype, const void* base, int rank, cons
 bool make_fp8_map(CUtensorMap* m, const void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
                   uint32_t box_rows);
 
-// FP8 path: e4m3 operands dequantised to bf16 in shared memory, tcgen05 bf16 MMA.
+// FP8 path: tcgen05.mma.kind::f8f6f4 per 128-wide K block, fp32 block-scale
+// promotion in the epilogue. GEMM1 writes e4m3 act rows + per-128 scales
+// (SiLU*mul quantised in the epilogue); GEMM2 writes bf16 pair slots.
 cudaError_t launch_fp8_gemm1(const void* xq_sorted, const float* xs_sorted, int64_t rows_cap, const void* w1q,
-                             const float* w1s, int E, int K, int N, const int32_t* block_start,
-                             const int32_t* expert_counts, void* actq, float* acts, int* status, cudaStream_t st);
+                             const float* w1s, int E, int K, int N, const int32_t* block_start, void* actq,
+                             float* acts, int* status, cudaStream_t st);
 cudaError_t launch_fp8_gemm2(const void* actq, const float* acts, int64_t rows_cap, const void* w2q, const float* w2s,
-                             int E, int K, int N, const int32_t* block_start, const int32_t* expert_counts,
-                             const int32_t* sorted_pairs, void* y_slots, int* status, cudaStream_t st);
+                             int E, int K, int N, const int32_t* block_start, const int32_t* sorted_pairs,
+                             void* y_slots, int* status, cudaStream_t st);
 // dst[r] = src[sorted_pairs[r] / topk] (row_bytes each) for the rows the align stage filled.
 cudaError_t launch_gather_rows(const void* src, int64_t row_bytes, const int32_t* sorted_pairs,
                                const int32_t* block_start, int E, int topk, int64_t cap, void* dst, cudaStream_t st);

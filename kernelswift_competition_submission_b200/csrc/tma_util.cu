@@ -45,18 +45,18 @@ bool make_kmajor_map(CUtensorMap* m, int dtype, const void* base, int rank, cons
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// e4m3 (byte) operand map: innermost box of 64 bytes, no swizzle (the converter
-// warps read it with plain shared loads), out-of-bounds bytes read as zero.
+// e4m3 (byte) operand map: innermost box of 128 bytes (one 128-wide K block) with
+// the 128-byte swizzle the tcgen05 descriptors expect; out-of-bounds bytes read as zero.
 bool make_fp8_map(CUtensorMap* m, const void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
                   uint32_t box_rows) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return false;
   cuuint64_t gdim[3], gstr[2];
-  cuuint32_t box[3] = {64, box_rows, 1}, estr[3] = {1, 1, 1};
+  cuuint32_t box[3] = {128, box_rows, 1}, estr[3] = {1, 1, 1};
   for (int i = 0; i < rank; ++i) gdim[i] = dims[i];
   for (int i = 0; i < rank - 1; ++i) gstr[i] = strides_bytes[i];
   return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, rank, const_cast<void*>(base), gdim, gstr, box, estr,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 

@@ -284,12 +284,15 @@ def fused_moe_fp8(hidden_states, w1_q, w1_scale, w2_q, w2_scale, topk_weights, t
     return out
 
 
-def fused_moe_staged(hidden_states, w1, w2, topk_weights, topk_ids, *, out=None, workspace=None, events=None):
+def fused_moe_staged(hidden_states, w1, w2, topk_weights, topk_ids, *, out=None, workspace=None, events=None,
+                     max_ctas=0):
     """``fused_moe`` issued as its four C-ABI stages (same kernels, same order).
 
     ``events``: optional list of 5 ``torch.cuda.Event`` recorded on the current
     stream before align, before GEMM1, before GEMM2, before combine and after
     combine, so a caller can time each stage on the stream it runs on.
+    ``max_ctas`` limits the persistent GEMM grids (0 = one CTA per SM), leaving
+    SMs for work on other streams such as overlapping collectives.
     """
     dev = _require_cuda("fused_moe_staged", hidden_states, w1, w2, topk_weights, topk_ids)
     dt = _DTYPES[hidden_states.dtype]
@@ -314,10 +317,10 @@ def fused_moe_staged(hidden_states, w1, w2, topk_weights, topk_ids, *, out=None,
                "moe_expert_align_gather")
     if ev[1] is not None:
         ev[1].record()
-    _lib.check(lib.moe_expert_gemm1(dt, _ptr(w1), M, E, k, K, N, ws, wsn, status, st), "moe_expert_gemm1")
+    _lib.check(lib.moe_expert_gemm1(dt, _ptr(w1), M, E, k, K, N, ws, wsn, status, max_ctas, st), "moe_expert_gemm1")
     if ev[2] is not None:
         ev[2].record()
-    _lib.check(lib.moe_expert_gemm2(dt, _ptr(w2), M, E, k, K, N, ws, wsn, status, st), "moe_expert_gemm2")
+    _lib.check(lib.moe_expert_gemm2(dt, _ptr(w2), M, E, k, K, N, ws, wsn, status, max_ctas, st), "moe_expert_gemm2")
     if ev[3] is not None:
         ev[3].record()
     _lib.check(lib.moe_expert_combine(dt, _ptr(tw), _ptr(ti), M, E, k, K, N, _ptr(out), ws, wsn, st),

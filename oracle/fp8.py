@@ -75,21 +75,15 @@ def dequant_blocks(q, s):
     return (qb * np.asarray(s)[..., :, None, :, None]).reshape(*lead, R, C)
 
 
-def moe_experts_fp8_ref(x, w1q, w1s, w2q, w2s, topk_weights, topk_ids, operand_rounding=None):
+def moe_experts_fp8_ref(x, w1q, w1s, w2q, w2s, topk_weights, topk_ids):
     """fp32 expert path on dequantised operands; x is quantised per token per 128 here,
-    and the SiLU*mul output is quantised the same way before the down projection.
+    and the SiLU*mul output is quantised the same way before the down projection."""
+    from .fused_moe import silu
 
-    operand_rounding="bf16" rounds every dequantised GEMM operand (q * s) to
-    bfloat16 before the fp32-accumulated products, which is what a kernel that
-    dequantises into a bf16 tensor-core pipeline multiplies; None keeps them exact.
-    """
-    from .fused_moe import silu, to_bf16
-
-    rnd = to_bf16 if operand_rounding == "bf16" else (lambda a: a)
     xq, xs = quantize_rows_128(x)
-    xd = rnd(dequant_rows(xq, xs))
-    w1 = rnd(dequant_blocks(w1q, w1s))
-    w2 = rnd(dequant_blocks(w2q, w2s))
+    xd = dequant_rows(xq, xs)
+    w1 = dequant_blocks(w1q, w1s)
+    w2 = dequant_blocks(w2q, w2s)
     M, K = xd.shape
     N = w1.shape[1] // 2
     ids = np.asarray(topk_ids).astype(np.int64)
@@ -105,7 +99,7 @@ def moe_experts_fp8_ref(x, w1q, w1s, w2q, w2s, topk_weights, topk_ids, operand_r
         gu = xd[tok[rows]] @ w1[e].T
         act = silu(gu[:, :N]) * gu[:, N:]
         aq, as_ = quantize_rows_128(act)
-        y[rows] = rnd(dequant_rows(aq, as_)) @ w2[e].T
+        y[rows] = dequant_rows(aq, as_) @ w2[e].T
     valid = (flat >= 0) & (flat < w1.shape[0])
     y *= (w.reshape(-1) * valid)[:, None]
     return y.reshape(M, k, K).sum(axis=1, dtype=np.float32)

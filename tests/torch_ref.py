@@ -30,17 +30,16 @@ def experts_rows_fp32(x, w1, w2, topk_weights, topk_ids, rows):
 
 
 def _e4m3_rows_128(a):
-    """Per row per 128 e4m3 quantise-dequantise (scale = amax / 448, 1 for zero blocks),
-    the dequantised value rounded to bf16 as the kernel's tensor-core operands are."""
+    """Per row per 128 e4m3 quantise-dequantise (scale = amax / 448, 1 for zero blocks)."""
     M, K = a.shape
     b = a.float().reshape(M, K // 128, 128)
     amax = b.abs().amax(-1, keepdim=True)
     s = torch.where(amax > 0, amax / 448.0, torch.ones_like(amax))
-    return ((b / s).clamp(-448, 448).to(torch.float8_e4m3fn).float() * s).reshape(M, K).bfloat16().float()
+    return ((b / s).clamp(-448, 448).to(torch.float8_e4m3fn).float() * s).reshape(M, K)
 
 
 def experts_rows_fp8(x, w1q, w1s, w2q, w2s, topk_weights, topk_ids, rows):
-    """fp32 restatement of the FP8 expert path (oracle/fp8.py, operand_rounding="bf16") for
+    """fp32 restatement of the FP8 expert path (oracle/fp8.py, exact dequantised operands) for
     sampled token rows, on the GPU."""
     prev = torch.backends.cuda.matmul.allow_tf32
     torch.backends.cuda.matmul.allow_tf32 = False
@@ -56,7 +55,6 @@ def experts_rows_fp8(x, w1q, w1s, w2q, w2s, topk_weights, topk_ids, rows):
             r, j = torch.nonzero(ids == e, as_tuple=True)
             w1 = (w1q[e].float().reshape(twoN // 128, 128, K // 128, 128) * w1s[e][:, None, :, None]).reshape(twoN, K)
             w2 = (w2q[e].float().reshape(K // 128, 128, N // 128, 128) * w2s[e][:, None, :, None]).reshape(K, N)
-            w1, w2 = w1.bfloat16().float(), w2.bfloat16().float()
             gu = xs[r] @ w1.T
             act = _e4m3_rows_128(torch.nn.functional.silu(gu[:, :N]) * gu[:, N:])
             out.index_add_(0, r, (act @ w2.T) * ws[r, j][:, None])
