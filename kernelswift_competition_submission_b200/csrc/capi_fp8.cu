@@ -1,6 +1,7 @@
 // C-ABI entry of the FP8 w8a8 expert path: quantise the token rows (per token
-// per 128) -> align -> gather e4m3 rows and scales -> FP8 GEMM1 (+ SiLU*mul +
-// per-row e4m3 quantisation of act) -> FP8 GEMM2 -> top-k combine.
+// per 128) -> align -> gather e4m3 rows, and their scales into a [K blocks][rows]
+// table -> FP8 GEMM1 (+ SiLU*mul + per-row e4m3 quantisation of act, scales
+// written as a [N blocks][rows] table) -> FP8 GEMM2 -> top-k combine.
 #include "common.cuh"
 #include "moe_internal.h"
 
@@ -79,8 +80,8 @@ extern "C" int moe_fused_experts_fp8(const void* hidden_states, const void* w1_q
   if (err == cudaSuccess)
     err = launch_gather_rows(ws + l.xq, K, sorted, am.block_start, E, topk, l.cap, ws + l.xq_s, st);
   if (err == cudaSuccess)
-    err = launch_gather_rows(ws + l.xs, 4 * (int64_t)(K / 128), sorted, am.block_start, E, topk, l.cap, ws + l.xs_s,
-                             st);
+    err = launch_gather_scales_t(reinterpret_cast<const float*>(ws + l.xs), K / 128, sorted, am.block_start, E, topk,
+                                 l.cap, reinterpret_cast<float*>(ws + l.xs_s), st);
   if (err == cudaSuccess)
     err = launch_fp8_gemm1(ws + l.xq_s, reinterpret_cast<const float*>(ws + l.xs_s), l.cap, w1_q, w1_scale, E, K, N,
                            am.block_start, ws + l.actq, reinterpret_cast<float*>(ws + l.acts), status, st);

@@ -13,23 +13,32 @@
 // partial buffers let the MMAs of block kb + 1 run while block kb is promoted.
 //
 //   warp 0      TMA producer: one 128-wide K block per stage, A = 128 rows x 128 B,
-//               B = 256 rows x 128 B, 128-byte swizzle. GEMM1 stacks the B rows
-//               as [gate 0..63 | up 0..63 | gate 64..127 | up 64..127] of the
-//               tile's 128 intermediate channels, so each epilogue warpgroup owns
+//               B = 256 rows x 128 B, 128-byte swizzle, plus the K block's 128 row
+//               scales (one 512-byte row of a [K blocks][rows] table). GEMM1 stacks
+//               the B rows as [gate 0..63 | up 0..63 | gate 64..127 | up 64..127] of
+//               the tile's 128 intermediate channels, so each epilogue warpgroup owns
 //               the gate and up columns of the same 64 channels.
 //   warp 1      MMA issuer: 4 x tcgen05.mma.kind::f8f6f4 (M=128, N=256, K=32) per
 //               stage into partial buffer kb & 1.
 //   warp 2      TMEM allocator (2 partial buffers x 256 fp32 columns); warp 3 idle.
 //   warps 4-11  promotion + tile epilogue; warp w reads TMEM lanes 32 * (w % 4)
 //               (one row per thread) and columns 128 * h, h = (w - 4) / 4: 128 fp32
-//               totals per thread. Warpgroup 0 (warps 0-3) gives registers back
-//               (setmaxnreg 40) so the two epilogue warpgroups can hold 232 each.
+//               totals per thread, updated with packed fp32 FMAs. A stage is free
+//               once its MMAs completed and every epilogue warp read its row scales.
+//               Warpgroup 0 (warps 0-3) gives registers back (setmaxnreg 40) so the
+//               two epilogue warpgroups can hold 232 each.
 //               GEMM1: act = SiLU(gate) * up in fp32, quantised per row per 128
 //               channels (scale = amax / 448, the two warpgroups' halves of the
-//               amax meet in shared memory) -> e4m3 act rows + scales, the A
-//               operand of GEMM2. GEMM2: bf16 rows of the pair slots.
-//               Stores are staged per warp in shared memory and leave as 64-byte
-//               row segments.
+//               amax meet in shared memory) -> e4m3 act rows + scales ([channel
+//               blocks][rows] table), the A operand of GEMM2. GEMM2: bf16 rows of
+//               the pair slots. Stores are staged per warp in shared memory and
+//               leave as 64-byte row segments.
+//
+// Where the time goes (measured on B200, DeepSeek-V3 shapes): with the promotion
+// removed the two GEMMs run near the e4m3 tensor rate; the promotion's fp32 work
+// (128 x 256 FMAs per 128-wide K block, on the CUDA cores, between a partial's
+// tcgen05.ld and its buffer's release) is as long as the MMAs it has to overlap,
+// and with two buffers the MMA waits for it part of the time.
 // Rows come from the align stage (pairs grouped by expert, 128-row m-blocks).
 // All mbarrier waits are bounded (common.cuh); the one named barrier of the
 // epilogue is an AND-reduction, so a warp that gave up makes all of them stop.
@@ -58,7 +67,8 @@ template <int STAGES>
 struct F8Smem {
   static constexpr int kEpiOffset = STAGES * kF8Stage;
   static constexpr int kAmaxOffset = kEpiOffset + kF8EpiWarps * kF8EpiWarpBytes;  // [2 tiles][2 halves][128] fp32
-  static constexpr int kBarOffset = kAmaxOffset + 2 * 2 * 128 * 4;
+  static constexpr int kAScaleOffset = kAmaxOffset + 2 * 2 * 128 * 4;             // [STAGES][128] fp32 row scales
+  static constexpr int kBarOffset = kAScaleOffset + STAGES * 128 * 4;
   static constexpr int kNumBars = 2 * STAGES + 5;
   static constexpr int kMiscOffset = kBarOffset + kNumBars * 8;
   static constexpr int kTableOffset = kMiscOffset + 16;
@@ -135,11 +145,12 @@ template <int R> __device__ __forceinline__ void setmaxnreg_inc() {
 template <int MODE, int STAGES>
 __global__ void __launch_bounds__(kF8Threads, 1)
 moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                    const float* __restrict__ a_scale, int a_scale_cols, const float* __restrict__ b_scale,
+                    const __grid_constant__ CUtensorMap map_sa, const float* __restrict__ b_scale,
                     const int32_t* __restrict__ block_start, int E, int k_red, int n_out, int NB,
-                    void* __restrict__ out, float* __restrict__ out_scale, const int32_t* __restrict__ sorted_pairs,
-                    int* status) {
+                    void* __restrict__ out, float* __restrict__ out_scale, int64_t out_scale_stride,
+                    const int32_t* __restrict__ sorted_pairs, int* status) {
   using L = F8Smem<STAGES>;
+  constexpr int kBatch = 1;  // K blocks whose row scales the epilogue reads at once (measured: 1 is fastest)
   constexpr uint32_t kTmemCols = 2 * kF8BN;
   constexpr uint32_t kIdesc = idesc_e4m3(kBlockM, kF8BN);
 
@@ -159,13 +170,14 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
 
   for (int i = threadIdx.x; i <= E; i += kF8Threads) s_bs[i] = __ldg(block_start + i);
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    // a stage is free once its MMAs finished (commit) and every epilogue warp read its row scales
+    for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1 + kF8EpiWarps); }
     for (int b = 0; b < 2; ++b) { mbar_init(&pfull[b], 1); mbar_init(&pempty[b], kF8EpiWarps); }
     mbar_init(mma_done, 1);
     *s_abort = 0;
     fence_mbar_init();
   }
-  if (warp == 0 && lane == 0) { tma_prefetch_desc(&map_a); tma_prefetch_desc(&map_b); }
+  if (warp == 0 && lane == 0) { tma_prefetch_desc(&map_a); tma_prefetch_desc(&map_b); tma_prefetch_desc(&map_sa); }
   if (warp == 2) { tmem_alloc(s_tmem, kTmemCols); tmem_relinquish(); }
   tc_fence_before();
   __syncthreads();
@@ -191,8 +203,10 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
           if (!mbar_wait(&empty[stage], phase ^ 1, status, s_abort)) { ok = false; break; }
           uint8_t* a_dst = smem + stage * kF8Stage;
           uint8_t* b_dst = a_dst + kF8ATile;
-          mbar_arrive_expect_tx(&full[stage], kF8Stage);
+          mbar_arrive_expect_tx(&full[stage], kF8Stage + kBlockM * 4);
           tma_load_2d(&map_a, &full[stage], a_dst, kb * kF8BK, mb * kBlockM);
+          // the 128 row scales of this K block: one 512-byte row of the [K blocks][rows] table
+          tma_load_2d(&map_sa, &full[stage], smem + L::kAScaleOffset + stage * kBlockM * 4, mb * kBlockM, kb);
           if constexpr (MODE == F8_GEMM1) {
 #pragma unroll
             for (int q = 0; q < 4; ++q)  // gate lo, up lo, gate hi, up hi: 64 rows x 128 B each
@@ -250,15 +264,16 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
     float* s_amax = reinterpret_cast<float*>(smem + L::kAmaxOffset);
     const int kb128 = (k_red + 127) / 128;
     const int rd_r = lane >> 2, rd_c = lane & 3;  // staged-read mapping: 8 rows x 4 chunks per instruction
-    int pb = 0, tpar = 0;
-    uint32_t pphase = 0;
+    int pb = 0, tpar = 0, stage = 0;
+    uint32_t pphase = 0, sphase = 0;
+    const float* s_sa = reinterpret_cast<const float*>(smem + L::kAScaleOffset);
     bool ok = true;
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, tpar ^= 1) {
       int e, nb, mb;
       decode_tile_f8(s_bs, E, NB, tile, e, nb, mb);
       const int64_t grow = (int64_t)mb * kBlockM + row;
-      const float* sa_row = a_scale + grow * a_scale_cols;
-      // weight-scale rows for this thread's column halves (lo: columns 0..63, hi: 64..127)
+      // weight scales of the tile's K blocks: lane i holds blocks i and i + 32 (a shuffle
+      // broadcasts block kb); blocks from 64 on are read per block
       const float* sw_lo;
       const float* sw_hi;
       bool cols_live = true;
@@ -272,22 +287,46 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
         sw_lo = b_scale + ((int64_t)e * ((n_out + 127) / 128) + (cols_live ? cblk : 0)) * kb128;
         sw_hi = sw_lo;
       }
+      const float wl_r0 = lane < kb128 ? __ldg(sw_lo + lane) : 0.f;
+      const float wl_r1 = lane + 32 < kb128 ? __ldg(sw_lo + lane + 32) : 0.f;
+      const float wh_r0 = lane < kb128 ? __ldg(sw_hi + lane) : 0.f;
+      const float wh_r1 = lane + 32 < kb128 ? __ldg(sw_hi + lane + 32) : 0.f;
       // totals as fp32 pairs: column 2j in .x, 2j + 1 in .y (packed FMA, two columns per instruction)
       float2 tot[64];
 #pragma unroll
       for (int j = 0; j < 64; ++j) tot[j] = make_float2(0.f, 0.f);
-      // scales of K blocks kb and kb + 1 in flight ahead of their use
-      float sa0 = __ldg(sa_row), wl0 = __ldg(sw_lo), wh0 = __ldg(sw_hi);
-      float sa1 = 0.f, wl1 = 0.f, wh1 = 0.f;
-      if (num_kb > 1) { sa1 = __ldg(sa_row + 1); wl1 = __ldg(sw_lo + 1); wh1 = __ldg(sw_hi + 1); }
+      float sa_q[kBatch];
       for (int kb = 0; kb < num_kb; ++kb) {
-        const float2 f_lo = make_float2(sa0 * wl0, sa0 * wl0), f_hi = make_float2(sa0 * wh0, sa0 * wh0);
-        sa0 = sa1; wl0 = wl1; wh0 = wh1;
-        if (kb + 2 < num_kb) {
-          sa1 = __ldg(sa_row + kb + 2);
-          wl1 = __ldg(sw_lo + kb + 2);
-          wh1 = __ldg(sw_hi + kb + 2);
+        if (kb % kBatch == 0) {
+          // row scales of the next kBatch K blocks (they land with the operands, and the
+          // producer is at least that far ahead), then release this warp's hold on those stages
+          const int first = stage;
+          const int nq = min(kBatch, num_kb - kb);
+#pragma unroll
+          for (int i = 0; i < kBatch; ++i) {
+            if (i < nq) {
+              if (!mbar_wait(&full[stage], sphase, status, s_abort)) ok = false;
+              sa_q[i] = s_sa[stage * kBlockM + row];
+              if (++stage == STAGES) { stage = 0; sphase ^= 1; }
+            }
+          }
+          if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+          __syncwarp();
+          if (lane == 0)
+            for (int i = 0, st = first; i < nq; ++i, st = (st + 1 == STAGES ? 0 : st + 1)) mbar_arrive(&empty[st]);
         }
+        const float sa = sa_q[0];
+#pragma unroll
+        for (int i = 0; i + 1 < kBatch; ++i) sa_q[i] = sa_q[i + 1];
+        float wl, wh;
+        if (kb < 64) {
+          wl = __shfl_sync(0xffffffffu, kb < 32 ? wl_r0 : wl_r1, kb & 31);
+          wh = __shfl_sync(0xffffffffu, kb < 32 ? wh_r0 : wh_r1, kb & 31);
+        } else {
+          wl = __ldg(sw_lo + kb);
+          wh = __ldg(sw_hi + kb);
+        }
+        const float2 f_lo = make_float2(sa * wl, sa * wl), f_hi = make_float2(sa * wh, sa * wh);
         if (!mbar_wait(&pfull[pb], pphase, status, s_abort)) ok = false;
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
         tc_fence_after();
@@ -327,7 +366,7 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
         if (!ok) break;
         amax = fmaxf(amax, s_amax[(tpar * 2 + (h ^ 1)) * 128 + row]);
         const float sc = amax > 0.f ? amax / 448.0f : 1.0f;
-        if (h == 0) out_scale[grow * (n_out / 128) + nb] = sc;
+        if (h == 0) out_scale[(int64_t)nb * out_scale_stride + grow] = sc;  // [channel blocks][rows]
         uint32_t q[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
@@ -413,8 +452,28 @@ gather_rows_kernel(const uint8_t* __restrict__ src, int64_t row_bytes, const int
   }
 }
 
+// Transposed gather of per-row scales: dst[kb * cap + r] = src[(sorted_pairs[r] / topk) * KB + kb]
+// for the rows the align stage filled (0 for padding rows), so the 128 scales of one m-block
+// and K block are 512 contiguous bytes (one TMA box).
+__global__ void __launch_bounds__(256)
+gather_scales_t_kernel(const float* __restrict__ src, int KB, const int32_t* __restrict__ sorted_pairs,
+                       const int32_t* __restrict__ block_start, int E, int topk, int64_t cap, float* __restrict__ dst) {
+  const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= cap || r >= (int64_t)__ldg(block_start + E) * kBlockM) return;
+  const int pair = __ldg(sorted_pairs + r);
+  const float* s = pair >= 0 ? src + (int64_t)(pair / topk) * KB : nullptr;
+  for (int kb = 0; kb < KB; ++kb) dst[(int64_t)kb * cap + r] = s ? __ldg(s + kb) : 0.f;
+}
+
+// [K blocks][rows_cap] fp32 scale table; box = 128 rows of one K block.
+bool make_scale_map(CUtensorMap* m, const float* base, int64_t rows_cap, int kblocks) {
+  const uint64_t dims[2] = {(uint64_t)rows_cap, (uint64_t)kblocks};
+  const uint64_t str[1] = {(uint64_t)rows_cap * 4};
+  return make_f32_rows_map(m, base, dims, str, kBlockM);
+}
+
 template <int MODE, int STAGES>
-cudaError_t launch_f8_stages(const CUtensorMap& ma, const CUtensorMap& mb, const float* a_scale, int a_scale_cols,
+cudaError_t launch_f8_stages(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& msa,
                              const float* b_scale, const int32_t* block_start, int E, int k_red, int n_out, int NB,
                              int64_t rows_cap, void* out, float* out_scale, const int32_t* sorted_pairs, int* status,
                              cudaStream_t st) {
@@ -430,23 +489,22 @@ cudaError_t launch_f8_stages(const CUtensorMap& ma, const CUtensorMap& mb, const
   if (err != cudaSuccess) return err;
   const int64_t tiles_cap = (rows_cap / kBlockM) * NB;
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(num_sms(), tiles_cap));
-  kern<<<grid, kF8Threads, smem, st>>>(ma, mb, a_scale, a_scale_cols, b_scale, block_start, E, k_red, n_out, NB, out,
-                                       out_scale, sorted_pairs, status);
+  kern<<<grid, kF8Threads, smem, st>>>(ma, mb, msa, b_scale, block_start, E, k_red, n_out, NB, out, out_scale,
+                                       rows_cap, sorted_pairs, status);
   return cudaGetLastError();
 }
 
 template <int MODE>
-cudaError_t launch_f8(const CUtensorMap& ma, const CUtensorMap& mb, const float* a_scale, int a_scale_cols,
-                      const float* b_scale, const int32_t* block_start, int E, int k_red, int n_out, int NB,
-                      int64_t rows_cap, void* out, float* out_scale, const int32_t* sorted_pairs, int* status,
-                      cudaStream_t st) {
+cudaError_t launch_f8(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& msa, const float* b_scale,
+                      const int32_t* block_start, int E, int k_red, int n_out, int NB, int64_t rows_cap, void* out,
+                      float* out_scale, const int32_t* sorted_pairs, int* status, cudaStream_t st) {
   constexpr int kMaxSmem = 227 * 1024;
   if (F8Smem<4>::bytes(E) <= kMaxSmem)
-    return launch_f8_stages<MODE, 4>(ma, mb, a_scale, a_scale_cols, b_scale, block_start, E, k_red, n_out, NB,
-                                     rows_cap, out, out_scale, sorted_pairs, status, st);
+    return launch_f8_stages<MODE, 4>(ma, mb, msa, b_scale, block_start, E, k_red, n_out, NB, rows_cap, out,
+                                     out_scale, sorted_pairs, status, st);
   if (F8Smem<3>::bytes(E) <= kMaxSmem)
-    return launch_f8_stages<MODE, 3>(ma, mb, a_scale, a_scale_cols, b_scale, block_start, E, k_red, n_out, NB,
-                                     rows_cap, out, out_scale, sorted_pairs, status, st);
+    return launch_f8_stages<MODE, 3>(ma, mb, msa, b_scale, block_start, E, k_red, n_out, NB, rows_cap, out,
+                                     out_scale, sorted_pairs, status, st);
   return cudaErrorInvalidValue;
 }
 
@@ -461,32 +519,42 @@ cudaError_t launch_gather_rows(const void* src, int64_t row_bytes, const int32_t
   return cudaGetLastError();
 }
 
-cudaError_t launch_fp8_gemm1(const void* xq_sorted, const float* xs_sorted, int64_t rows_cap, const void* w1q,
+cudaError_t launch_gather_scales_t(const float* src, int KB, const int32_t* sorted_pairs, const int32_t* block_start,
+                                   int E, int topk, int64_t cap, float* dst, cudaStream_t st) {
+  if (cap == 0) return cudaSuccess;
+  gather_scales_t_kernel<<<(unsigned)ceil_div(cap, 256), 256, 0, st>>>(src, KB, sorted_pairs, block_start, E, topk,
+                                                                       cap, dst);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_fp8_gemm1(const void* xq_sorted, const float* xs_sorted_t, int64_t rows_cap, const void* w1q,
                              const float* w1s, int E, int K, int N, const int32_t* block_start, void* actq,
-                             float* acts, int* status, cudaStream_t st) {
-  CUtensorMap ma, mbm;
+                             float* acts_t, int* status, cudaStream_t st) {
+  CUtensorMap ma, mbm, msa;
   const uint64_t a_dims[2] = {(uint64_t)K, (uint64_t)rows_cap};
   const uint64_t a_str[1] = {(uint64_t)K};
   const uint64_t b_dims[3] = {(uint64_t)K, (uint64_t)N, (uint64_t)2 * E};
   const uint64_t b_str[2] = {(uint64_t)K, (uint64_t)N * K};
   if (!make_fp8_map(&ma, xq_sorted, 2, a_dims, a_str, kBlockM)) return cudaErrorInvalidValue;
   if (!make_fp8_map(&mbm, w1q, 3, b_dims, b_str, 64)) return cudaErrorInvalidValue;
-  return launch_f8<F8_GEMM1>(ma, mbm, xs_sorted, K / 128, w1s, block_start, E, K, N, N / 128, rows_cap, actq, acts,
-                             nullptr, status, st);
+  if (!make_scale_map(&msa, xs_sorted_t, rows_cap, K / 128)) return cudaErrorInvalidValue;
+  return launch_f8<F8_GEMM1>(ma, mbm, msa, w1s, block_start, E, K, N, N / 128, rows_cap, actq, acts_t, nullptr,
+                             status, st);
 }
 
-cudaError_t launch_fp8_gemm2(const void* actq, const float* acts, int64_t rows_cap, const void* w2q, const float* w2s,
-                             int E, int K, int N, const int32_t* block_start, const int32_t* sorted_pairs,
-                             void* y_slots, int* status, cudaStream_t st) {
-  CUtensorMap ma, mbm;
+cudaError_t launch_fp8_gemm2(const void* actq, const float* acts_t, int64_t rows_cap, const void* w2q,
+                             const float* w2s, int E, int K, int N, const int32_t* block_start,
+                             const int32_t* sorted_pairs, void* y_slots, int* status, cudaStream_t st) {
+  CUtensorMap ma, mbm, msa;
   const uint64_t a_dims[2] = {(uint64_t)N, (uint64_t)rows_cap};
   const uint64_t a_str[1] = {(uint64_t)N};
   const uint64_t b_dims[3] = {(uint64_t)N, (uint64_t)K, (uint64_t)E};
   const uint64_t b_str[2] = {(uint64_t)N, (uint64_t)K * N};
   if (!make_fp8_map(&ma, actq, 2, a_dims, a_str, kBlockM)) return cudaErrorInvalidValue;
   if (!make_fp8_map(&mbm, w2q, 3, b_dims, b_str, kF8BN)) return cudaErrorInvalidValue;
-  return launch_f8<F8_GEMM2>(ma, mbm, acts, N / 128, w2s, block_start, E, N, K, (int)ceil_div(K, kF8BN), rows_cap,
-                             y_slots, nullptr, sorted_pairs, status, st);
+  if (!make_scale_map(&msa, acts_t, rows_cap, N / 128)) return cudaErrorInvalidValue;
+  return launch_f8<F8_GEMM2>(ma, mbm, msa, w2s, block_start, E, N, K, (int)ceil_div(K, kF8BN), rows_cap, y_slots,
+                             nullptr, sorted_pairs, status, st);
 }
 
 }  // namespace moe

@@ -53,14 +53,20 @@ bool make_fp8_map(CUtensorMap* m, const void* base, int rank, const uint64_t* di
                   uint32_t box_rows);
 
 // FP8 path: tcgen05.mma.kind::f8f6f4 per 128-wide K block, fp32 block-scale
-// promotion in the epilogue. GEMM1 writes e4m3 act rows + per-128 scales
+// promotion in the epilogue. Row scales are [K blocks][rows_cap] tables (the
+// transpose of the per-row layout). GEMM1 writes e4m3 act rows + their scales
 // (SiLU*mul quantised in the epilogue); GEMM2 writes bf16 pair slots.
-cudaError_t launch_fp8_gemm1(const void* xq_sorted, const float* xs_sorted, int64_t rows_cap, const void* w1q,
+bool make_f32_rows_map(CUtensorMap* m, const float* base, const uint64_t* dims, const uint64_t* strides_bytes,
+                       uint32_t box_rows);
+cudaError_t launch_fp8_gemm1(const void* xq_sorted, const float* xs_sorted_t, int64_t rows_cap, const void* w1q,
                              const float* w1s, int E, int K, int N, const int32_t* block_start, void* actq,
-                             float* acts, int* status, cudaStream_t st);
-cudaError_t launch_fp8_gemm2(const void* actq, const float* acts, int64_t rows_cap, const void* w2q, const float* w2s,
-                             int E, int K, int N, const int32_t* block_start, const int32_t* sorted_pairs,
-                             void* y_slots, int* status, cudaStream_t st);
+                             float* acts_t, int* status, cudaStream_t st);
+cudaError_t launch_fp8_gemm2(const void* actq, const float* acts_t, int64_t rows_cap, const void* w2q,
+                             const float* w2s, int E, int K, int N, const int32_t* block_start,
+                             const int32_t* sorted_pairs, void* y_slots, int* status, cudaStream_t st);
+// dst[kb * cap + r] = src[(sorted_pairs[r] / topk) * KB + kb] for the rows the align stage filled.
+cudaError_t launch_gather_scales_t(const float* src, int KB, const int32_t* sorted_pairs, const int32_t* block_start,
+                                   int E, int topk, int64_t cap, float* dst, cudaStream_t st);
 // dst[r] = src[sorted_pairs[r] / topk] (row_bytes each) for the rows the align stage filled.
 cudaError_t launch_gather_rows(const void* src, int64_t row_bytes, const int32_t* sorted_pairs,
                                const int32_t* block_start, int E, int topk, int64_t cap, void* dst, cudaStream_t st);

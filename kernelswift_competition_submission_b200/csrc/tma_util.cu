@@ -60,4 +60,16 @@ bool make_fp8_map(CUtensorMap* m, const void* base, int rank, const uint64_t* di
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// fp32 table map, no swizzle: innermost box of `box_rows` elements, one row of the outer dimension.
+bool make_f32_rows_map(CUtensorMap* m, const float* base, const uint64_t* dims, const uint64_t* strides_bytes,
+                       uint32_t box_rows) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return false;
+  cuuint64_t gdim[2] = {dims[0], dims[1]}, gstr[1] = {strides_bytes[0]};
+  cuuint32_t box[2] = {box_rows, 1}, estr[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), gdim, gstr, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace moe
