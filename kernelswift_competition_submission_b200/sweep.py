@@ -1,0 +1,189 @@
+"""Per-configuration measurements of the MoE-layer path on one B200.
+
+    python -m kernelswift_competition_submission_b200.sweep [--iters N] [--only NAME ...]
+
+One JSON line per configuration row, each timed with CUDA events on the
+launching stream after warm-up, L2 flushed (a 256 MiB write) before every
+timed call, median over the calls:
+
+  grouped_topk   M = 128 and 32768, E = 256, sigmoid + bias, 8 groups / top-4, k = 8, x2.5
+  mixtral        M = 256, E = 8, top-2 softmax routing, K = 4096, N = 14336, bf16
+  dsv3_bf16      grouped_topk + fused_moe at the DeepSeek-V3 shape, M = 1, 64, 512, 4096
+  dsv3_fp8       the same with e4m3 weights (128 x 128 block scales) and per-token-per-128
+                 activation quantisation, M = 1, 8, 32, 128
+
+Each line carries the algorithmic work (FLOPs = 6 M k K N for the expert path;
+bytes = A 3 K N b_w (+ block scales) + M K b_x + M K 2 + M k 8 + M E 4 with A the
+distinct experts hit; grouped_topk alone: M E 4 + E 4 + M k 8), the binding
+roofline (measured HBM GB/s or tensor TFLOP/s from MEASURED_PEAKS.json, e4m3 at
+twice the bf16 rate) and the fraction of it achieved. Inputs are seeded synthetic
+Gaussians with the configurations' shapes; weights ~N(0, 1/sqrt(fan_in)).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import statistics
+from pathlib import Path
+
+import torch
+
+from . import ops
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def _peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+class _Timer:
+    def __init__(self, dev):
+        self.flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def median_ms(self, fn, iters: int, warmup: int = 3) -> float:
+        for _ in range(warmup):
+            fn()
+        ts = []
+        for _ in range(iters):
+            self.flush.fill_(1)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            b.synchronize()
+            ts.append(a.elapsed_time(b))
+        return statistics.median(ts)
+
+
+def _weights(E, K, N, dev, seed):
+    w1 = torch.empty(E, 2 * N, K, dtype=torch.bfloat16, device=dev)
+    w2 = torch.empty(E, K, N, dtype=torch.bfloat16, device=dev)
+    for e in range(E):
+        g = torch.Generator(device=dev).manual_seed(seed + e)
+        w1[e].copy_(torch.randn(2 * N, K, generator=g, device=dev) / K ** 0.5)
+        w2[e].copy_(torch.randn(K, N, generator=g, device=dev) / N ** 0.5)
+    return w1, w2
+
+
+def _line(name, M, ms, flops, nbytes, peaks, tc_tflops, extra=None):
+    t_tc = flops / (tc_tflops * 1e12) if flops else 0.0
+    t_hbm = nbytes / (peaks["hbm_gbs"] * 1e9)
+    bound = "tensor" if t_tc > t_hbm else "hbm"
+    d = {"config": name, "tokens": M, "ms": ms, "tokens_per_s": M / (ms / 1e3),
+         "tflops": flops / (ms / 1e3) / 1e12 if flops else None, "gbs": nbytes / (ms / 1e3) / 1e9,
+         "alg_flops": flops, "alg_bytes": nbytes, "bound": bound,
+         "roofline_frac": max(t_tc, t_hbm) / (ms / 1e3),
+         "peak": {"hbm_gbs": peaks["hbm_gbs"], "tensor_tflops": tc_tflops, "source": peaks["source"]}}
+    if extra:
+        d.update(extra)
+    print(json.dumps(d), flush=True)
+
+
+def sweep_grouped_topk(dev, timer, peaks, iters):
+    E, k = 256, 8
+    bias = torch.randn(E, generator=torch.Generator(device=dev).manual_seed(44), device=dev) * 0.01
+    for M in (128, 32768):
+        g = torch.randn(M, E, generator=torch.Generator(device=dev).manual_seed(M), device=dev)
+        x = torch.empty(M, 1, dtype=torch.bfloat16, device=dev)
+        ms = timer.median_ms(lambda: ops.grouped_topk(x, g, k, True, 8, 4, "sigmoid", 2.5,
+                                                      e_score_correction_bias=bias), iters)
+        _line("grouped_topk", M, ms, 0, M * E * 4 + E * 4 + M * k * 8, peaks, peaks["bf16_tflops"])
+
+
+def _layer_bytes(ids, E, K, N, M, k, wbytes, scale_bytes=0):
+    A = int(torch.unique(ids).numel())
+    return A * (3 * K * N * wbytes + scale_bytes) + M * K * 2 * 2 + M * k * 8 + M * E * 4, A
+
+
+def sweep_mixtral(dev, timer, peaks, iters):
+    E, k, K, N, M = 8, 2, 4096, 14336, 256
+    w1, w2 = _weights(E, K, N, dev, seed=5000)
+    gen = torch.Generator(device=dev).manual_seed(42)
+    x = torch.randn(M, K, generator=gen, device=dev).to(torch.bfloat16)
+    logits = torch.randn(M, E, generator=gen, device=dev)
+    out = torch.empty(M, K, dtype=torch.bfloat16, device=dev)
+    ws = torch.empty(ops.fused_moe_workspace_bytes(M, E, k, K, N), dtype=torch.uint8, device=dev)
+
+    def run():
+        w, ids = ops.softmax_topk(logits, k)
+        ops.fused_moe(x, w1, w2, w, ids, out=out, workspace=ws)
+
+    ms = timer.median_ms(run, iters)
+    _, ids = ops.softmax_topk(logits, k)
+    nbytes, A = _layer_bytes(ids, E, K, N, M, k, 2)
+    _line("mixtral_bf16", M, ms, 6.0 * M * k * K * N, nbytes, peaks, peaks["bf16_tflops"], {"experts_hit": A})
+
+
+def _dsv3_inputs(M, dev):
+    gen = torch.Generator(device=dev).manual_seed(1000 + M)
+    x = torch.randn(M, 7168, generator=gen, device=dev).to(torch.bfloat16)
+    g = torch.randn(M, 256, generator=gen, device=dev)
+    bias = torch.randn(256, generator=torch.Generator(device=dev).manual_seed(44), device=dev) * 0.01
+    return x, g, bias
+
+
+def sweep_dsv3(dev, timer, peaks, iters, fp8: bool):
+    E, k, K, N = 256, 8, 7168, 2048
+    w1, w2 = _weights(E, K, N, dev, seed=43_000)
+    if fp8:
+        w1q, w1s = ops.quantize_weights_fp8(w1)
+        w2q, w2s = ops.quantize_weights_fp8(w2)
+        del w1, w2
+        torch.cuda.empty_cache()
+    for M in ((1, 8, 32, 128) if fp8 else (1, 64, 512, 4096)):
+        x, g, bias = _dsv3_inputs(M, dev)
+        out = torch.empty(M, K, dtype=torch.bfloat16, device=dev)
+        if fp8:
+            ws = torch.empty(int(ops._lib.load().moe_fused_workspace_bytes_fp8(M, E, k, K, N)), dtype=torch.uint8,
+                             device=dev)
+        else:
+            ws = torch.empty(ops.fused_moe_workspace_bytes(M, E, k, K, N), dtype=torch.uint8, device=dev)
+
+        def run():
+            w, ids = ops.grouped_topk(x, g, k, True, 8, 4, "sigmoid", 2.5, e_score_correction_bias=bias)
+            if fp8:
+                ops.fused_moe_fp8(x, w1q, w1s, w2q, w2s, w, ids, out=out, workspace=ws)
+            else:
+                ops.fused_moe(x, w1, w2, w, ids, out=out, workspace=ws)
+
+        ms = timer.median_ms(run, iters)
+        _, ids = ops.grouped_topk(x, g, k, True, 8, 4, "sigmoid", 2.5, e_score_correction_bias=bias)
+        scale_bytes = 3 * (K // 128) * (N // 128) * 4 if fp8 else 0
+        nbytes, A = _layer_bytes(ids, E, K, N, M, k, 1 if fp8 else 2, scale_bytes)
+        tc = peaks["bf16_tflops"] * (2.0 if fp8 else 1.0)
+        _line("dsv3_fp8" if fp8 else "dsv3_bf16", M, ms, 6.0 * M * k * K * N, nbytes, peaks, tc,
+              {"experts_hit": A})
+        ops.check_device_status(dev)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--only", nargs="*", default=None,
+                    choices=["grouped_topk", "mixtral", "dsv3_bf16", "dsv3_fp8"])
+    a = ap.parse_args()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    peaks = _peaks()
+    timer = _Timer(dev)
+    want = set(a.only or ["grouped_topk", "mixtral", "dsv3_bf16", "dsv3_fp8"])
+    if "grouped_topk" in want:
+        sweep_grouped_topk(dev, timer, peaks, a.iters)
+    if "mixtral" in want:
+        sweep_mixtral(dev, timer, peaks, a.iters)
+        torch.cuda.empty_cache()
+    if "dsv3_bf16" in want:
+        sweep_dsv3(dev, timer, peaks, a.iters, fp8=False)
+        torch.cuda.empty_cache()
+    if "dsv3_fp8" in want:
+        sweep_dsv3(dev, timer, peaks, a.iters, fp8=True)
+
+
+if __name__ == "__main__":
+    main()
