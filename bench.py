@@ -61,6 +61,9 @@ def parse():
                     help="expert-parallel overlap: token chunks per step (default: the layer's choice)")
     ap.add_argument("--ep-reserve-sms", type=int, default=None,
                     help="expert-parallel overlap: SMs the expert GEMMs leave to the all-to-alls")
+    ap.add_argument("--replicate-hot", type=int, default=0,
+                    help="expert-parallel: replicate the N busiest experts (from the first batch's routing) on "
+                         "every rank")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=5)
     return ap.parse_args()
@@ -148,6 +151,20 @@ def make_inputs(M_local, rank, dev, skewed):
         hot = torch.randperm(DSV3["E"], generator=torch.Generator().manual_seed(44))[:16]
         bias[hot.to(dev)] += 2.0
     return x, g, bias
+
+
+def make_expert_weights(expert_ids, dev):
+    """The weights make_weights gives experts `expert_ids` (same per-expert seeds)."""
+    import torch
+
+    K, N = DSV3["K"], DSV3["N"]
+    w1 = torch.empty(len(expert_ids), 2 * N, K, dtype=torch.bfloat16, device=dev)
+    w2 = torch.empty(len(expert_ids), K, N, dtype=torch.bfloat16, device=dev)
+    for i, e in enumerate(expert_ids):
+        gen = torch.Generator(device=dev).manual_seed(43_000 + e)
+        w1[i].copy_(torch.randn(2 * N, K, generator=gen, device=dev) / K ** 0.5)
+        w2[i].copy_(torch.randn(K, N, generator=gen, device=dev) / N ** 0.5)
+    return w1, w2
 
 
 def make_weights(E_local, e0, dev):
@@ -312,6 +329,12 @@ def run_native(args):
                                   **{k_: v_ for k_, v_ in (("chunks", args.ep_chunks),
                                                            ("reserve_sms", args.ep_reserve_sms)) if v_ is not None})
 
+        if args.replicate_hot > 0:
+            _, ids0 = layer.route_fn(x, g)
+            hot = layer.hot_experts(ids0, args.replicate_hot)
+            layer.replicate(hot, *make_expert_weights(hot, dev))
+            del ids0
+
         def step(events=None):
             return layer.forward(x, g, events=events)
 
@@ -429,6 +452,8 @@ def run_native(args):
     }
     if world > 1:
         result["config"]["ep_overlap"] = {"chunks": layer.chunks, "reserve_sms": layer.reserve_sms}
+        if layer.replicated:
+            result["config"]["replicated_experts"] = layer.replicated
         result["ep_phases_ms_rank0"] = phases
         result["ep_local_pairs_rank0"] = pairs_local
 

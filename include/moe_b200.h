@@ -270,6 +270,20 @@ MOE_API int moe_ep_pack(int dtype, const void* hidden_states, const int32_t* top
 MOE_API int moe_ep_combine(int dtype, const void* returned_rows, const int32_t* tok_rows,
                            int64_t num_tokens, int hidden_size, int world, void* out, void* stream);
 
+/* Expert placement by table instead of contiguous ranges: expert_map int32 [num_experts]
+ * holds (rank << 16) | local_id for every expert, so a rank can keep replicas of hot
+ * experts and route their pairs to itself (the map is then per rank). Otherwise the
+ * same as moe_ep_plan / moe_ep_pack (no reference counterpart: load placement for
+ * skewed routing). */
+MOE_API int moe_ep_plan_mapped(const int32_t* topk_ids, int64_t num_tokens, int topk, int num_experts,
+                               const int32_t* expert_map, int world, int32_t* scratch, int32_t* offsets,
+                               int64_t* counts, void* stream);
+MOE_API int moe_ep_pack_mapped(int dtype, const void* hidden_states, const int32_t* topk_ids,
+                               const float* topk_weights, int64_t num_tokens, int hidden_size, int topk,
+                               int num_experts, const int32_t* expert_map, int world, int32_t* scratch,
+                               const int32_t* offsets, void* send_x, int32_t* send_meta, int32_t* tok_rows,
+                               void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -63,6 +63,9 @@ SIGNATURES = {
     "moe_ep_send_capacity": (_i64, [_i64, _i32, _i32]),
     "moe_ep_plan": (_i32, [_c_p, _i64, _i32, _i32, _i32, _c_p, _c_p, _c_p, _c_p]),
     "moe_ep_pack": (_i32, [_i32, _c_p, _c_p, _c_p, _i64, _i32, _i32, _i32, _i32, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p]),
+    "moe_ep_plan_mapped": (_i32, [_c_p, _i64, _i32, _i32, _c_p, _i32, _c_p, _c_p, _c_p, _c_p]),
+    "moe_ep_pack_mapped": (_i32, [_i32, _c_p, _c_p, _c_p, _i64, _i32, _i32, _i32, _c_p, _i32, _c_p, _c_p, _c_p, _c_p,
+                                  _c_p, _c_p]),
     "moe_ep_combine": (_i32, [_i32, _c_p, _c_p, _i64, _i32, _i32, _c_p, _c_p]),
 }
 

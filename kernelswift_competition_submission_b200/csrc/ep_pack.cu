@@ -2,7 +2,9 @@
 // code; these serve the expert-parallel form of its MoE layer).
 //
 // A token is sent once to every rank that owns at least one of its top-k
-// experts (rank d owns experts [d * epr, (d + 1) * epr)). Three launches:
+// experts (rank d owns experts [d * epr, (d + 1) * epr), or, with an expert map,
+// the experts the map places on d, which lets every rank hold replicas of hot
+// experts and keep those pairs at home). Three launches:
 //   ep_count_kernel    per-destination row counts (shared-memory histogram of
 //                      each token's destination set, then global atomics); the
 //                      last CTA scans them into row offsets and also writes the
@@ -28,25 +30,36 @@ namespace {
 constexpr int kEpThreads = 256;
 constexpr int kEpMaxWorld = 64;
 
-__device__ __forceinline__ uint64_t dest_mask(const int32_t* ids_row, int topk, int epr, int world) {
+// Where expert e lives: rank e / epr, local id e % epr, or, with an expert map,
+// rank map[e] >> 16 and local id map[e] & 0xffff (ranks holding replicas of hot
+// experts route those experts to themselves). Experts outside [0, E) are ignored.
+struct ExpertPlace {
+  const int32_t* map;
+  int epr, E;
+  __device__ __forceinline__ bool valid(int e) const { return e >= 0 && e < E; }
+  __device__ __forceinline__ int dest(int e) const { return map ? (__ldg(map + e) >> 16) : e / epr; }
+  __device__ __forceinline__ int local(int e) const { return map ? (__ldg(map + e) & 0xffff) : e % epr; }
+};
+
+__device__ __forceinline__ uint64_t dest_mask(const int32_t* ids_row, int topk, const ExpertPlace& pl) {
   uint64_t m = 0;
   for (int j = 0; j < topk; ++j) {
     const int e = __ldg(ids_row + j);
-    if (e >= 0 && e < epr * world) m |= 1ull << (e / epr);
+    if (pl.valid(e)) m |= 1ull << pl.dest(e);
   }
   return m;
 }
 
 // meta: [world] counts | [world] cursors | [1] done | [world + 1] offsets (int32), counts64 separate
 __global__ void __launch_bounds__(kEpThreads)
-ep_count_kernel(const int32_t* __restrict__ ids, int64_t M, int topk, int epr, int world, int32_t* counts,
+ep_count_kernel(const int32_t* __restrict__ ids, int64_t M, int topk, ExpertPlace pl, int world, int32_t* counts,
                 int32_t* done, int32_t* offsets, int64_t* counts64) {
   __shared__ int s_cnt[kEpMaxWorld];
   __shared__ int s_last;
   for (int i = threadIdx.x; i < world; i += blockDim.x) s_cnt[i] = 0;
   __syncthreads();
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < M; t += (int64_t)gridDim.x * blockDim.x) {
-    uint64_t m = dest_mask(ids + t * topk, topk, epr, world);
+    uint64_t m = dest_mask(ids + t * topk, topk, pl);
     while (m) {
       const int d = __ffsll((long long)m) - 1;
       m &= m - 1;
@@ -75,12 +88,12 @@ ep_count_kernel(const int32_t* __restrict__ ids, int64_t M, int topk, int epr, i
 template <typename T>
 __global__ void __launch_bounds__(kEpThreads)
 ep_pack_kernel(const uint4* __restrict__ x, const int32_t* __restrict__ ids, const float* __restrict__ w, int64_t M,
-               int topk, int epr, int world, int64_t row_vecs, const int32_t* __restrict__ offsets, int32_t* cursor,
+               int topk, ExpertPlace pl, int world, int64_t row_vecs, const int32_t* __restrict__ offsets, int32_t* cursor,
                uint4* __restrict__ send_x, int32_t* __restrict__ send_meta, int32_t* __restrict__ tok_rows) {
   const int lane = threadIdx.x & 31;
   const int64_t t = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   if (t >= M) return;
-  const uint64_t mask = dest_mask(ids + t * topk, topk, epr, world);
+  const uint64_t mask = dest_mask(ids + t * topk, topk, pl);
   const int my_e = lane < topk ? __ldg(ids + t * topk + lane) : -1;
   const float my_w = lane < topk ? __ldg(w + t * topk + lane) : 0.f;
   for (int d = 0; d < world; ++d) {
@@ -90,8 +103,8 @@ ep_pack_kernel(const uint4* __restrict__ x, const int32_t* __restrict__ ids, con
       row = __shfl_sync(0xffffffffu, row, 0);
       // metadata: ids in d's numbering (-1 if not owned by d), then the weights
       if (lane < topk) {
-        const bool own = my_e >= 0 && my_e / epr == d && my_e < epr * world;
-        send_meta[(int64_t)row * 2 * topk + lane] = own ? my_e - d * epr : -1;
+        const bool own = pl.valid(my_e) && pl.dest(my_e) == d;
+        send_meta[(int64_t)row * 2 * topk + lane] = own ? pl.local(my_e) : -1;
         send_meta[(int64_t)row * 2 * topk + topk + lane] = __float_as_int(my_w);
       }
       const uint4* src = x + t * row_vecs;
@@ -143,27 +156,26 @@ extern "C" int64_t moe_ep_send_capacity(int64_t num_tokens, int topk, int world)
   return num_tokens * (int64_t)(topk < world ? topk : world);
 }
 
-extern "C" int moe_ep_plan(const int32_t* topk_ids, int64_t num_tokens, int topk, int experts_per_rank, int world,
-                           int32_t* scratch, int32_t* offsets, int64_t* counts, void* stream) {
-  using namespace moe;
-  if (!ep_args_ok(num_tokens, topk, experts_per_rank, world)) return MOE_ERR_INVALID_ARG;
+namespace moe {
+namespace {
+
+int ep_plan_impl(const int32_t* topk_ids, int64_t num_tokens, int topk, ExpertPlace pl, int world, int32_t* scratch,
+                 int32_t* offsets, int64_t* counts, void* stream) {
   if (!scratch || !offsets || !counts || (num_tokens > 0 && !topk_ids)) return MOE_ERR_INVALID_ARG;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // scratch: [world] counts | [world] cursors | [1] done
   if (cudaMemsetAsync(scratch, 0, sizeof(int32_t) * (2 * (size_t)world + 1), st) != cudaSuccess) return MOE_ERR_CUDA;
   const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div(num_tokens, kEpThreads), 2 * num_sms()));
-  ep_count_kernel<<<blocks, kEpThreads, 0, st>>>(topk_ids, num_tokens, topk, experts_per_rank, world, scratch,
-                                                 scratch + 2 * world, offsets, counts);
+  ep_count_kernel<<<blocks, kEpThreads, 0, st>>>(topk_ids, num_tokens, topk, pl, world, scratch, scratch + 2 * world,
+                                                 offsets, counts);
   return cudaGetLastError() == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
 }
 
-extern "C" int moe_ep_pack(int dtype, const void* hidden_states, const int32_t* topk_ids, const float* topk_weights,
-                           int64_t num_tokens, int hidden_size, int topk, int experts_per_rank, int world,
-                           int32_t* scratch, const int32_t* offsets, void* send_x, int32_t* send_meta,
-                           int32_t* tok_rows, void* stream) {
-  using namespace moe;
+int ep_pack_impl(int dtype, const void* hidden_states, const int32_t* topk_ids, const float* topk_weights,
+                 int64_t num_tokens, int hidden_size, int topk, ExpertPlace pl, int world, int32_t* scratch,
+                 const int32_t* offsets, void* send_x, int32_t* send_meta, int32_t* tok_rows, void* stream) {
   if (dtype != MOE_DTYPE_BF16 && dtype != MOE_DTYPE_FP16) return MOE_ERR_UNSUPPORTED;
-  if (!ep_args_ok(num_tokens, topk, experts_per_rank, world) || hidden_size <= 0) return MOE_ERR_INVALID_ARG;
+  if (hidden_size <= 0) return MOE_ERR_INVALID_ARG;
   if (hidden_size % 8 != 0) return MOE_ERR_BAD_SHAPE;
   if (num_tokens == 0) return MOE_OK;
   if (!hidden_states || !topk_ids || !topk_weights || !scratch || !offsets || !send_x || !send_meta || !tok_rows)
@@ -175,13 +187,61 @@ extern "C" int moe_ep_pack(int dtype, const void* hidden_states, const int32_t* 
   const int64_t row_vecs = (int64_t)hidden_size * 2 / 16;
   if (dtype == MOE_DTYPE_BF16)
     ep_pack_kernel<__nv_bfloat16><<<blocks, kEpThreads, 0, st>>>(
-        static_cast<const uint4*>(hidden_states), topk_ids, topk_weights, num_tokens, topk, experts_per_rank, world,
-        row_vecs, offsets, scratch + world, static_cast<uint4*>(send_x), send_meta, tok_rows);
+        static_cast<const uint4*>(hidden_states), topk_ids, topk_weights, num_tokens, topk, pl, world, row_vecs,
+        offsets, scratch + world, static_cast<uint4*>(send_x), send_meta, tok_rows);
   else
     ep_pack_kernel<__half><<<blocks, kEpThreads, 0, st>>>(
-        static_cast<const uint4*>(hidden_states), topk_ids, topk_weights, num_tokens, topk, experts_per_rank, world,
-        row_vecs, offsets, scratch + world, static_cast<uint4*>(send_x), send_meta, tok_rows);
+        static_cast<const uint4*>(hidden_states), topk_ids, topk_weights, num_tokens, topk, pl, world, row_vecs,
+        offsets, scratch + world, static_cast<uint4*>(send_x), send_meta, tok_rows);
   return cudaGetLastError() == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
+}
+
+// expert_map entries: (rank << 16) | local id, rank < world, local id < 65536
+bool map_ok(const int32_t* expert_map, int num_experts, int world) {
+  return expert_map && num_experts > 0 && world > 0 && world <= kEpMaxWorld;
+}
+
+}  // namespace
+}  // namespace moe
+
+extern "C" int moe_ep_plan(const int32_t* topk_ids, int64_t num_tokens, int topk, int experts_per_rank, int world,
+                           int32_t* scratch, int32_t* offsets, int64_t* counts, void* stream) {
+  using namespace moe;
+  if (!ep_args_ok(num_tokens, topk, experts_per_rank, world)) return MOE_ERR_INVALID_ARG;
+  return ep_plan_impl(topk_ids, num_tokens, topk, ExpertPlace{nullptr, experts_per_rank, experts_per_rank * world},
+                      world, scratch, offsets, counts, stream);
+}
+
+extern "C" int moe_ep_pack(int dtype, const void* hidden_states, const int32_t* topk_ids, const float* topk_weights,
+                           int64_t num_tokens, int hidden_size, int topk, int experts_per_rank, int world,
+                           int32_t* scratch, const int32_t* offsets, void* send_x, int32_t* send_meta,
+                           int32_t* tok_rows, void* stream) {
+  using namespace moe;
+  if (!ep_args_ok(num_tokens, topk, experts_per_rank, world)) return MOE_ERR_INVALID_ARG;
+  return ep_pack_impl(dtype, hidden_states, topk_ids, topk_weights, num_tokens, hidden_size, topk,
+                      ExpertPlace{nullptr, experts_per_rank, experts_per_rank * world}, world, scratch, offsets,
+                      send_x, send_meta, tok_rows, stream);
+}
+
+extern "C" int moe_ep_plan_mapped(const int32_t* topk_ids, int64_t num_tokens, int topk, int num_experts,
+                                  const int32_t* expert_map, int world, int32_t* scratch, int32_t* offsets,
+                                  int64_t* counts, void* stream) {
+  using namespace moe;
+  if (!ep_args_ok(num_tokens, topk, 1, world) || !map_ok(expert_map, num_experts, world)) return MOE_ERR_INVALID_ARG;
+  return ep_plan_impl(topk_ids, num_tokens, topk, ExpertPlace{expert_map, 1, num_experts}, world, scratch, offsets,
+                      counts, stream);
+}
+
+extern "C" int moe_ep_pack_mapped(int dtype, const void* hidden_states, const int32_t* topk_ids,
+                                  const float* topk_weights, int64_t num_tokens, int hidden_size, int topk,
+                                  int num_experts, const int32_t* expert_map, int world, int32_t* scratch,
+                                  const int32_t* offsets, void* send_x, int32_t* send_meta, int32_t* tok_rows,
+                                  void* stream) {
+  using namespace moe;
+  if (!ep_args_ok(num_tokens, topk, 1, world) || !map_ok(expert_map, num_experts, world)) return MOE_ERR_INVALID_ARG;
+  return ep_pack_impl(dtype, hidden_states, topk_ids, topk_weights, num_tokens, hidden_size, topk,
+                      ExpertPlace{expert_map, 1, num_experts}, world, scratch, offsets, send_x, send_meta, tok_rows,
+                      stream);
 }
 
 extern "C" int moe_ep_combine(int dtype, const void* returned_rows, const int32_t* tok_rows, int64_t num_tokens,

@@ -37,24 +37,34 @@ import torch
 import torch.distributed as dist
 
 
-def plan_dispatch(ids: torch.Tensor, w: torch.Tensor, experts_per_rank: int, world: int):
+def plan_dispatch(ids: torch.Tensor, w: torch.Tensor, experts_per_rank: int, world: int,
+                  expert_map: torch.Tensor | None = None):
     """Deduplicated per-destination send list for routed tokens.
 
-    ids int [M, k] global expert ids, w float [M, k].
+    ids int [M, k] global expert ids, w float [M, k]. Expert e lives on rank
+    e // experts_per_rank as local expert e % experts_per_rank, or, with
+    ``expert_map`` (int [E], (rank << 16) | local id), where the map puts it.
     Returns (send_tok int64 [S], send_counts int64 [world], send_ids int32 [S, k], send_w fp32 [S, k]),
     rows ordered by destination rank then token.
     """
     M, k = ids.shape
     ids64 = ids.long()
-    valid = (ids64 >= 0) & (ids64 < experts_per_rank * world)
-    dst = torch.div(ids64, experts_per_rank, rounding_mode="floor").clamp(0, world - 1)
+    n_exp = experts_per_rank * world if expert_map is None else expert_map.numel()
+    valid = (ids64 >= 0) & (ids64 < n_exp)
+    if expert_map is None:
+        dst = torch.div(ids64, experts_per_rank, rounding_mode="floor").clamp(0, world - 1)
+        loc = ids64 - dst * experts_per_rank
+    else:
+        m = expert_map.long()[ids64.clamp(0, n_exp - 1)]
+        dst = (m >> 16).clamp(0, world - 1)
+        loc = m & 0xFFFF
     hit = torch.zeros(M, world, dtype=torch.int32, device=ids.device)
     hit.scatter_add_(1, dst, valid.to(torch.int32))
     hit = hit > 0
     send_dst, send_tok = hit.t().nonzero(as_tuple=True)  # sorted by destination, then token
     send_counts = hit.sum(0).to(torch.int64)
     own = (dst[send_tok] == send_dst[:, None]) & valid[send_tok]
-    local = ids64[send_tok] - send_dst[:, None] * experts_per_rank
+    local = loc[send_tok]
     send_ids = torch.where(own, local, torch.full_like(local, -1)).to(torch.int32)
     send_w = w[send_tok].to(torch.float32)
     return send_tok, send_counts, send_ids, send_w
@@ -106,6 +116,45 @@ class ExpertParallelMoE:
         self._comm = None
         self._bufs = {}
         self.gemm_log = []  # (gemm1 ms, gemm2 ms, local pairs) per chunk, when profiling
+        self._expert_map = None  # int32 [E]: (rank << 16) | local id, set by replicate()
+        self.replicated = []
+
+    # ------------------------------------------------------------------ hot-expert replicas
+    def replicate(self, expert_ids, w1_rep, w2_rep):
+        """Keep replicas of ``expert_ids`` (weights w1_rep [R, 2N, K], w2_rep [R, K, N], the
+        same on every rank) on this rank and compute their pairs where the token lives.
+
+        Every rank must call it with the same ids. Pairs routed to a replicated expert then
+        never cross the network and spread over all ranks with the tokens, instead of all
+        landing on the expert's owner; the other experts keep their owner. The result is the
+        same layer: each pair is still computed once, with the same weights.
+        """
+        ids = [int(e) for e in expert_ids]
+        if len(set(ids)) != len(ids) or any(e < 0 or e >= self.E for e in ids):
+            raise ValueError("replicate: expert ids must be distinct and in [0, num_experts)")
+        if w1_rep.shape[0] != len(ids) or w2_rep.shape[0] != len(ids):
+            raise ValueError("replicate: one weight slice per replicated expert")
+        if self.E_local + len(ids) > 0xFFFF:
+            raise ValueError("replicate: too many local experts")
+        base_w1 = self.w1[: self.E_local]
+        base_w2 = self.w2[: self.E_local]
+        self.w1 = torch.cat([base_w1, w1_rep.to(base_w1.dtype)], dim=0).contiguous() if ids else base_w1
+        self.w2 = torch.cat([base_w2, w2_rep.to(base_w2.dtype)], dim=0).contiguous() if ids else base_w2
+        emap = [((e // self.E_local) << 16) | (e % self.E_local) for e in range(self.E)]
+        for j, e in enumerate(ids):
+            emap[e] = (self.rank << 16) | (self.E_local + j)
+        self.replicated = ids
+        self._expert_map = torch.tensor(emap, dtype=torch.int32, device=self.w1.device) if ids else None
+
+    def hot_experts(self, topk_ids, n):
+        """The n experts with the most (token, slot) pairs in ``topk_ids`` summed over all
+        ranks (ties to the lower id): the candidates for ``replicate``."""
+        cnt = torch.bincount(topk_ids.reshape(-1).long().clamp(0, self.E - 1), minlength=self.E).to(torch.int64)
+        if dist.get_backend(self.group) == "nccl" and not cnt.is_cuda:
+            cnt = cnt.cuda()
+        dist.all_reduce(cnt, group=self.group)
+        order = sorted(range(self.E), key=lambda e: (-int(cnt[e]), e))
+        return order[:n]
 
     # ------------------------------------------------------------------ default (CUDA) stages
     def _route_cuda(self, x, gating):
@@ -124,7 +173,7 @@ class ExpertParallelMoE:
                 for e in events:
                     e.record()
             return torch.empty(0, x.shape[1], dtype=x.dtype, device=x.device) if out is None else out
-        need = fused_moe_workspace_bytes(M, self.E_local, ids.shape[1], x.shape[1], self.w2.shape[2])
+        need = fused_moe_workspace_bytes(M, self.w1.shape[0], ids.shape[1], x.shape[1], self.w2.shape[2])
         if self._ws is None or self._ws.numel() < need:
             self._ws = torch.empty(int(need * 1.25) + 256, dtype=torch.uint8, device=x.device)
         return fused_moe_staged(x, self.w1, self.w2, w, ids, workspace=self._ws, events=events, out=out,
@@ -160,7 +209,8 @@ class ExpertParallelMoE:
         if x.is_cuda:
             send_x, send_meta, send_counts, tok_rows = self._dispatch_cuda(x, w, ids)
         else:  # CPU tensors (gloo tests): the same plan restated with torch ops
-            send_tok, send_counts, send_ids, send_w = plan_dispatch(ids, w, self.E_local, self.world)
+            send_tok, send_counts, send_ids, send_w = plan_dispatch(ids, w, self.E_local, self.world,
+                                                                    self._expert_map)
             send_x = x.index_select(0, send_tok)
             send_meta = torch.cat([send_ids, send_w.view(torch.int32)], dim=1).contiguous()
         recv_counts = torch.empty_like(send_counts)
@@ -317,11 +367,22 @@ class ExpertParallelMoE:
         ids32 = ids.to(torch.int32).contiguous()
         w32 = w.to(torch.float32).contiguous()
         st = _stream(dev)
-        _lib.check(lib.moe_ep_plan(_ptr(ids32), M, self.topk, self.E_local, self.world, _ptr(scratch),
-                                   _ptr(offsets), _ptr(counts), st), "moe_ep_plan")
-        _lib.check(lib.moe_ep_pack(_DTYPES[x.dtype], _ptr(xc), _ptr(ids32), _ptr(w32), M, K, self.topk, self.E_local,
-                                   self.world, _ptr(scratch), _ptr(offsets), _ptr(send_x), _ptr(send_meta),
-                                   _ptr(tok_rows), st), "moe_ep_pack")
+        if self._expert_map is None:
+            _lib.check(lib.moe_ep_plan(_ptr(ids32), M, self.topk, self.E_local, self.world, _ptr(scratch),
+                                       _ptr(offsets), _ptr(counts), st), "moe_ep_plan")
+            _lib.check(lib.moe_ep_pack(_DTYPES[x.dtype], _ptr(xc), _ptr(ids32), _ptr(w32), M, K, self.topk,
+                                       self.E_local, self.world, _ptr(scratch), _ptr(offsets), _ptr(send_x),
+                                       _ptr(send_meta), _ptr(tok_rows), st), "moe_ep_pack")
+        else:
+            emap = self._expert_map
+            if emap.device != dev:
+                emap = self._expert_map = emap.to(dev)
+            _lib.check(lib.moe_ep_plan_mapped(_ptr(ids32), M, self.topk, self.E, _ptr(emap), self.world,
+                                              _ptr(scratch), _ptr(offsets), _ptr(counts), st), "moe_ep_plan_mapped")
+            _lib.check(lib.moe_ep_pack_mapped(_DTYPES[x.dtype], _ptr(xc), _ptr(ids32), _ptr(w32), M, K, self.topk,
+                                              self.E, _ptr(emap), self.world, _ptr(scratch), _ptr(offsets),
+                                              _ptr(send_x), _ptr(send_meta), _ptr(tok_rows), st),
+                       "moe_ep_pack_mapped")
         return send_x, send_meta, counts, tok_rows
 
     def _combine_cuda(self, back, tok_rows, M, K, dtype):

@@ -151,3 +151,67 @@ def test_rank_leaving_makes_peers_fail_not_hang():
     res = _run(2, [0, 0], target=_leaver, timeout=60)
     assert res.get(1, ("?",))[0] == "left", res
     assert res.get(0, ("?",))[0] == "raised", res
+
+
+def _worker_replicated(rank, world, port, q, m_per_rank):
+    """Same as _worker, with the three busiest experts replicated on every rank."""
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        from datetime import timedelta
+
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=30))
+        w1, w2 = _weights()
+        el = E // world
+        w1l, w2l = w1[rank * el:(rank + 1) * el], w2[rank * el:(rank + 1) * el]
+        holder = {}
+
+        def experts(x, w, ids, events=None):
+            lw1, lw2 = holder["layer"].w1.numpy(), holder["layer"].w2.numpy()
+            ids_np = ids.numpy()
+            w_np = np.where(ids_np >= 0, w.numpy(), 0.0).astype(np.float32)
+            if x.shape[0] == 0:
+                return torch.zeros(0, HID)
+            return torch.from_numpy(moe_experts_ref(x.numpy(), lw1, lw2, w_np, np.clip(ids_np, 0, None)))
+
+        layer = ExpertParallelMoE(torch.from_numpy(w1l), torch.from_numpy(w2l), num_experts=E, topk=K_TOP,
+                                  route_fn=_route, expert_fn=experts)
+        holder["layer"] = layer
+        m = m_per_rank[rank]
+        x, g = _tokens(rank, m)
+        _, ids = _route(None, torch.from_numpy(g))
+        hot = layer.hot_experts(ids, 3)
+        layer.replicate(hot, torch.from_numpy(w1[hot]), torch.from_numpy(w2[hot]))
+        out = layer.forward(torch.from_numpy(x), torch.from_numpy(g))
+        w, ids = _route(None, torch.from_numpy(g))
+        ref = moe_experts_ref(x, w1, w2, w.numpy(), ids.numpy())
+        err = float(np.abs(out.numpy() - ref).max()) if m else 0.0
+        q.put((rank, "ok", (err, hot)))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        q.put((rank, "error", traceback.format_exc()))
+
+
+@pytest.mark.parametrize("world,m", [(2, [37, 50]), (4, [20, 0, 33, 8])])
+def test_ep_replicated_hot_experts_match(world, m):
+    res = _run(world, m, target=_worker_replicated)
+    assert len(res) == world, res
+    hots = set()
+    for r, (status, val) in res.items():
+        assert status == "ok", val
+        err, hot = val
+        assert err < 1e-4, f"rank {r} max err {err}"
+        hots.add(tuple(hot))
+    assert len(hots) == 1  # every rank picked the same experts
+
+
+def test_plan_dispatch_with_expert_map_keeps_replicas_home():
+    # 8 experts on 2 ranks; rank 1's view: expert 2 (owned by rank 0) replicated at rank 1, local slot 4
+    emap = torch.tensor([(e // 4) << 16 | (e % 4) for e in range(8)], dtype=torch.int32)
+    emap[2] = (1 << 16) | 4
+    ids = torch.tensor([[2, 5], [0, 2], [2, 6]], dtype=torch.int32)
+    w = torch.ones(3, 2)
+    tok, counts, lids, _ = plan_dispatch(ids, w, experts_per_rank=4, world=2, expert_map=emap)
+    assert counts.tolist() == [1, 3]                    # only token 1's expert 0 leaves for rank 0
+    assert tok.tolist() == [1, 0, 1, 2]
+    assert lids.tolist() == [[0, -1], [4, 1], [-1, 4], [4, 2]]

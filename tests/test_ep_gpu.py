@@ -25,7 +25,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, mode):
     try:
         import torch.distributed as dist
         from datetime import timedelta
@@ -48,7 +48,12 @@ def _worker(rank, world, port, q):
         el = E // world
         layer = ExpertParallelMoE(w1[rank * el:(rank + 1) * el].contiguous(), w2[rank * el:(rank + 1) * el].contiguous(),
                                   num_experts=E, topk=K_TOP, num_expert_group=8, topk_group=4,
-                                  scoring_func="sigmoid", routed_scaling_factor=2.5, e_score_correction_bias=bias)
+                                  scoring_func="sigmoid", routed_scaling_factor=2.5, e_score_correction_bias=bias,
+                                  chunks=2 if mode == "overlap" else 1)
+        if mode == "replicate":
+            w_, ids_ = pkg.grouped_topk(x, g, K_TOP, True, 8, 4, "sigmoid", 2.5, e_score_correction_bias=bias)
+            hot = layer.hot_experts(ids_, 5)
+            layer.replicate(hot, w1[hot], w2[hot])
         out = layer.forward(x, g)
         ref = pkg.moe_layer(x, g, w1, w2, topk=K_TOP, renormalize=True, num_expert_group=8, topk_group=4,
                             scoring_func="sigmoid", routed_scaling_factor=2.5, e_score_correction_bias=bias)
@@ -62,14 +67,17 @@ def _worker(rank, world, port, q):
         q.put((rank, "error", traceback.format_exc()))
 
 
-def test_ep_two_gpus_matches_single_gpu(cuda_device):
+@pytest.mark.parametrize("mode", ["plain", "overlap", "replicate"])
+def test_ep_two_gpus_matches_single_gpu(cuda_device, mode):
+    """plain: one all-to-all each way; overlap: 2 token chunks on a side stream;
+    replicate: the 5 busiest experts replicated on both ranks (their pairs stay home)."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, mode)) for r in range(world)]
     for p in procs:
         p.start()
     res = {}
