@@ -153,20 +153,6 @@ def make_inputs(M_local, rank, dev, skewed):
     return x, g, bias
 
 
-def make_expert_weights(expert_ids, dev):
-    """The weights make_weights gives experts `expert_ids` (same per-expert seeds)."""
-    import torch
-
-    K, N = DSV3["K"], DSV3["N"]
-    w1 = torch.empty(len(expert_ids), 2 * N, K, dtype=torch.bfloat16, device=dev)
-    w2 = torch.empty(len(expert_ids), K, N, dtype=torch.bfloat16, device=dev)
-    for i, e in enumerate(expert_ids):
-        gen = torch.Generator(device=dev).manual_seed(43_000 + e)
-        w1[i].copy_(torch.randn(2 * N, K, generator=gen, device=dev) / K ** 0.5)
-        w2[i].copy_(torch.randn(K, N, generator=gen, device=dev) / N ** 0.5)
-    return w1, w2
-
-
 def make_weights(E_local, e0, dev):
     """Expert weights ~N(0, 1/sqrt(fan_in)) in bf16; expert e's values depend only on e."""
     import torch
@@ -331,8 +317,7 @@ def run_native(args):
 
         if args.replicate_hot > 0:
             _, ids0 = layer.route_fn(x, g)
-            hot = layer.hot_experts(ids0, args.replicate_hot)
-            layer.replicate(hot, *make_expert_weights(hot, dev))
+            layer.rebalance(ids0, args.replicate_hot)  # weights broadcast from the experts' owners
             del ids0
 
         def step(events=None):

@@ -146,6 +146,25 @@ class ExpertParallelMoE:
         self.replicated = ids
         self._expert_map = torch.tensor(emap, dtype=torch.int32, device=self.w1.device) if ids else None
 
+    def rebalance(self, topk_ids, n):
+        """Replicate the n busiest experts of ``topk_ids`` (summed over ranks) on every rank,
+        their weights broadcast from their owners (collective: every rank calls it with its
+        own routing sample). Returns the replicated expert ids."""
+        hot = self.hot_experts(topk_ids, n)
+        base_w1, base_w2 = self.w1[: self.E_local], self.w2[: self.E_local]
+        w1r = torch.empty((len(hot),) + tuple(base_w1.shape[1:]), dtype=base_w1.dtype, device=base_w1.device)
+        w2r = torch.empty((len(hot),) + tuple(base_w2.shape[1:]), dtype=base_w2.dtype, device=base_w2.device)
+        for j, e in enumerate(hot):
+            owner = e // self.E_local
+            if owner == self.rank:
+                w1r[j].copy_(base_w1[e % self.E_local])
+                w2r[j].copy_(base_w2[e % self.E_local])
+            src = dist.get_global_rank(self.group, owner) if self.group is not None else owner
+            dist.broadcast(w1r[j], src=src, group=self.group)
+            dist.broadcast(w2r[j], src=src, group=self.group)
+        self.replicate(hot, w1r, w2r)
+        return hot
+
     def hot_experts(self, topk_ids, n):
         """The n experts with the most (token, slot) pairs in ``topk_ids`` summed over all
         ranks (ties to the lower id): the candidates for ``replicate``."""

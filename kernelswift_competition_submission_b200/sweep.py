@@ -11,6 +11,8 @@ timed call, median over the calls:
   dsv3_bf16      grouped_topk + fused_moe at the DeepSeek-V3 shape, M = 1, 64, 512, 4096
   dsv3_fp8       the same with e4m3 weights (128 x 128 block scales) and per-token-per-128
                  activation quantisation, M = 1, 8, 32, 128
+  tasks          the reference's task shapes through the drop-in ModelNew modules (latency per
+                 call, the harness's protocol), graph replay and eager
 
 Each line carries the algorithmic work (FLOPs = 6 M k K N for the expert path;
 bytes = A 3 K N b_w (+ block scales) + M K b_x + M K 2 + M k 8 + M E 4 with A the
@@ -162,17 +164,64 @@ def sweep_dsv3(dev, timer, peaks, iters, fp8: bool):
         ops.check_device_status(dev)
 
 
+def sweep_tasks(dev, iters_unused=None):
+    """The reference's own task shapes through the drop-in ModelNew modules, timed the way
+    its harness times them: per call, host clock around the call and a device synchronise,
+    200 warm-up calls, median of 500. Reported for the graph-replay forward and for the
+    eager forward (the same ops launched one by one)."""
+    import importlib.util
+    import time
+
+    tasks = Path(__file__).resolve().parent / "tasks"
+
+    def load(name):
+        spec = importlib.util.spec_from_file_location(f"task_{name}", tasks / f"{name}.py")
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        return mod
+
+    def median_call_ms(fn, args):
+        for _ in range(200):
+            fn(*args)
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(500):
+            t0 = time.perf_counter()
+            fn(*args)
+            torch.cuda.synchronize()
+            ts.append((time.perf_counter() - t0) * 1e3)
+        return statistics.median(ts)
+
+    torch.manual_seed(42)
+    for name in ("grouped_topk", "fused_moe"):
+        mod = load(name)
+        model = mod.ModelNew(*mod.get_init_inputs()).to(dev)
+        args = [t.to(dev) for t in mod.get_inputs()]
+        with torch.no_grad():
+            graph_ms = median_call_ms(model, args)
+            if name == "fused_moe":
+                w1, w2 = model._prepared_weights(args[0].dtype)
+                eager_ms = median_call_ms(lambda a, b: model._forward_eager(a, b, w1, w2), args)
+            else:
+                eager_ms = median_call_ms(model._forward_eager, args)
+        print(json.dumps({"config": f"task_{name}", "tokens": int(args[0].shape[0]), "graph_replay_ms": graph_ms,
+                          "eager_ms": eager_ms, "protocol": "host clock per call + synchronize, median of 500 "
+                                                            "after 200 warm-up calls"}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--only", nargs="*", default=None,
-                    choices=["grouped_topk", "mixtral", "dsv3_bf16", "dsv3_fp8"])
+                    choices=["grouped_topk", "mixtral", "dsv3_bf16", "dsv3_fp8", "tasks"])
     a = ap.parse_args()
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     peaks = _peaks()
     timer = _Timer(dev)
-    want = set(a.only or ["grouped_topk", "mixtral", "dsv3_bf16", "dsv3_fp8"])
+    want = set(a.only or ["grouped_topk", "mixtral", "dsv3_bf16", "dsv3_fp8", "tasks"])
+    if "tasks" in want:
+        sweep_tasks(dev)
     if "grouped_topk" in want:
         sweep_grouped_topk(dev, timer, peaks, a.iters)
     if "mixtral" in want:

@@ -5,6 +5,8 @@ Constructor, parameter names and shapes match the reference
 the harness's ``load_state_dict`` weight copy works. The forward runs the
 softmax top-k routing kernel and the sm_100a expert path (align, tcgen05
 gate/up GEMM with fused SiLU*mul, tcgen05 down GEMM, top-k combine).
+Repeated calls on the same input buffers replay a CUDA graph of the whole
+forward (``graphs.GraphCache``: one launch instead of six kernels plus host work).
 Weights cast to the hidden dtype are cached and refreshed when the parameter's
 ``_version`` or storage changes (the idea of ``fused_moe/v1/fused_moe.py:285-303``);
 the cache is a plain attribute, not a registered buffer, so ``state_dict`` is
@@ -48,6 +50,9 @@ class ModelNew(nn.Module):
         nn.init.normal_(self.w2, std=0.02)
         self._ops = _bootstrap()
         self._cache = None
+        from kernelswift_competition_submission_b200.graphs import GraphCache
+
+        self._graph = GraphCache(self._forward_eager)
 
     def _prepared_weights(self, dtype):
         key = (dtype, self.w1.device, self.w1.data_ptr(), self.w1._version, self.w2.data_ptr(), self.w2._version)
@@ -58,10 +63,14 @@ class ModelNew(nn.Module):
             self._cache = (key, w1, w2)
         return self._cache[1], self._cache[2]
 
-    def forward(self, hidden_states: torch.Tensor, router_logits: torch.Tensor) -> torch.Tensor:
+    def _forward_eager(self, hidden_states, router_logits, w1, w2):
         w, ids = self._ops.softmax_topk(router_logits, self.top_k, self.renormalize)
-        w1, w2 = self._prepared_weights(hidden_states.dtype)
         return self._ops.fused_moe(hidden_states, w1, w2, w, ids)
+
+    def forward(self, hidden_states: torch.Tensor, router_logits: torch.Tensor) -> torch.Tensor:
+        # repeated calls on the same buffers replay one CUDA graph of the whole forward
+        w1, w2 = self._prepared_weights(hidden_states.dtype)
+        return self._graph(hidden_states, router_logits, w1, w2)
 
 
 def get_inputs():

@@ -42,11 +42,20 @@ class ModelNew(nn.Module):
         self.scoring_func = scoring_func
         self.routed_scaling_factor = routed_scaling_factor
         self._ops = _bootstrap()
+        self._graph = None
 
-    def forward(self, hidden_states: torch.Tensor, gating_output: torch.Tensor):
+    def _forward_eager(self, hidden_states, gating_output):
         return self._ops.grouped_topk(
             hidden_states, gating_output, self.topk, self.renormalize, self.num_expert_group,
             self.topk_group, self.scoring_func, self.routed_scaling_factor)
+
+    def forward(self, hidden_states: torch.Tensor, gating_output: torch.Tensor):
+        # repeated calls on the same buffers replay a CUDA graph of the routing kernel
+        if self._graph is None:
+            from kernelswift_competition_submission_b200.graphs import GraphCache
+
+            self._graph = GraphCache(self._forward_eager)
+        return self._graph(hidden_states, gating_output)
 
 
 def get_inputs():

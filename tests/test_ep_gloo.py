@@ -154,7 +154,8 @@ def test_rank_leaving_makes_peers_fail_not_hang():
 
 
 def _worker_replicated(rank, world, port, q, m_per_rank):
-    """Same as _worker, with the three busiest experts replicated on every rank."""
+    """Same as _worker, with the three busiest experts replicated on every rank (weights
+    broadcast from their owners by ``rebalance``)."""
     try:
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
         from datetime import timedelta
@@ -179,8 +180,7 @@ def _worker_replicated(rank, world, port, q, m_per_rank):
         m = m_per_rank[rank]
         x, g = _tokens(rank, m)
         _, ids = _route(None, torch.from_numpy(g))
-        hot = layer.hot_experts(ids, 3)
-        layer.replicate(hot, torch.from_numpy(w1[hot]), torch.from_numpy(w2[hot]))
+        hot = layer.rebalance(ids, 3)  # replica weights broadcast from their owners
         out = layer.forward(torch.from_numpy(x), torch.from_numpy(g))
         w, ids = _route(None, torch.from_numpy(g))
         ref = moe_experts_ref(x, w1, w2, w.numpy(), ids.numpy())

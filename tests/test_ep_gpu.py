@@ -52,8 +52,8 @@ def _worker(rank, world, port, q, mode):
                                   chunks=2 if mode == "overlap" else 1)
         if mode == "replicate":
             w_, ids_ = pkg.grouped_topk(x, g, K_TOP, True, 8, 4, "sigmoid", 2.5, e_score_correction_bias=bias)
-            hot = layer.hot_experts(ids_, 5)
-            layer.replicate(hot, w1[hot], w2[hot])
+            hot = layer.rebalance(ids_, 5)  # replica weights broadcast from their owners
+            assert hot == layer.replicated
         out = layer.forward(x, g)
         ref = pkg.moe_layer(x, g, w1, w2, topk=K_TOP, renormalize=True, num_expert_group=8, topk_group=4,
                             scoring_func="sigmoid", routed_scaling_factor=2.5, e_score_correction_bias=bias)

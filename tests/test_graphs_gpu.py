@@ -1,0 +1,51 @@
+"""CUDA-graph replay of the task drop-ins: same buffers replay one graph and still follow
+their contents; other buffers take the eager path again (and re-capture)."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _task(name):
+    from test_tasks_cpu import TASKS, load_like_harness
+
+    return load_like_harness(TASKS / f"{name}.py")
+
+
+def test_fused_moe_task_replay_follows_inputs(cuda_device):
+    m = _task("fused_moe")
+    model = m.ModelNew(*m.get_init_inputs()).to(cuda_device)
+    gen = torch.Generator(device=cuda_device).manual_seed(3)
+    x = torch.randn(83, 128, generator=gen, device=cuda_device).half()
+    g = torch.randn(83, 8, generator=gen, device=cuda_device)
+    with torch.no_grad():
+        first = model(x, g).clone()          # eager, then captured
+        again = model(x, g).clone()          # replay
+        assert model._graph.replays == 1
+        assert torch.equal(first, again)
+        x.mul_(-0.5)
+        g.copy_(torch.randn(83, 8, generator=gen, device=cuda_device))
+        replayed = model(x, g).clone()       # replay on new contents
+        eager = model._forward_eager(x, g, *model._prepared_weights(x.dtype))
+        assert model._graph.replays == 2
+        assert torch.equal(replayed, eager)
+        x2 = x.clone()                        # another buffer: eager path again
+        out2 = model(x2, g)
+        assert model._graph.replays == 2
+        assert torch.equal(out2, eager)
+
+
+def test_grouped_topk_task_replay(cuda_device):
+    m = _task("grouped_topk")
+    model = m.ModelNew(8, True, 8, 4, "softmax", 1.0)
+    gen = torch.Generator(device=cuda_device).manual_seed(4)
+    h = torch.randn(83, 16, generator=gen, device=cuda_device).half()
+    g = torch.randn(83, 256, generator=gen, device=cuda_device)
+    w0, i0 = (t.clone() for t in model(h, g))
+    w1, i1 = (t.clone() for t in model(h, g))
+    assert model._graph.replays == 1
+    assert torch.equal(i0, i1) and torch.equal(w0, w1)
+    g.copy_(torch.randn(83, 256, generator=gen, device=cuda_device))
+    w2, i2 = (t.clone() for t in model(h, g))
+    we, ie = model._forward_eager(h, g)
+    assert torch.equal(i2, ie) and torch.equal(w2, we)
