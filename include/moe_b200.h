@@ -270,6 +270,23 @@ MOE_API int moe_ep_pack(int dtype, const void* hidden_states, const int32_t* top
 MOE_API int moe_ep_combine(int dtype, const void* returned_rows, const int32_t* tok_rows,
                            int64_t num_tokens, int hidden_size, int world, void* out, void* stream);
 
+/* Router GEMM fused with grouped_topk (no reference counterpart: the reference's
+ * path starts from the logits, grouped_topk/v0/grouped_topk.py:93-94).
+ *   logits_out fp32 [num_tokens, 256] = hidden_states [num_tokens, hidden_size] .
+ *   w_gate [256, hidden_size]^T (bf16 or fp16, dtype MOE_DTYPE_*, fp32 accumulation),
+ *   then the moe_grouped_topk rule on those logits into topk_weights / topk_ids.
+ * num_experts must be 256, hidden_size % 64 == 0, and when groups are masked each
+ * group must span a power-of-two number of 8-expert lanes. scratch: int32
+ * [moe_router_scratch_ints(num_tokens)] per-call counters. logits_out is written
+ * (and zeroed first when an m-block's K range is split over several CTAs). */
+MOE_API int64_t moe_router_scratch_ints(int64_t num_tokens);
+MOE_API int moe_router_grouped_topk(int dtype, const void* hidden_states, const void* w_gate, const float* bias,
+                                    int64_t num_tokens, int num_experts, int hidden_size, int topk,
+                                    int renormalize, int num_expert_group, int topk_group, int scoring_func,
+                                    int group_score_mode, float routed_scaling_factor, float* logits_out,
+                                    float* topk_weights, int32_t* topk_ids, int32_t* scratch, int* status,
+                                    void* stream);
+
 /* Expert placement by table instead of contiguous ranges: expert_map int32 [num_experts]
  * holds (rank << 16) | local_id for every expert, so a rank can keep replicas of hot
  * experts and route their pairs to itself (the map is then per rank). Otherwise the

@@ -23,8 +23,10 @@ from .ops import (  # noqa: F401
     moe_layer,
     quantize_rows_fp8,
     quantize_weights_fp8,
+    router_grouped_topk,
     softmax_topk,
 )
 
 __all__ = ["grouped_topk", "fused_moe", "fused_moe_fp8", "softmax_topk", "moe_align", "moe_layer",
-           "fused_moe_workspace_bytes", "quantize_rows_fp8", "quantize_weights_fp8", "check_device_status"]
+           "fused_moe_workspace_bytes", "quantize_rows_fp8", "quantize_weights_fp8", "check_device_status",
+           "router_grouped_topk"]

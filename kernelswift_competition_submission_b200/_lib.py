@@ -63,6 +63,9 @@ SIGNATURES = {
     "moe_ep_send_capacity": (_i64, [_i64, _i32, _i32]),
     "moe_ep_plan": (_i32, [_c_p, _i64, _i32, _i32, _i32, _c_p, _c_p, _c_p, _c_p]),
     "moe_ep_pack": (_i32, [_i32, _c_p, _c_p, _c_p, _i64, _i32, _i32, _i32, _i32, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p]),
+    "moe_router_scratch_ints": (_i64, [_i64]),
+    "moe_router_grouped_topk": (_i32, [_i32, _c_p, _c_p, _c_p, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
+                                       _f32, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p]),
     "moe_ep_plan_mapped": (_i32, [_c_p, _i64, _i32, _i32, _c_p, _i32, _c_p, _c_p, _c_p, _c_p]),
     "moe_ep_pack_mapped": (_i32, [_i32, _c_p, _c_p, _c_p, _i64, _i32, _i32, _i32, _c_p, _i32, _c_p, _c_p, _c_p, _c_p,
                                   _c_p, _c_p]),

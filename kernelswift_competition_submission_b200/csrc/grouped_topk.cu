@@ -16,6 +16,7 @@
 // group size works; the top-k is k rounds of a warp arg-max over
 // (choice, -index) carrying the unbiased score. HBM-bound at large M.
 #include "common.cuh"
+#include "routing.cuh"
 
 namespace moe {
 namespace {
@@ -178,147 +179,15 @@ grouped_topk_kernel(const float* __restrict__ gating, const float* __restrict__ 
   }
 }
 
-// Order-preserving map of a float to an unsigned key (a < b as floats <=> key(a) < key(b));
-// +0 and -0 map to one key, as they compare equal.
-__device__ __forceinline__ unsigned ordered_key(float f) {
-  const unsigned u = __float_as_uint(f + 0.0f);  // -0 + 0 = +0
-  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
-
-// Register-only variant for the common layouts: E = 32 * VPL (every lane full) and,
-// when groups are masked, groups of whole lanes (LPG = E / n_group / VPL lanes per
-// group, a power of two): a group's top-2 sum (or max) is a per-lane reduction over
-// its VPL values followed by log2(LPG) shuffle steps inside the group's lanes, with no
-// shared memory and no serial loop. Each lane then sorts its VPL candidates once
-// (value descending, index ascending, the same strict order as above) and each top-k
-// round is one warp arg-max over the lanes' current heads (two redux.sync reductions);
-// the winner pops its head.
-// The scores (weights before renormalisation) travel with the sorted candidates.
 template <int VPL, int LPG>
 __global__ void __launch_bounds__(kWarpsPerBlock * 32)
 grouped_topk_lanes_kernel(const float* __restrict__ gating, const float* __restrict__ bias, int64_t M, int topk,
                           int renormalize, int n_group, int topk_group, int scoring, int gmode, float scale,
                           float* __restrict__ out_w, int32_t* __restrict__ out_ids) {
-  constexpr int E = 32 * VPL;
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-  const int64_t tok = (int64_t)blockIdx.x * kWarpsPerBlock + warp;
+  const int64_t tok = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
   if (tok >= M) return;  // whole warp exits together
-
-  const float* row = gating + tok * (int64_t)E;
-  const int e0 = lane * VPL;
-  float x[VPL];
-#pragma unroll
-  for (int i = 0; i < VPL; i += 4) {
-    const float4 v = __ldg(reinterpret_cast<const float4*>(row + e0 + i));
-    x[i] = v.x; x[i + 1] = v.y; x[i + 2] = v.z; x[i + 3] = v.w;
-  }
-  float s[VPL];
-  if (scoring == MOE_SCORING_SOFTMAX) {
-    float m = -INFINITY;
-#pragma unroll
-    for (int i = 0; i < VPL; ++i) m = fmaxf(m, x[i]);
-    m = warp_max(m);
-    float z = 0.f;
-#pragma unroll
-    for (int i = 0; i < VPL; ++i) {
-      s[i] = expf(x[i] - m);
-      z += s[i];
-    }
-    z = warp_sum(z);
-#pragma unroll
-    for (int i = 0; i < VPL; ++i) s[i] = s[i] / z;
-  } else {
-#pragma unroll
-    for (int i = 0; i < VPL; ++i) s[i] = 1.0f / (1.0f + expf(-x[i]));
-  }
-  float c[VPL];
-  if (bias) {
-#pragma unroll
-    for (int i = 0; i < VPL; i += 4) {
-      const float4 b = __ldg(reinterpret_cast<const float4*>(bias + e0 + i));
-      c[i] = s[i] + b.x; c[i + 1] = s[i + 1] + b.y; c[i + 2] = s[i + 2] + b.z; c[i + 3] = s[i + 3] + b.w;
-    }
-  } else {
-#pragma unroll
-    for (int i = 0; i < VPL; ++i) c[i] = s[i];
-  }
-
-  if (topk_group < n_group) {
-    // group score: top-2 sum (or max) of the group's VPL * LPG values
-    float b1 = -INFINITY, b2 = -INFINITY;
-#pragma unroll
-    for (int i = 0; i < VPL; ++i) {
-      const float v = c[i];
-      b2 = fmaxf(b2, fminf(b1, v));
-      b1 = fmaxf(b1, v);
-    }
-#pragma unroll
-    for (int off = 1; off < LPG; off <<= 1) {
-      const float o1 = __shfl_xor_sync(0xffffffffu, b1, off);
-      const float o2 = __shfl_xor_sync(0xffffffffu, b2, off);
-      // the two largest of {b1, b2, o1, o2} with b1 >= b2, o1 >= o2
-      const float n1 = fmaxf(b1, o1);
-      const float n2 = fmaxf(fminf(b1, o1), fmaxf(b2, o2));
-      b1 = n1;
-      b2 = n2;
-    }
-    const float gs = (gmode == MOE_GROUP_SCORE_MAX) ? b1 : b1 + b2;
-    const int my_g = lane / LPG;
-    int rank = 0;
-    for (int h = 0; h < n_group; ++h) {
-      const float o = __shfl_sync(0xffffffffu, gs, h * LPG);
-      rank += (o > gs) || (o == gs && h < my_g);
-    }
-    if (rank >= topk_group) {
-#pragma unroll
-      for (int i = 0; i < VPL; ++i) c[i] = -INFINITY;
-    }
-  }
-
-  // sort this lane's candidates: value descending; equal values keep index order
-  int id[VPL];
-#pragma unroll
-  for (int i = 0; i < VPL; ++i) id[i] = e0 + i;
-#pragma unroll
-  for (int i = 1; i < VPL; ++i) {
-#pragma unroll
-    for (int j = i; j > 0; --j) {
-      if (c[j] > c[j - 1]) {
-        const float tc = c[j]; c[j] = c[j - 1]; c[j - 1] = tc;
-        const float ts = s[j]; s[j] = s[j - 1]; s[j - 1] = ts;
-        const int ti = id[j]; id[j] = id[j - 1]; id[j - 1] = ti;
-      }
-    }
-  }
-
-  float my_w = 0.f;
-  int my_id = 0;
-  for (int r = 0; r < topk; ++r) {
-    // warp arg-max of the heads in two reductions: the largest value (as an order-preserving
-    // integer key), then the lowest index among the lanes holding it
-    const unsigned kmax = __reduce_max_sync(0xffffffffu, ordered_key(c[0]));
-    const int bi = (int)__reduce_min_sync(0xffffffffu, ordered_key(c[0]) == kmax ? (unsigned)id[0] : 0xffffffffu);
-    const int owner = bi / VPL;
-    const float bs = __shfl_sync(0xffffffffu, s[0], owner);
-    if (lane == owner) {  // pop the head
-#pragma unroll
-      for (int i = 0; i + 1 < VPL; ++i) { c[i] = c[i + 1]; s[i] = s[i + 1]; id[i] = id[i + 1]; }
-      c[VPL - 1] = -INFINITY;
-      id[VPL - 1] = INT_MAX;
-    }
-    if (lane == r) { my_w = bs; my_id = bi; }
-  }
-
-  if (renormalize) {
-    const float tot = warp_sum(lane < topk ? my_w : 0.f);
-    my_w = my_w / tot;
-  }
-  if (scale != 1.0f) my_w *= scale;
-  if (lane < topk) {
-    out_w[tok * topk + lane] = my_w;
-    out_ids[tok * topk + lane] = my_id;
-  }
+  route_token_lanes<VPL, LPG, false>(gating + tok * (int64_t)(32 * VPL), bias, tok, topk, renormalize, n_group,
+                                     topk_group, scoring, gmode, scale, out_w, out_ids);
 }
 
 template <int VPL>

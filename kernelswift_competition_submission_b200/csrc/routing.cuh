@@ -1,0 +1,168 @@
+// Warp-per-token routing rule shared by the grouped_topk kernel and the fused
+// router kernel (router GEMM + routing). Rule of grouped_topk/v0/grouped_topk.py:91-132
+// of the reference plus the DeepSeek-V3 bias / top-2-sum extension; ordering is the
+// strict total order (value descending, index ascending), the rank rule of
+// grouped_topk/v1/grouped_topk.py:94.
+#pragma once
+
+#include "common.cuh"
+
+namespace moe {
+
+__device__ __forceinline__ bool route_better(float v1, int i1, float v2, int i2) {
+  return (v1 > v2) || (v1 == v2 && i1 < i2);
+}
+__device__ __forceinline__ float route_warp_max(float v) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+  return v;
+}
+__device__ __forceinline__ float route_warp_sum(float v) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  return v;
+}
+
+// Order-preserving map of a float to an unsigned key (a < b as floats <=> key(a) < key(b));
+// +0 and -0 map to one key, as they compare equal.
+__device__ __forceinline__ unsigned ordered_key(float f) {
+  const unsigned u = __float_as_uint(f + 0.0f);  // -0 + 0 = +0
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// Register-only variant for the common layouts: E = 32 * VPL (every lane full) and,
+// when groups are masked, groups of whole lanes (LPG = E / n_group / VPL lanes per
+// group, a power of two): a group's top-2 sum (or max) is a per-lane reduction over
+// its VPL values followed by log2(LPG) shuffle steps inside the group's lanes, with no
+// shared memory and no serial loop. Each lane then sorts its VPL candidates once
+// (value descending, index ascending, the same strict order as above) and each top-k
+// round is one warp arg-max over the lanes' current heads (two redux.sync reductions);
+// the winner pops its head.
+// The scores (weights before renormalisation) travel with the sorted candidates.
+// One token's routing by one warp (all 32 lanes): `row` holds its E = 32 * VPL
+// logits. kCoherent reads them through L2 (rows that other CTAs of the same
+// launch wrote), otherwise through the read-only path.
+template <int VPL, int LPG, bool kCoherent>
+__device__ __forceinline__ void route_token_lanes(const float* row, const float* __restrict__ bias, int64_t tok,
+                                                  int topk, int renormalize, int n_group, int topk_group,
+                                                  int scoring, int gmode, float scale, float* __restrict__ out_w,
+                                                  int32_t* __restrict__ out_ids) {
+  const int lane = threadIdx.x & 31;
+  const int e0 = lane * VPL;
+  float x[VPL];
+#pragma unroll
+  for (int i = 0; i < VPL; i += 4) {
+    const float4 v = kCoherent ? __ldcg(reinterpret_cast<const float4*>(row + e0 + i))
+                               : __ldg(reinterpret_cast<const float4*>(row + e0 + i));
+    x[i] = v.x; x[i + 1] = v.y; x[i + 2] = v.z; x[i + 3] = v.w;
+  }
+  float s[VPL];
+  if (scoring == MOE_SCORING_SOFTMAX) {
+    float m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) m = fmaxf(m, x[i]);
+    m = route_warp_max(m);
+    float z = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      s[i] = expf(x[i] - m);
+      z += s[i];
+    }
+    z = route_warp_sum(z);
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) s[i] = s[i] / z;
+  } else {
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) s[i] = 1.0f / (1.0f + expf(-x[i]));
+  }
+  float c[VPL];
+  if (bias) {
+#pragma unroll
+    for (int i = 0; i < VPL; i += 4) {
+      const float4 b = __ldg(reinterpret_cast<const float4*>(bias + e0 + i));
+      c[i] = s[i] + b.x; c[i + 1] = s[i + 1] + b.y; c[i + 2] = s[i + 2] + b.z; c[i + 3] = s[i + 3] + b.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) c[i] = s[i];
+  }
+
+  if (topk_group < n_group) {
+    // group score: top-2 sum (or max) of the group's VPL * LPG values
+    float b1 = -INFINITY, b2 = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const float v = c[i];
+      b2 = fmaxf(b2, fminf(b1, v));
+      b1 = fmaxf(b1, v);
+    }
+#pragma unroll
+    for (int off = 1; off < LPG; off <<= 1) {
+      const float o1 = __shfl_xor_sync(0xffffffffu, b1, off);
+      const float o2 = __shfl_xor_sync(0xffffffffu, b2, off);
+      // the two largest of {b1, b2, o1, o2} with b1 >= b2, o1 >= o2
+      const float n1 = fmaxf(b1, o1);
+      const float n2 = fmaxf(fminf(b1, o1), fmaxf(b2, o2));
+      b1 = n1;
+      b2 = n2;
+    }
+    const float gs = (gmode == MOE_GROUP_SCORE_MAX) ? b1 : b1 + b2;
+    const int my_g = lane / LPG;
+    int rank = 0;
+    for (int h = 0; h < n_group; ++h) {
+      const float o = __shfl_sync(0xffffffffu, gs, h * LPG);
+      rank += (o > gs) || (o == gs && h < my_g);
+    }
+    if (rank >= topk_group) {
+#pragma unroll
+      for (int i = 0; i < VPL; ++i) c[i] = -INFINITY;
+    }
+  }
+
+  // sort this lane's candidates: value descending; equal values keep index order
+  int id[VPL];
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) id[i] = e0 + i;
+#pragma unroll
+  for (int i = 1; i < VPL; ++i) {
+#pragma unroll
+    for (int j = i; j > 0; --j) {
+      if (c[j] > c[j - 1]) {
+        const float tc = c[j]; c[j] = c[j - 1]; c[j - 1] = tc;
+        const float ts = s[j]; s[j] = s[j - 1]; s[j - 1] = ts;
+        const int ti = id[j]; id[j] = id[j - 1]; id[j - 1] = ti;
+      }
+    }
+  }
+
+  float my_w = 0.f;
+  int my_id = 0;
+  for (int r = 0; r < topk; ++r) {
+    // warp arg-max of the heads in two reductions: the largest value (as an order-preserving
+    // integer key), then the lowest index among the lanes holding it
+    const unsigned kmax = __reduce_max_sync(0xffffffffu, ordered_key(c[0]));
+    const int bi = (int)__reduce_min_sync(0xffffffffu, ordered_key(c[0]) == kmax ? (unsigned)id[0] : 0xffffffffu);
+    const int owner = bi / VPL;
+    const float bs = __shfl_sync(0xffffffffu, s[0], owner);
+    if (lane == owner) {  // pop the head
+#pragma unroll
+      for (int i = 0; i + 1 < VPL; ++i) { c[i] = c[i + 1]; s[i] = s[i + 1]; id[i] = id[i + 1]; }
+      c[VPL - 1] = -INFINITY;
+      id[VPL - 1] = INT_MAX;
+    }
+    if (lane == r) { my_w = bs; my_id = bi; }
+  }
+
+  if (renormalize) {
+    const float tot = route_warp_sum(lane < topk ? my_w : 0.f);
+    my_w = my_w / tot;
+  }
+  if (scale != 1.0f) my_w *= scale;
+  if (lane < topk) {
+    out_w[tok * topk + lane] = my_w;
+    out_ids[tok * topk + lane] = my_id;
+  }
+}
+
+
+}  // namespace moe

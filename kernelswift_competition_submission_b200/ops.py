@@ -117,6 +117,63 @@ def grouped_topk(
     return w, ids
 
 
+def router_grouped_topk(
+    hidden_states: torch.Tensor,
+    w_gate: torch.Tensor,
+    topk: int,
+    renormalize: bool,
+    num_expert_group: int,
+    topk_group: int,
+    scoring_func: str = "softmax",
+    routed_scaling_factor: float = 1.0,
+    e_score_correction_bias: torch.Tensor | None = None,
+    group_score: str | None = None,
+    return_logits: bool = False,
+):
+    """Router GEMM and grouped_topk in one launch: logits = hidden_states @ w_gate.T (bf16 or
+    fp16 operands, fp32 accumulation), routed with the rule of ``grouped_topk``.
+
+    hidden_states [M, K], w_gate [256, K] in the same dtype, K a multiple of 64. Returns
+    (topk_weights fp32 [M, topk], topk_ids int32 [M, topk]) and, with ``return_logits``,
+    the fp32 logits [M, 256] as a third element.
+    """
+    if scoring_func == "softmax":
+        sf = _lib.MOE_SCORING_SOFTMAX
+    elif scoring_func == "sigmoid":
+        sf = _lib.MOE_SCORING_SIGMOID
+    else:
+        raise ValueError(f"Unsupported scoring_func: {scoring_func}")
+    if group_score is None:
+        group_score = "max" if e_score_correction_bias is None else "top2sum"
+    gm = {"max": _lib.MOE_GROUP_SCORE_MAX, "top2sum": _lib.MOE_GROUP_SCORE_TOP2_SUM}[group_score]
+    dev = _require_cuda("router_grouped_topk", hidden_states, w_gate, e_score_correction_bias)
+    dt = hidden_states.dtype
+    if dt not in _DTYPES:
+        raise TypeError(f"router_grouped_topk: dtype {dt} not supported (bf16 or fp16)")
+    if w_gate.dtype != dt:
+        raise TypeError("router_grouped_topk: w_gate must have the dtype of hidden_states")
+    M, K = hidden_states.shape
+    E = w_gate.shape[0]
+    if tuple(w_gate.shape) != (E, K):
+        raise ValueError(f"router_grouped_topk: w_gate {tuple(w_gate.shape)} must be [E, {K}]")
+    x = hidden_states.contiguous()
+    wg = w_gate.contiguous()
+    bias = None
+    if e_score_correction_bias is not None:
+        bias = e_score_correction_bias.to(torch.float32).contiguous()
+    lib = _lib.load()
+    logits = torch.empty(M, E, dtype=torch.float32, device=dev)
+    w = torch.empty(M, topk, dtype=torch.float32, device=dev)
+    ids = torch.empty(M, topk, dtype=torch.int32, device=dev)
+    scratch = torch.empty(max(1, int(lib.moe_router_scratch_ints(M))), dtype=torch.int32, device=dev)
+    _lib.check(
+        lib.moe_router_grouped_topk(_DTYPES[dt], _ptr(x), _ptr(wg), _ptr(bias), M, E, K, topk, int(bool(renormalize)),
+                                    num_expert_group, topk_group, sf, gm, float(routed_scaling_factor), _ptr(logits),
+                                    _ptr(w), _ptr(ids), _ptr(scratch), _ptr(status_word(dev)), _stream(dev)),
+        "moe_router_grouped_topk")
+    return (w, ids, logits) if return_logits else (w, ids)
+
+
 def softmax_topk(router_logits: torch.Tensor, top_k: int, renormalize: bool = True):
     """Mixtral routing (fused_moe/v0/fused_moe.py:134-139): one group, softmax, no scale."""
     return grouped_topk(None, router_logits, top_k, renormalize, 1, 1, "softmax", 1.0)

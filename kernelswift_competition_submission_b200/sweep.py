@@ -13,6 +13,8 @@ timed call, median over the calls:
                  activation quantisation, M = 1, 8, 32, 128
   tasks          the reference's task shapes through the drop-in ModelNew modules (latency per
                  call, the harness's protocol), graph replay and eager
+  router         router GEMM fused with grouped_topk, M = 1, 128, 4096, 32768, against the
+                 unfused pair (cuBLAS bf16 GEMM + grouped_topk)
 
 Each line carries the algorithmic work (FLOPs = 6 M k K N for the expert path;
 bytes = A 3 K N b_w (+ block scales) + M K b_x + M K 2 + M k 8 + M E 4 with A the
@@ -209,17 +211,37 @@ def sweep_tasks(dev, iters_unused=None):
                                                             "after 200 warm-up calls"}), flush=True)
 
 
+def sweep_router(dev, timer, peaks, iters):
+    """Router GEMM fused with grouped_topk (E = 256, K = 7168, sigmoid + bias, 8 groups / top-4,
+    k = 8) against the same two steps unfused: the bf16 GEMM by torch (cuBLAS) and the
+    grouped_topk kernel on its (fp32-cast) output."""
+    E, K, k = 256, 7168, 8
+    wg = (torch.randn(E, K, generator=torch.Generator(device=dev).manual_seed(7), device=dev) / K ** 0.5).bfloat16()
+    bias = torch.randn(E, generator=torch.Generator(device=dev).manual_seed(44), device=dev) * 0.01
+    for M in (1, 128, 4096, 32768):
+        x = torch.randn(M, K, generator=torch.Generator(device=dev).manual_seed(M), device=dev).bfloat16()
+        fused = timer.median_ms(lambda: ops.router_grouped_topk(x, wg, k, True, 8, 4, "sigmoid", 2.5,
+                                                                e_score_correction_bias=bias), iters)
+        unfused = timer.median_ms(lambda: ops.grouped_topk(x, (x @ wg.T).float(), k, True, 8, 4, "sigmoid", 2.5,
+                                                           e_score_correction_bias=bias), iters)
+        flops = 2.0 * M * K * E
+        nbytes = E * K * 2 + M * K * 2 + M * k * 8
+        _line("router_fused", M, fused, flops, nbytes, peaks, peaks["bf16_tflops"], {"unfused_ms": unfused})
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--only", nargs="*", default=None,
-                    choices=["grouped_topk", "mixtral", "dsv3_bf16", "dsv3_fp8", "tasks"])
+                    choices=["grouped_topk", "mixtral", "dsv3_bf16", "dsv3_fp8", "tasks", "router"])
     a = ap.parse_args()
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     peaks = _peaks()
     timer = _Timer(dev)
-    want = set(a.only or ["grouped_topk", "mixtral", "dsv3_bf16", "dsv3_fp8", "tasks"])
+    want = set(a.only or ["grouped_topk", "mixtral", "dsv3_bf16", "dsv3_fp8", "tasks", "router"])
+    if "router" in want:
+        sweep_router(dev, timer, peaks, a.iters)
     if "tasks" in want:
         sweep_tasks(dev)
     if "grouped_topk" in want:
