@@ -65,7 +65,8 @@ def parse():
                     help="expert-parallel: replicate the N busiest experts (from the first batch's routing) on "
                          "every rank")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--e2e-steps", type=int, default=20,
+                    help="batches streamed through HostPipeline for the end-to-end figure (fill and drain amortised)")
     return ap.parse_args()
 
 
