@@ -61,6 +61,8 @@ def parse():
                     help="expert-parallel overlap: token chunks per step (default: the layer's choice)")
     ap.add_argument("--ep-reserve-sms", type=int, default=None,
                     help="expert-parallel overlap: SMs the expert GEMMs leave to the all-to-alls")
+    ap.add_argument("--ep-transport", choices=["nccl", "p2p"], default="nccl",
+                    help="expert-parallel dispatch/combine: NCCL all-to-all, or NVLink stores into peer arenas")
     ap.add_argument("--replicate-hot", type=int, default=0,
                     help="expert-parallel: replicate the N busiest experts (from the first batch's routing) on "
                          "every rank")
@@ -313,6 +315,7 @@ def run_native(args):
         layer = ExpertParallelMoE(w1, w2, num_experts=E, topk=k, num_expert_group=DSV3["n_group"],
                                   topk_group=DSV3["topk_group"], scoring_func="sigmoid",
                                   routed_scaling_factor=DSV3["scale"], e_score_correction_bias=bias,
+                                  transport=args.ep_transport,
                                   **{k_: v_ for k_, v_ in (("chunks", args.ep_chunks),
                                                            ("reserve_sms", args.ep_reserve_sms)) if v_ is not None})
 
@@ -438,6 +441,7 @@ def run_native(args):
     }
     if world > 1:
         result["config"]["ep_overlap"] = {"chunks": layer.chunks, "reserve_sms": layer.reserve_sms}
+        result["config"]["ep_transport"] = layer.transport
         if layer.replicated:
             result["config"]["replicated_experts"] = layer.replicated
         result["ep_phases_ms_rank0"] = phases

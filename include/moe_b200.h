@@ -287,6 +287,41 @@ MOE_API int moe_router_grouped_topk(int dtype, const void* hidden_states, const 
                                     float* topk_weights, int32_t* topk_ids, int32_t* scratch, int* status,
                                     void* stream);
 
+/* Expert-parallel dispatch / combine over NVLink peer memory (no reference counterpart;
+ * decode-sized batches). Each rank allocates one arena (moe_p2p_arena_bytes, moe_p2p_alloc
+ * -> its 64-byte CUDA IPC handle), opens every other rank's handle (moe_p2p_open) and keeps
+ * the world base pointers in a device int64 array `peer_bases` (its own at index me).
+ * Per step with sequence number seq (1, 2, ...): moe_p2p_signal(which 0: ready),
+ * moe_p2p_dispatch (waits for every rank's ready, writes token rows / ids / weights into
+ * the destination ranks' arenas, then their disp flags), moe_p2p_wait(which 1) before the
+ * local expert path over the world * cap received rows (recv_x, recv_id, recv_w at
+ * moe_p2p_arena_offsets[4..6]), moe_p2p_combine_back (returns the partial rows, then back
+ * flags), moe_p2p_wait(which 2), then moe_ep_combine over back_x (offset [7]) with the
+ * tok_rows the dispatch wrote. scratch: int32 [2 * world + 1] zeroed once (dispatch),
+ * int32 [1] zeroed once (combine_back). Waits are bounded (MOE_ERR_TIMEOUT in status).
+ * offsets[9]: ready, disp, back, counts, recv_x, recv_id, recv_w, back_x, total. */
+MOE_API int64_t moe_p2p_arena_bytes(int world, int64_t cap, int hidden_size, int topk);
+MOE_API int moe_p2p_arena_offsets(int world, int64_t cap, int hidden_size, int topk, int64_t* offsets);
+MOE_API int moe_p2p_alloc(size_t bytes, void** base, void* ipc_handle);
+MOE_API int moe_p2p_open(const void* ipc_handle, void** base);
+MOE_API int moe_p2p_close(void* base);
+MOE_API int moe_p2p_free(void* base);
+MOE_API int moe_p2p_signal(const int64_t* peer_bases, int world, int me, int which, int64_t cap, int hidden_size,
+                           int topk, uint32_t seq, void* stream);
+MOE_API int moe_p2p_wait(const void* own_base, int world, int which, int64_t cap, int hidden_size, int topk,
+                         uint32_t seq, int* status, void* stream);
+MOE_API int moe_p2p_dispatch(int dtype, const void* hidden_states, const int32_t* topk_ids,
+                             const float* topk_weights, int64_t num_tokens, int hidden_size, int topk,
+                             int experts_per_rank, int world, int me, int64_t cap, const int64_t* peer_bases,
+                             const void* own_base, uint32_t seq, int32_t* scratch, int32_t* tok_rows, int* status,
+                             void* stream);
+/* copy of the received expert ids [world * cap, topk] (statistics, tests) */
+MOE_API int moe_p2p_copy_recv_ids(const void* own_base, int world, int64_t cap, int hidden_size, int topk,
+                                  int32_t* dst, void* stream);
+MOE_API int moe_p2p_combine_back(int dtype, const void* partial, int hidden_size, int topk, int world, int me,
+                                 int64_t cap, const int64_t* peer_bases, const void* own_base, uint32_t seq,
+                                 int32_t* scratch, void* stream);
+
 /* Expert placement by table instead of contiguous ranges: expert_map int32 [num_experts]
  * holds (rank << 16) | local_id for every expert, so a rank can keep replicas of hot
  * experts and route their pairs to itself (the map is then per rank). Otherwise the

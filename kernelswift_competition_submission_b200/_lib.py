@@ -66,6 +66,19 @@ SIGNATURES = {
     "moe_router_scratch_ints": (_i64, [_i64]),
     "moe_router_grouped_topk": (_i32, [_i32, _c_p, _c_p, _c_p, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
                                        _f32, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p]),
+    "moe_p2p_arena_bytes": (_i64, [_i32, _i64, _i32, _i32]),
+    "moe_p2p_arena_offsets": (_i32, [_i32, _i64, _i32, _i32, _c_p]),
+    "moe_p2p_alloc": (_i32, [ctypes.c_size_t, _c_p, _c_p]),
+    "moe_p2p_open": (_i32, [_c_p, _c_p]),
+    "moe_p2p_close": (_i32, [_c_p]),
+    "moe_p2p_free": (_i32, [_c_p]),
+    "moe_p2p_signal": (_i32, [_c_p, _i32, _i32, _i32, _i64, _i32, _i32, ctypes.c_uint32, _c_p]),
+    "moe_p2p_wait": (_i32, [_c_p, _i32, _i32, _i64, _i32, _i32, ctypes.c_uint32, _c_p, _c_p]),
+    "moe_p2p_dispatch": (_i32, [_i32, _c_p, _c_p, _c_p, _i64, _i32, _i32, _i32, _i32, _i32, _i64, _c_p, _c_p,
+                                ctypes.c_uint32, _c_p, _c_p, _c_p, _c_p]),
+    "moe_p2p_copy_recv_ids": (_i32, [_c_p, _i32, _i64, _i32, _i32, _c_p, _c_p]),
+    "moe_p2p_combine_back": (_i32, [_i32, _c_p, _i32, _i32, _i32, _i32, _i64, _c_p, _c_p, ctypes.c_uint32, _c_p,
+                                    _c_p]),
     "moe_ep_plan_mapped": (_i32, [_c_p, _i64, _i32, _i32, _c_p, _i32, _c_p, _c_p, _c_p, _c_p]),
     "moe_ep_pack_mapped": (_i32, [_i32, _c_p, _c_p, _c_p, _i64, _i32, _i32, _i32, _c_p, _i32, _c_p, _c_p, _c_p, _c_p,
                                   _c_p, _c_p]),

@@ -33,6 +33,8 @@ inject the numpy oracle to check the dispatch/combine logic on gloo ranks.
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 import torch.distributed as dist
 
@@ -78,7 +80,8 @@ class ExpertParallelMoE:
 
     def __init__(self, w1_local, w2_local, *, num_experts, topk, num_expert_group=1, topk_group=1,
                  scoring_func="softmax", routed_scaling_factor=1.0, e_score_correction_bias=None,
-                 renormalize=True, group=None, route_fn=None, expert_fn=None, chunks=None, reserve_sms=8):
+                 renormalize=True, group=None, route_fn=None, expert_fn=None, chunks=None, reserve_sms=8,
+                 transport="nccl", max_tokens=None):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -118,6 +121,13 @@ class ExpertParallelMoE:
         self.gemm_log = []  # (gemm1 ms, gemm2 ms, local pairs) per chunk, when profiling
         self._expert_map = None  # int32 [E]: (rank << 16) | local id, set by replicate()
         self.replicated = []
+        # transport "p2p": dispatch / combine by NVLink stores into the other ranks' arenas
+        # (CUDA IPC), no NCCL and no host round trip per step; for decode-sized batches
+        if transport not in ("nccl", "p2p"):
+            raise ValueError(f"transport must be 'nccl' or 'p2p', not {transport!r}")
+        self.transport = transport
+        self.max_tokens = max_tokens  # p2p arena size in tokens per rank (default: the first batch, max over ranks)
+        self._p2p = None
 
     # ------------------------------------------------------------------ hot-expert replicas
     def replicate(self, expert_ids, w1_rep, w2_rep):
@@ -214,6 +224,8 @@ class ExpertParallelMoE:
             self._marks.append((name, ev))
 
     def forward(self, x: torch.Tensor, gating: torch.Tensor, events=None) -> torch.Tensor:
+        if x.is_cuda and self.transport == "p2p":
+            return self._forward_p2p(x, gating)
         if x.is_cuda and self.chunks > 1 and self.expert_fn == self._experts_cuda:
             return self._forward_overlapped(x, gating, events)
         return self._forward_simple(x, gating, events)
@@ -446,5 +458,134 @@ class ExpertParallelMoE:
         valid = ids[ids >= 0]
         return int(valid.numel()), int(torch.unique(valid).numel())
 
+    # ------------------------------------------------------------------ NVLink peer-memory transport
+    def _p2p_setup(self, M, K, dtype, dev):
+        """Collective: every rank allocates an arena for `cap` tokens per rank (the largest
+        local batch over the ranks), exchanges CUDA IPC handles and opens the others'."""
+        from . import _lib
+
+        lib = _lib.load()
+        self._p2p_release()
+        m = torch.tensor([M], dtype=torch.int64, device=dev)
+        dist.all_reduce(m, op=dist.ReduceOp.MAX, group=self.group)
+        cap = max(1, int(m.item()))
+        nbytes = int(lib.moe_p2p_arena_bytes(self.world, cap, K, self.topk))
+        if nbytes <= 0:
+            raise ValueError("p2p transport: unsupported shape")
+        base = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(64)
+        _lib.check(lib.moe_p2p_alloc(nbytes, ctypes.cast(ctypes.pointer(base), ctypes.c_void_p), handle),
+                   "moe_p2p_alloc")
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle.raw), group=self.group)
+        bases = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                bases.append(base.value)
+            else:
+                pb = ctypes.c_void_p()
+                _lib.check(lib.moe_p2p_open(ctypes.create_string_buffer(h, 64),
+                                            ctypes.cast(ctypes.pointer(pb), ctypes.c_void_p)), "moe_p2p_open")
+                bases.append(pb.value)
+        offs = (ctypes.c_int64 * 9)()
+        _lib.check(lib.moe_p2p_arena_offsets(self.world, cap, K, self.topk, offs), "moe_p2p_arena_offsets")
+        self._p2p = {
+            "cap": cap, "K": K, "dtype": dtype, "base": base.value, "bases": bases, "offs": list(offs), "seq": 0,
+            "peer_bases": torch.tensor(bases, dtype=torch.int64, device=dev),
+            "scr_d": torch.zeros(2 * self.world + 1, dtype=torch.int32, device=dev),
+            "scr_c": torch.zeros(1, dtype=torch.int32, device=dev),
+        }
+        torch.cuda.synchronize(dev)
+        dist.barrier(group=self.group)
+
+    def _p2p_release(self):
+        if self._p2p is None:
+            return
+        from . import _lib
+
+        lib = _lib.load()
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)  # no rank still writes into an arena being unmapped
+        for r, b in enumerate(self._p2p["bases"]):
+            if r != self.rank:
+                lib.moe_p2p_close(ctypes.c_void_p(b))
+        dist.barrier(group=self.group)
+        lib.moe_p2p_free(ctypes.c_void_p(self._p2p["base"]))
+        self._p2p = None
+
+    def _forward_p2p(self, x, gating):
+        from . import _lib
+        from .ops import _DTYPES, _ptr, _stream, status_word
+
+        M, K = x.shape
+        dev = x.device
+        p = self._p2p
+        if p is None:  # collective: the first forward of every rank
+            self._p2p_setup(max(M, int(self.max_tokens or 0)), K, x.dtype, dev)
+            p = self._p2p
+        if M > p["cap"] or K != p["K"] or x.dtype != p["dtype"]:
+            raise ValueError(f"p2p transport: batch [{M}, {K}] {x.dtype} does not fit the arena "
+                             f"(max_tokens {p['cap']}, hidden {p['K']}, {p['dtype']})")
+        lib = _lib.load()
+        st = _stream(dev)
+        status = _ptr(status_word(dev))
+        dt = _DTYPES[x.dtype]
+        W, cap, k = self.world, p["cap"], self.topk
+        p["seq"] = (p["seq"] + 1) & 0xFFFFFFFF or 1
+        seq = p["seq"]
+        self._on_cuda = True
+        self._marks = []
+        self._mark("start")
+        w, ids = self.route_fn(x, gating)
+        self._mark("route")
+        xc = x.contiguous()
+        ids32 = ids.to(torch.int32).contiguous()
+        w32 = w.to(torch.float32).contiguous()
+        tok_rows = self._buf("p2p_tr", max(M, 1), W, torch.int32, dev)[: max(M, 1)]
+        pb = _ptr(p["peer_bases"])
+        base = p["base"]
+        _lib.check(lib.moe_p2p_signal(pb, W, self.rank, 0, cap, K, k, seq, st), "moe_p2p_signal")
+        _lib.check(lib.moe_p2p_dispatch(dt, _ptr(xc), _ptr(ids32), _ptr(w32), M, K, k, self.E_local, W, self.rank,
+                                        cap, pb, base, seq, _ptr(p["scr_d"]), _ptr(tok_rows), status, st),
+                   "moe_p2p_dispatch")
+        _lib.check(lib.moe_p2p_wait(base, W, 1, cap, K, k, seq, status, st), "moe_p2p_wait")
+        self._mark("dispatch")
+        if self.profile:  # received ids, for local_work() statistics
+            rids = torch.empty(W * cap, k, dtype=torch.int32, device=dev)
+            _lib.check(lib.moe_p2p_copy_recv_ids(base, W, cap, K, k, _ptr(rids), st), "moe_p2p_copy_recv_ids")
+            self._last_recv_ids = rids
+        # local experts over every received row (unused rows carry id -1)
+        R = W * cap
+        o = p["offs"]
+        E_l, N = self.w1.shape[0], self.w2.shape[2]
+        need = int(lib.moe_fused_workspace_bytes(R, E_l, k, K, N))
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = torch.empty(int(need * 1.25) + 256, dtype=torch.uint8, device=dev)
+        ws, wsn = _ptr(self._ws), self._ws.numel()
+        part = self._buf("p2p_part", R, K, x.dtype, dev)[:R]
+        rx, rid, rw = base + o[4], base + o[5], base + o[6]
+        _lib.check(lib.moe_expert_align_gather(dt, ctypes.c_void_p(rx), ctypes.c_void_p(rid), R, E_l, k, K, N, ws,
+                                               wsn, st), "moe_expert_align_gather")
+        _lib.check(lib.moe_expert_gemm1(dt, _ptr(self.w1), R, E_l, k, K, N, ws, wsn, status, 0, st),
+                   "moe_expert_gemm1")
+        _lib.check(lib.moe_expert_gemm2(dt, _ptr(self.w2), R, E_l, k, K, N, ws, wsn, status, 0, st),
+                   "moe_expert_gemm2")
+        _lib.check(lib.moe_expert_combine(dt, ctypes.c_void_p(rw), ctypes.c_void_p(rid), R, E_l, k, K, N,
+                                          _ptr(part), ws, wsn, st), "moe_expert_combine")
+        self._mark("experts")
+        _lib.check(lib.moe_p2p_combine_back(dt, _ptr(part), K, k, W, self.rank, cap, pb, base, seq,
+                                            _ptr(p["scr_c"]), st), "moe_p2p_combine_back")
+        _lib.check(lib.moe_p2p_wait(base, W, 2, cap, K, k, seq, status, st), "moe_p2p_wait")
+        self._mark("combine_back")
+        out = torch.empty(M, K, dtype=x.dtype, device=dev)
+        if M:
+            _lib.check(lib.moe_ep_combine(dt, ctypes.c_void_p(base + o[7]), _ptr(tok_rows), M, K, W, _ptr(out), st),
+                       "moe_ep_combine")
+        self._mark("reduce")
+        if self.profile and self._marks:
+            self.phase_log.append(self._marks)
+        return out
+
     def close(self):
+        self._p2p_release()
         self._ws = None

@@ -54,12 +54,33 @@ def _worker(rank, world, port, q, mode):
             w_, ids_ = pkg.grouped_topk(x, g, K_TOP, True, 8, 4, "sigmoid", 2.5, e_score_correction_bias=bias)
             hot = layer.rebalance(ids_, 5)  # replica weights broadcast from their owners
             assert hot == layer.replicated
-        out = layer.forward(x, g)
-        ref = pkg.moe_layer(x, g, w1, w2, topk=K_TOP, renormalize=True, num_expert_group=8, topk_group=4,
-                            scoring_func="sigmoid", routed_scaling_factor=2.5, e_score_correction_bias=bias)
-        torch.cuda.synchronize()
-        ok = torch.allclose(out.float(), ref.float(), atol=2e-2, rtol=2e-2)
-        err = float((out.float() - ref.float()).abs().max())
+        if mode == "p2p":
+            # three steps through the peer-memory transport, batch sizes changing per step and rank
+            # (rows a rank stops using must be cleared in the destination's arena)
+            layer = ExpertParallelMoE(w1[rank * el:(rank + 1) * el].contiguous(),
+                                      w2[rank * el:(rank + 1) * el].contiguous(), num_experts=E, topk=K_TOP,
+                                      num_expert_group=8, topk_group=4, scoring_func="sigmoid",
+                                      routed_scaling_factor=2.5, e_score_correction_bias=bias, transport="p2p",
+                                      max_tokens=400)
+            ok, err = True, 0.0
+            for mm in (m, 120 - 50 * rank, 390):
+                xs = x[:mm] if mm <= m else torch.randn(mm, HID, generator=tg, device=dev).to(torch.bfloat16)
+                gs = torch.randn(mm, E, generator=tg, device=dev)
+                out = layer.forward(xs, gs)
+                ref = pkg.moe_layer(xs, gs, w1, w2, topk=K_TOP, renormalize=True, num_expert_group=8, topk_group=4,
+                                    scoring_func="sigmoid", routed_scaling_factor=2.5, e_score_correction_bias=bias)
+                torch.cuda.synchronize()
+                pkg.check_device_status(dev)
+                ok = ok and torch.allclose(out.float(), ref.float(), atol=2e-2, rtol=2e-2)
+                err = max(err, float((out.float() - ref.float()).abs().max()))
+            layer.close()
+        else:
+            out = layer.forward(x, g)
+            ref = pkg.moe_layer(x, g, w1, w2, topk=K_TOP, renormalize=True, num_expert_group=8, topk_group=4,
+                                scoring_func="sigmoid", routed_scaling_factor=2.5, e_score_correction_bias=bias)
+            torch.cuda.synchronize()
+            ok = torch.allclose(out.float(), ref.float(), atol=2e-2, rtol=2e-2)
+            err = float((out.float() - ref.float()).abs().max())
         q.put((rank, "ok" if ok else "mismatch", err))
         dist.barrier()
         dist.destroy_process_group()
@@ -67,10 +88,11 @@ def _worker(rank, world, port, q, mode):
         q.put((rank, "error", traceback.format_exc()))
 
 
-@pytest.mark.parametrize("mode", ["plain", "overlap", "replicate"])
+@pytest.mark.parametrize("mode", ["plain", "overlap", "replicate", "p2p"])
 def test_ep_two_gpus_matches_single_gpu(cuda_device, mode):
     """plain: one all-to-all each way; overlap: 2 token chunks on a side stream;
-    replicate: the 5 busiest experts replicated on both ranks (their pairs stay home)."""
+    replicate: the 5 busiest experts replicated on both ranks (their pairs stay home);
+    p2p: dispatch and combine by NVLink stores into the peer's arena, three steps."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     world = 2
