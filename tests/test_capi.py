@@ -88,3 +88,38 @@ def test_workspace_bytes_monotone(lib):
     b = lib.moe_fused_workspace_bytes(4096, 256, 8, 7168, 2048)
     assert 0 < a < b
     assert lib.moe_fused_workspace_bytes(0, 0, 8, 7168, 2048) == 0
+
+
+def test_p2p_arena_layout(lib):
+    """The peer-memory arena layout: regions in order, 256-byte aligned, sized as documented."""
+    world, cap, K, k = 8, 4096, 7168, 8
+    offs = (ctypes.c_int64 * 9)()
+    assert lib.moe_p2p_arena_offsets(world, cap, K, k, offs) == 0
+    ready, disp, back, counts, rx, rid, rw, bx, total = list(offs)
+    assert (ready, disp, back, counts) == (0, 4 * world, 8 * world, 12 * world)
+    assert rx % 256 == 0 and rid % 256 == 0 and rw % 256 == 0 and bx % 256 == 0
+    assert rid - rx >= world * cap * K * 2 and rw - rid >= world * cap * k * 4
+    assert bx - rw >= world * cap * k * 4 and total - bx >= world * cap * K * 2
+    assert lib.moe_p2p_arena_bytes(world, cap, K, k) == total
+    # rejected shapes
+    assert lib.moe_p2p_arena_bytes(65, cap, K, k) == -1
+    assert lib.moe_p2p_arena_bytes(world, 0, K, k) == -1
+    assert lib.moe_p2p_arena_offsets(world, cap, K, 33, offs) == _lib.MOE_ERR_INVALID_ARG
+
+
+def test_router_argument_validation(lib):
+    f = lib.moe_router_grouped_topk
+    args = dict(dt=0, x=None, wg=None, b=None, M=4, E=256, K=7168, k=8, rn=1, ng=8, tg=4, sc=1, gm=1, s=2.5)
+
+    def call(**kw):
+        a = {**args, **kw}
+        return f(a["dt"], a["x"], a["wg"], a["b"], a["M"], a["E"], a["K"], a["k"], a["rn"], a["ng"], a["tg"],
+                 a["sc"], a["gm"], a["s"], None, None, None, None, None, None)
+
+    assert call(E=128) == _lib.MOE_ERR_BAD_SHAPE        # the tile is all 256 experts
+    assert call(K=7000) == _lib.MOE_ERR_BAD_SHAPE       # K in 64-wide steps
+    assert call(ng=64) == _lib.MOE_ERR_BAD_SHAPE        # 4-expert groups are not whole lanes
+    assert call(dt=2) == _lib.MOE_ERR_UNSUPPORTED       # fp32 operands
+    assert call() == _lib.MOE_ERR_INVALID_ARG           # null pointers, caught before any launch
+    assert call(M=0) == 0
+    assert lib.moe_router_scratch_ints(257) == 3
