@@ -15,6 +15,7 @@ timed call, median over the calls:
                  call, the harness's protocol), graph replay and eager
   router         router GEMM fused with grouped_topk, M = 1, 128, 4096, 32768, against the
                  unfused pair (cuBLAS bf16 GEMM + grouped_topk)
+  decode_graph   the DeepSeek-V3 bf16 layer at M = 1, 8, 64, eager and as one replayed CUDA graph
 
 Each line carries the algorithmic work (FLOPs = 6 M k K N for the expert path;
 bytes = A 3 K N b_w (+ block scales) + M K b_x + M K 2 + M k 8 + M E 4 with A the
@@ -166,6 +167,30 @@ def sweep_dsv3(dev, timer, peaks, iters, fp8: bool):
         ops.check_device_status(dev)
 
 
+def sweep_decode_graph(dev, timer, peaks, iters):
+    """DeepSeek-V3 bf16 layer (grouped_topk + fused_moe) at decode sizes, each call eager
+    (one launch per kernel, host work between) and replayed as one CUDA graph of the whole
+    layer (graphs.GraphCache on the same buffers)."""
+    from .graphs import GraphCache
+
+    E, k, K, N = 256, 8, 7168, 2048
+    w1, w2 = _weights(E, K, N, dev, seed=43_000)
+    for M in (1, 8, 64):
+        x, g, bias = _dsv3_inputs(M, dev)
+
+        def layer(xx, gg):
+            return ops.moe_layer(xx, gg, w1, w2, topk=k, renormalize=True, num_expert_group=8, topk_group=4,
+                                 scoring_func="sigmoid", routed_scaling_factor=2.5, e_score_correction_bias=bias)
+
+        eager = timer.median_ms(lambda: layer(x, g), iters)
+        cache = GraphCache(layer)
+        graph = timer.median_ms(lambda: cache(x, g), iters)
+        _, ids = ops.grouped_topk(x, g, k, True, 8, 4, "sigmoid", 2.5, e_score_correction_bias=bias)
+        nbytes, A = _layer_bytes(ids, E, K, N, M, k, 2)
+        _line("dsv3_bf16_graph", M, graph, 6.0 * M * k * K * N, nbytes, peaks, peaks["bf16_tflops"],
+              {"experts_hit": A, "eager_ms": eager, "replays": cache.replays})
+
+
 def sweep_tasks(dev, iters_unused=None):
     """The reference's own task shapes through the drop-in ModelNew modules, timed the way
     its harness times them: per call, host clock around the call and a device synchronise,
@@ -233,13 +258,17 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--only", nargs="*", default=None,
-                    choices=["grouped_topk", "mixtral", "dsv3_bf16", "dsv3_fp8", "tasks", "router"])
+                    choices=["grouped_topk", "mixtral", "dsv3_bf16", "dsv3_fp8", "tasks", "router",
+                             "decode_graph"])
     a = ap.parse_args()
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     peaks = _peaks()
     timer = _Timer(dev)
-    want = set(a.only or ["grouped_topk", "mixtral", "dsv3_bf16", "dsv3_fp8", "tasks", "router"])
+    want = set(a.only or ["grouped_topk", "mixtral", "dsv3_bf16", "dsv3_fp8", "tasks", "router", "decode_graph"])
+    if "decode_graph" in want:
+        sweep_decode_graph(dev, timer, peaks, a.iters)
+        torch.cuda.empty_cache()
     if "router" in want:
         sweep_router(dev, timer, peaks, a.iters)
     if "tasks" in want:
