@@ -57,6 +57,11 @@ extern "C" {
 #define MOE_DTYPE_BF16 0
 #define MOE_DTYPE_FP16 1
 #define MOE_DTYPE_FP32 2 /* FP8 quantiser inputs only */
+/* Packed e4m3 token row (expert-parallel FP8 payload): hidden_size e4m3 codes, then
+ * hidden_size / 128 fp32 scales (per token per 128), padded to a multiple of 16 bytes
+ * (moe_fp8_row_bytes). Accepted by moe_ep_pack*, moe_p2p_dispatch and
+ * moe_p2p_combine_experts_back. */
+#define MOE_DTYPE_E4M3_ROW 3
 
 /* Human-readable name of a status code (static string). */
 MOE_API const char* moe_status_string(int status);
@@ -226,9 +231,10 @@ MOE_API int moe_quantize_blocks_fp8(int dtype, const void* w, int64_t batch, int
  *   w2_q, w2_scale e4m3 [E, K, N]  and fp32 [E, K/128, N/128]
  *   out            bf16 [num_tokens, hidden_size]
  * The SiLU*mul output is quantised per row per 128 before the down projection.
- * e4m3 tiles stream from HBM at one byte per element and are dequantised to
- * bf16 in shared memory for the tcgen05 MMA (fp32 accumulate). Requires
- * hidden_size % 128 == 0 and intermediate_size % 128 == 0, both <= 16384.
+ * Both GEMMs run tcgen05.mma.kind::f8f6f4 on the e4m3 operands, one MMA chain per
+ * 128-wide K block, and promote each block's fp32 partial sums into the totals
+ * with its row and weight scales. Requires hidden_size % 128 == 0 and
+ * intermediate_size % 128 == 0.
  */
 MOE_API size_t moe_fused_workspace_bytes_fp8(int64_t num_tokens, int num_experts, int topk, int hidden_size,
                                              int intermediate_size);
@@ -237,6 +243,31 @@ MOE_API int moe_fused_experts_fp8(const void* hidden_states, const void* w1_q, c
                                   const int32_t* topk_ids, int64_t num_tokens, int num_experts, int topk,
                                   int hidden_size, int intermediate_size, void* out, void* workspace,
                                   size_t workspace_bytes, int* status, void* stream);
+
+/*
+ * FP8 expert path from token rows quantised elsewhere (the expert-parallel FP8
+ * payload, MOE_DTYPE_E4M3_ROW): row t is `rows + t * row_stride`, its hidden_size
+ * e4m3 codes followed by hidden_size / 128 fp32 scales. row_stride >=
+ * moe_fp8_row_bytes(hidden_size) and a multiple of 16. Same workspace as
+ * moe_fused_experts_fp8. topk_ids may hold -1 (slot skipped). With out == NULL
+ * the combine is left out and the per-slot rows stay in the workspace, for
+ * moe_p2p_combine_experts_back (dtype MOE_DTYPE_E4M3_ROW); topk_weights may then
+ * be NULL. max_ctas limits the GEMMs' persistent grids (0 = one CTA per SM).
+ *
+ *   moe_fp8_row_bytes              bytes of one packed row: hidden_size + hidden_size / 32,
+ *                                  rounded up to 16 (-1 unless hidden_size % 128 == 0)
+ *   moe_quantize_rows_fp8_packed   x [num_rows, cols] (bf16 / fp16 / fp32) -> packed rows
+ *                                  [num_rows, moe_fp8_row_bytes(cols)], the quantisation of
+ *                                  moe_quantize_rows_fp8 (padding bytes are left as they are)
+ */
+MOE_API int64_t moe_fp8_row_bytes(int hidden_size);
+MOE_API int moe_quantize_rows_fp8_packed(int dtype, const void* x, int64_t num_rows, int cols, void* rows,
+                                         void* stream);
+MOE_API int moe_fused_experts_fp8_rows(const void* rows, int64_t row_stride, const void* w1_q, const float* w1_scale,
+                                       const void* w2_q, const float* w2_scale, const float* topk_weights,
+                                       const int32_t* topk_ids, int64_t num_tokens, int num_experts, int topk,
+                                       int hidden_size, int intermediate_size, void* out, void* workspace,
+                                       size_t workspace_bytes, int max_ctas, int* status, void* stream);
 
 /*
  * Expert-parallel dispatch / combine (the reference has no multi-device code;
@@ -315,6 +346,16 @@ MOE_API int moe_p2p_dispatch(int dtype, const void* hidden_states, const int32_t
                              int experts_per_rank, int world, int me, int64_t cap, const int64_t* peer_bases,
                              const void* own_base, uint32_t seq, int32_t* scratch, int32_t* tok_rows, int* status,
                              void* stream);
+/* the expert path's top-k combine fused with moe_p2p_combine_back: after moe_expert_gemm2
+ * over the world * cap received rows, sums each valid row's slots from the fused workspace
+ * (same M = world * cap, E, topk, K, N as the stages) and stores it into its source's back_x.
+ * FP8 payloads (dispatch with MOE_DTYPE_E4M3_ROW; rows at pitch moe_fp8_row_bytes in recv_x):
+ * the expert path is moe_fused_experts_fp8_rows with out == NULL, this call then takes
+ * dtype MOE_DTYPE_E4M3_ROW and its workspace, and returns bf16 rows. */
+MOE_API int moe_p2p_combine_experts_back(int dtype, const void* workspace, int num_experts, int hidden_size,
+                                         int intermediate_size, int topk, int world, int me, int64_t cap,
+                                         const int64_t* peer_bases, const void* own_base, uint32_t seq,
+                                         int32_t* scratch, void* stream);
 /* copy of the received expert ids [world * cap, topk] (statistics, tests) */
 MOE_API int moe_p2p_copy_recv_ids(const void* own_base, int world, int64_t cap, int hidden_size, int topk,
                                   int32_t* dst, void* stream);

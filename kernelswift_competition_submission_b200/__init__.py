@@ -15,13 +15,16 @@ layer is in ``ep``.
 
 from .ops import (  # noqa: F401
     check_device_status,
+    fp8_row_bytes,
     fused_moe,
     fused_moe_fp8,
+    fused_moe_fp8_rows,
     fused_moe_workspace_bytes,
     grouped_topk,
     moe_align,
     moe_layer,
     quantize_rows_fp8,
+    quantize_rows_fp8_packed,
     quantize_weights_fp8,
     router_grouped_topk,
     softmax_topk,
@@ -29,4 +32,4 @@ from .ops import (  # noqa: F401
 
 __all__ = ["grouped_topk", "fused_moe", "fused_moe_fp8", "softmax_topk", "moe_align", "moe_layer",
            "fused_moe_workspace_bytes", "quantize_rows_fp8", "quantize_weights_fp8", "check_device_status",
-           "router_grouped_topk"]
+           "router_grouped_topk", "fp8_row_bytes", "quantize_rows_fp8_packed", "fused_moe_fp8_rows"]

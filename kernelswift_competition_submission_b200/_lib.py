@@ -32,6 +32,7 @@ MOE_GROUP_SCORE_TOP2_SUM = 1
 MOE_DTYPE_BF16 = 0
 MOE_DTYPE_FP16 = 1
 MOE_DTYPE_FP32 = 2
+MOE_DTYPE_E4M3_ROW = 3
 
 _c_p = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -60,6 +61,10 @@ SIGNATURES = {
     "moe_fused_workspace_bytes_fp8": (_sz, [_i64, _i32, _i32, _i32, _i32]),
     "moe_fused_experts_fp8": (_i32, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _i64, _i32, _i32, _i32, _i32, _c_p,
                                      _c_p, _sz, _c_p, _c_p]),
+    "moe_fp8_row_bytes": (_i64, [_i32]),
+    "moe_quantize_rows_fp8_packed": (_i32, [_i32, _c_p, _i64, _i32, _c_p, _c_p]),
+    "moe_fused_experts_fp8_rows": (_i32, [_c_p, _i64, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _i64, _i32, _i32, _i32, _i32,
+                                          _c_p, _c_p, _sz, _i32, _c_p, _c_p]),
     "moe_ep_send_capacity": (_i64, [_i64, _i32, _i32]),
     "moe_ep_plan": (_i32, [_c_p, _i64, _i32, _i32, _i32, _c_p, _c_p, _c_p, _c_p]),
     "moe_ep_pack": (_i32, [_i32, _c_p, _c_p, _c_p, _i64, _i32, _i32, _i32, _i32, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p]),
@@ -76,6 +81,8 @@ SIGNATURES = {
     "moe_p2p_wait": (_i32, [_c_p, _i32, _i32, _i64, _i32, _i32, ctypes.c_uint32, _c_p, _c_p]),
     "moe_p2p_dispatch": (_i32, [_i32, _c_p, _c_p, _c_p, _i64, _i32, _i32, _i32, _i32, _i32, _i64, _c_p, _c_p,
                                 ctypes.c_uint32, _c_p, _c_p, _c_p, _c_p]),
+    "moe_p2p_combine_experts_back": (_i32, [_i32, _c_p, _i32, _i32, _i32, _i32, _i32, _i32, _i64, _c_p, _c_p,
+                                            ctypes.c_uint32, _c_p, _c_p]),
     "moe_p2p_copy_recv_ids": (_i32, [_c_p, _i32, _i64, _i32, _i32, _c_p, _c_p]),
     "moe_p2p_combine_back": (_i32, [_i32, _c_p, _i32, _i32, _i32, _i32, _i64, _c_p, _c_p, ctypes.c_uint32, _c_p,
                                     _c_p]),

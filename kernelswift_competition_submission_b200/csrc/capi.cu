@@ -49,6 +49,8 @@ FusedLayout fused_layout(int64_t M, int E, int topk, int K, int N) {
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace
+
+size_t fused_yslots_offset(int64_t M, int E, int topk, int K, int N) { return fused_layout(M, E, topk, K, N).y_slots; }
 }  // namespace moe
 
 extern "C" const char* moe_status_string(int status) {

@@ -10,7 +10,8 @@
 //                      last CTA scans them into row offsets and also writes the
 //                      counts as int64 for the all-to-all split sizes.
 //   ep_pack_kernel     warp per token: claims one row per destination, copies
-//                      the token's hidden row there, writes the row's metadata
+//                      the token's hidden row there (bf16 / fp16, or the packed
+//                      e4m3 row: K codes then K / 128 fp32 scales), writes the row's metadata
 //                      (k expert ids in the destination's numbering, -1 for
 //                      slots it does not own, then the k weights as fp32 bits)
 //                      and records where each (token, destination) went.
@@ -174,9 +175,9 @@ int ep_plan_impl(const int32_t* topk_ids, int64_t num_tokens, int topk, ExpertPl
 int ep_pack_impl(int dtype, const void* hidden_states, const int32_t* topk_ids, const float* topk_weights,
                  int64_t num_tokens, int hidden_size, int topk, ExpertPlace pl, int world, int32_t* scratch,
                  const int32_t* offsets, void* send_x, int32_t* send_meta, int32_t* tok_rows, void* stream) {
-  if (dtype != MOE_DTYPE_BF16 && dtype != MOE_DTYPE_FP16) return MOE_ERR_UNSUPPORTED;
+  if (dtype != MOE_DTYPE_BF16 && dtype != MOE_DTYPE_FP16 && dtype != MOE_DTYPE_E4M3_ROW) return MOE_ERR_UNSUPPORTED;
   if (hidden_size <= 0) return MOE_ERR_INVALID_ARG;
-  if (hidden_size % 8 != 0) return MOE_ERR_BAD_SHAPE;
+  if (hidden_size % (dtype == MOE_DTYPE_E4M3_ROW ? 128 : 8) != 0) return MOE_ERR_BAD_SHAPE;
   if (num_tokens == 0) return MOE_OK;
   if (!hidden_states || !topk_ids || !topk_weights || !scratch || !offsets || !send_x || !send_meta || !tok_rows)
     return MOE_ERR_INVALID_ARG;
@@ -184,8 +185,9 @@ int ep_pack_impl(int dtype, const void* hidden_states, const int32_t* topk_ids, 
     return MOE_ERR_INVALID_ARG;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const unsigned blocks = (unsigned)ceil_div(num_tokens * 32, kEpThreads);
-  const int64_t row_vecs = (int64_t)hidden_size * 2 / 16;
-  if (dtype == MOE_DTYPE_BF16)
+  // a row is copied as whole 16-byte vectors: K bf16 / fp16 values, or one packed e4m3 row
+  const int64_t row_vecs = (dtype == MOE_DTYPE_E4M3_ROW ? fp8_row_bytes(hidden_size) : (int64_t)hidden_size * 2) / 16;
+  if (dtype != MOE_DTYPE_FP16)
     ep_pack_kernel<__nv_bfloat16><<<blocks, kEpThreads, 0, st>>>(
         static_cast<const uint4*>(hidden_states), topk_ids, topk_weights, num_tokens, topk, pl, world, row_vecs,
         offsets, scratch + world, static_cast<uint4*>(send_x), send_meta, tok_rows);

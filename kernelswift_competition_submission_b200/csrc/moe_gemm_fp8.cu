@@ -433,35 +433,37 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
 // Gather of whole rows into expert-sorted order: dst[r] = src[sorted_pairs[r] / topk]
 // for the rows the align stage filled (r < block_start[E] * 128, pair >= 0).
 __global__ void __launch_bounds__(256)
-gather_rows_kernel(const uint8_t* __restrict__ src, int64_t row_bytes, const int32_t* __restrict__ sorted_pairs,
-                   const int32_t* __restrict__ block_start, int E, int topk, int64_t cap, uint8_t* __restrict__ dst) {
+gather_rows_kernel(const uint8_t* __restrict__ src, int64_t src_stride, int64_t row_bytes,
+                   const int32_t* __restrict__ sorted_pairs, const int32_t* __restrict__ block_start, int E, int topk,
+                   int64_t cap, uint8_t* __restrict__ dst) {
   const int lane = threadIdx.x & 31;
   const int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   if (r >= cap || r >= (int64_t)__ldg(block_start + E) * kBlockM) return;
   const int pair = __ldg(sorted_pairs + r);
   if (pair < 0) return;
   const int64_t t = pair / topk;
-  if ((row_bytes & 15) == 0) {
-    const uint4* s = reinterpret_cast<const uint4*>(src + t * row_bytes);
+  if ((row_bytes & 15) == 0 && (src_stride & 15) == 0) {
+    const uint4* s = reinterpret_cast<const uint4*>(src + t * src_stride);
     uint4* d = reinterpret_cast<uint4*>(dst + r * row_bytes);
     for (int64_t v = lane; v < row_bytes / 16; v += 32) d[v] = __ldg(s + v);
   } else {
-    const uint32_t* s = reinterpret_cast<const uint32_t*>(src + t * row_bytes);
+    const uint32_t* s = reinterpret_cast<const uint32_t*>(src + t * src_stride);
     uint32_t* d = reinterpret_cast<uint32_t*>(dst + r * row_bytes);
     for (int64_t v = lane; v < row_bytes / 4; v += 32) d[v] = __ldg(s + v);
   }
 }
 
-// Transposed gather of per-row scales: dst[kb * cap + r] = src[(sorted_pairs[r] / topk) * KB + kb]
+// Transposed gather of per-row scales: dst[kb * cap + r] = src[(sorted_pairs[r] / topk) * src_stride + kb]
 // for the rows the align stage filled (0 for padding rows), so the 128 scales of one m-block
 // and K block are 512 contiguous bytes (one TMA box).
 __global__ void __launch_bounds__(256)
-gather_scales_t_kernel(const float* __restrict__ src, int KB, const int32_t* __restrict__ sorted_pairs,
-                       const int32_t* __restrict__ block_start, int E, int topk, int64_t cap, float* __restrict__ dst) {
+gather_scales_t_kernel(const float* __restrict__ src, int64_t src_stride, int KB,
+                       const int32_t* __restrict__ sorted_pairs, const int32_t* __restrict__ block_start, int E,
+                       int topk, int64_t cap, float* __restrict__ dst) {
   const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= cap || r >= (int64_t)__ldg(block_start + E) * kBlockM) return;
   const int pair = __ldg(sorted_pairs + r);
-  const float* s = pair >= 0 ? src + (int64_t)(pair / topk) * KB : nullptr;
+  const float* s = pair >= 0 ? src + (int64_t)(pair / topk) * src_stride : nullptr;
   for (int kb = 0; kb < KB; ++kb) dst[(int64_t)kb * cap + r] = s ? __ldg(s + kb) : 0.f;
 }
 
@@ -476,7 +478,7 @@ template <int MODE, int STAGES>
 cudaError_t launch_f8_stages(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& msa,
                              const float* b_scale, const int32_t* block_start, int E, int k_red, int n_out, int NB,
                              int64_t rows_cap, void* out, float* out_scale, const int32_t* sorted_pairs, int* status,
-                             cudaStream_t st) {
+                             int max_ctas, cudaStream_t st) {
   auto kern = moe_gemm_fp8_kernel<MODE, STAGES>;
   const int smem = F8Smem<STAGES>::bytes(E);
   cudaFuncAttributes fa;
@@ -488,7 +490,8 @@ cudaError_t launch_f8_stages(const CUtensorMap& ma, const CUtensorMap& mb, const
   err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (err != cudaSuccess) return err;
   const int64_t tiles_cap = (rows_cap / kBlockM) * NB;
-  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(num_sms(), tiles_cap));
+  const int ctas = (max_ctas > 0 && max_ctas < num_sms()) ? max_ctas : num_sms();
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(ctas, tiles_cap));
   kern<<<grid, kF8Threads, smem, st>>>(ma, mb, msa, b_scale, block_start, E, k_red, n_out, NB, out, out_scale,
                                        rows_cap, sorted_pairs, status);
   return cudaGetLastError();
@@ -497,39 +500,40 @@ cudaError_t launch_f8_stages(const CUtensorMap& ma, const CUtensorMap& mb, const
 template <int MODE>
 cudaError_t launch_f8(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& msa, const float* b_scale,
                       const int32_t* block_start, int E, int k_red, int n_out, int NB, int64_t rows_cap, void* out,
-                      float* out_scale, const int32_t* sorted_pairs, int* status, cudaStream_t st) {
+                      float* out_scale, const int32_t* sorted_pairs, int* status, int max_ctas, cudaStream_t st) {
   constexpr int kMaxSmem = 227 * 1024;
   if (F8Smem<4>::bytes(E) <= kMaxSmem)
     return launch_f8_stages<MODE, 4>(ma, mb, msa, b_scale, block_start, E, k_red, n_out, NB, rows_cap, out,
-                                     out_scale, sorted_pairs, status, st);
+                                     out_scale, sorted_pairs, status, max_ctas, st);
   if (F8Smem<3>::bytes(E) <= kMaxSmem)
     return launch_f8_stages<MODE, 3>(ma, mb, msa, b_scale, block_start, E, k_red, n_out, NB, rows_cap, out,
-                                     out_scale, sorted_pairs, status, st);
+                                     out_scale, sorted_pairs, status, max_ctas, st);
   return cudaErrorInvalidValue;
 }
 
 }  // namespace
 
-cudaError_t launch_gather_rows(const void* src, int64_t row_bytes, const int32_t* sorted_pairs,
+cudaError_t launch_gather_rows(const void* src, int64_t src_stride, int64_t row_bytes, const int32_t* sorted_pairs,
                                const int32_t* block_start, int E, int topk, int64_t cap, void* dst, cudaStream_t st) {
   if (cap == 0) return cudaSuccess;
   const unsigned blocks = (unsigned)ceil_div(cap * 32, 256);
-  gather_rows_kernel<<<blocks, 256, 0, st>>>(static_cast<const uint8_t*>(src), row_bytes, sorted_pairs, block_start,
-                                             E, topk, cap, static_cast<uint8_t*>(dst));
+  gather_rows_kernel<<<blocks, 256, 0, st>>>(static_cast<const uint8_t*>(src), src_stride, row_bytes, sorted_pairs,
+                                             block_start, E, topk, cap, static_cast<uint8_t*>(dst));
   return cudaGetLastError();
 }
 
-cudaError_t launch_gather_scales_t(const float* src, int KB, const int32_t* sorted_pairs, const int32_t* block_start,
-                                   int E, int topk, int64_t cap, float* dst, cudaStream_t st) {
+cudaError_t launch_gather_scales_t(const float* src, int64_t src_stride, int KB, const int32_t* sorted_pairs,
+                                   const int32_t* block_start, int E, int topk, int64_t cap, float* dst,
+                                   cudaStream_t st) {
   if (cap == 0) return cudaSuccess;
-  gather_scales_t_kernel<<<(unsigned)ceil_div(cap, 256), 256, 0, st>>>(src, KB, sorted_pairs, block_start, E, topk,
-                                                                       cap, dst);
+  gather_scales_t_kernel<<<(unsigned)ceil_div(cap, 256), 256, 0, st>>>(src, src_stride, KB, sorted_pairs, block_start,
+                                                                       E, topk, cap, dst);
   return cudaGetLastError();
 }
 
 cudaError_t launch_fp8_gemm1(const void* xq_sorted, const float* xs_sorted_t, int64_t rows_cap, const void* w1q,
                              const float* w1s, int E, int K, int N, const int32_t* block_start, void* actq,
-                             float* acts_t, int* status, cudaStream_t st) {
+                             float* acts_t, int* status, int max_ctas, cudaStream_t st) {
   CUtensorMap ma, mbm, msa;
   const uint64_t a_dims[2] = {(uint64_t)K, (uint64_t)rows_cap};
   const uint64_t a_str[1] = {(uint64_t)K};
@@ -539,12 +543,12 @@ cudaError_t launch_fp8_gemm1(const void* xq_sorted, const float* xs_sorted_t, in
   if (!make_fp8_map(&mbm, w1q, 3, b_dims, b_str, 64)) return cudaErrorInvalidValue;
   if (!make_scale_map(&msa, xs_sorted_t, rows_cap, K / 128)) return cudaErrorInvalidValue;
   return launch_f8<F8_GEMM1>(ma, mbm, msa, w1s, block_start, E, K, N, N / 128, rows_cap, actq, acts_t, nullptr,
-                             status, st);
+                             status, max_ctas, st);
 }
 
 cudaError_t launch_fp8_gemm2(const void* actq, const float* acts_t, int64_t rows_cap, const void* w2q,
                              const float* w2s, int E, int K, int N, const int32_t* block_start,
-                             const int32_t* sorted_pairs, void* y_slots, int* status, cudaStream_t st) {
+                             const int32_t* sorted_pairs, void* y_slots, int* status, int max_ctas, cudaStream_t st) {
   CUtensorMap ma, mbm, msa;
   const uint64_t a_dims[2] = {(uint64_t)N, (uint64_t)rows_cap};
   const uint64_t a_str[1] = {(uint64_t)N};
@@ -554,7 +558,7 @@ cudaError_t launch_fp8_gemm2(const void* actq, const float* acts_t, int64_t rows
   if (!make_fp8_map(&mbm, w2q, 3, b_dims, b_str, kF8BN)) return cudaErrorInvalidValue;
   if (!make_scale_map(&msa, acts_t, rows_cap, N / 128)) return cudaErrorInvalidValue;
   return launch_f8<F8_GEMM2>(ma, mbm, msa, w2s, block_start, E, N, K, (int)ceil_div(K, kF8BN), rows_cap, y_slots,
-                             nullptr, sorted_pairs, status, st);
+                             nullptr, sorted_pairs, status, max_ctas, st);
 }
 
 }  // namespace moe

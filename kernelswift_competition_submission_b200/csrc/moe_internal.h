@@ -58,22 +58,38 @@ bool make_fp8_map(CUtensorMap* m, const void* base, int rank, const uint64_t* di
 // (SiLU*mul quantised in the epilogue); GEMM2 writes bf16 pair slots.
 bool make_f32_rows_map(CUtensorMap* m, const float* base, const uint64_t* dims, const uint64_t* strides_bytes,
                        uint32_t box_rows);
+// max_ctas: persistent grid size limit (0 = one CTA per SM).
 cudaError_t launch_fp8_gemm1(const void* xq_sorted, const float* xs_sorted_t, int64_t rows_cap, const void* w1q,
                              const float* w1s, int E, int K, int N, const int32_t* block_start, void* actq,
-                             float* acts_t, int* status, cudaStream_t st);
+                             float* acts_t, int* status, int max_ctas, cudaStream_t st);
 cudaError_t launch_fp8_gemm2(const void* actq, const float* acts_t, int64_t rows_cap, const void* w2q,
                              const float* w2s, int E, int K, int N, const int32_t* block_start,
-                             const int32_t* sorted_pairs, void* y_slots, int* status, cudaStream_t st);
-// dst[kb * cap + r] = src[(sorted_pairs[r] / topk) * KB + kb] for the rows the align stage filled.
-cudaError_t launch_gather_scales_t(const float* src, int KB, const int32_t* sorted_pairs, const int32_t* block_start,
-                                   int E, int topk, int64_t cap, float* dst, cudaStream_t st);
-// dst[r] = src[sorted_pairs[r] / topk] (row_bytes each) for the rows the align stage filled.
-cudaError_t launch_gather_rows(const void* src, int64_t row_bytes, const int32_t* sorted_pairs,
+                             const int32_t* sorted_pairs, void* y_slots, int* status, int max_ctas, cudaStream_t st);
+// dst[kb * cap + r] = src[(sorted_pairs[r] / topk) * src_stride + kb] for the rows the align
+// stage filled (src_stride in floats between token rows).
+cudaError_t launch_gather_scales_t(const float* src, int64_t src_stride, int KB, const int32_t* sorted_pairs,
+                                   const int32_t* block_start, int E, int topk, int64_t cap, float* dst,
+                                   cudaStream_t st);
+// dst[r] = row_bytes bytes of src at token row sorted_pairs[r] / topk (src_stride bytes apart),
+// for the rows the align stage filled; dst rows are row_bytes apart.
+cudaError_t launch_gather_rows(const void* src, int64_t src_stride, int64_t row_bytes, const int32_t* sorted_pairs,
                                const int32_t* block_start, int E, int topk, int64_t cap, void* dst, cudaStream_t st);
 
-// Per row, per 128 columns e4m3 quantisation (dtype bf16 / fp16 / fp32 input).
-cudaError_t launch_quantize_rows(int dtype, const void* x, int64_t M, int K, uint8_t* q, float* s, cudaStream_t st);
+// Per row, per 128 columns e4m3 quantisation (dtype bf16 / fp16 / fp32 input): row m's codes
+// at q + m * ldq (bytes), its K / 128 scales at s + m * lds (floats).
+cudaError_t launch_quantize_rows(int dtype, const void* x, int64_t M, int K, uint8_t* q, int64_t ldq, float* s,
+                                 int64_t lds, cudaStream_t st);
+
+// Packed e4m3 token row (MOE_DTYPE_E4M3_ROW): K codes, then K / 128 fp32 scales, padded to
+// a multiple of 16 bytes.
+inline int64_t fp8_row_bytes(int K) { return (int64_t)K + ((int64_t)K / 32 + 15) / 16 * 16; }
+
+// Byte offset of the bf16 y slot rows ([M * topk, K]) in the FP8 expert workspace.
+size_t fp8_yslots_offset(int64_t M, int E, int topk, int K, int N);
 
 int num_sms();
+
+// Byte offset of the y_slots region ([M * topk, K] slot rows) in the fused workspace.
+size_t fused_yslots_offset(int64_t M, int E, int topk, int K, int N);
 
 }  // namespace moe

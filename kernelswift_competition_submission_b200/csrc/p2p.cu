@@ -4,7 +4,8 @@
 // through CUDA IPC handles):
 //
 //   ctrl    ready[world] | disp[world] | back[world] | counts[world]   (u32 / int32)
-//   recv_x  [world][cap][K]       token rows sent to this rank, region = source rank
+//   recv_x  [world][cap][K]       token rows sent to this rank, region = source rank (bf16 /
+//                                 fp16, or packed e4m3 rows at their own smaller pitch)
 //   recv_id [world][cap][k]       expert ids in this rank's numbering (-1: not this rank's)
 //   recv_w  [world][cap][k]       the token's top-k weights
 //   back_x  [world][cap][K]       partial rows returned to this rank, region = expert rank
@@ -95,10 +96,9 @@ __global__ void p2p_wait_kernel(const uint32_t* flags, int world, uint32_t seq, 
 }
 
 // scratch: [world] rows claimed this step | [world] rows used last step | [1] CTAs done
-template <typename T>
 __global__ void __launch_bounds__(kP2PThreads)
 p2p_dispatch_kernel(const uint4* __restrict__ x, const int32_t* __restrict__ ids, const float* __restrict__ w,
-                    int64_t M, int K, int topk, int epr, int world, int me, int64_t cap,
+                    int64_t M, int64_t row_vecs, int topk, int epr, int world, int me, int64_t cap,
                     const int64_t* __restrict__ peer_base, P2PLayout lay, uint32_t seq, int32_t* scratch,
                     int32_t* __restrict__ tok_rows, const uint32_t* own_ready, int* status) {
   __shared__ int s_go, s_last;
@@ -108,7 +108,6 @@ p2p_dispatch_kernel(const uint4* __restrict__ x, const int32_t* __restrict__ ids
   if (threadIdx.x == 0) s_go = wait_flags(own_ready, world, seq, status) ? 1 : 0;
   __syncthreads();
   const int lane = threadIdx.x & 31;
-  const int64_t row_vecs = (int64_t)K * 2 / 16;
   if (s_go) {
     for (int64_t t = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; t < M;
          t += ((int64_t)gridDim.x * blockDim.x) >> 5) {
@@ -187,6 +186,59 @@ p2p_combine_back_kernel(const uint4* __restrict__ partial, int K, int world, int
                  ((int64_t)me * cap + r) * row_vecs;
     const uint4* s = partial + row * row_vecs;
     for (int64_t v = lane; v < row_vecs; v += 32) dst[v] = __ldg(s + v);
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = (atomicAdd(done, 1) == (int)gridDim.x - 1);
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence_system();
+  if (threadIdx.x < world)
+    st_release_sys(reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(peer_base[threadIdx.x]) + lay.back) + me,
+                   seq);
+  if (threadIdx.x == 0) *done = 0;
+}
+
+// The expert path's top-k combine fused with the return trip: for received row t
+// (region src = t / cap, row r = t % cap, r < counts[src]) the weighted sum of its k slot
+// rows of y_slots is stored straight into rank src's back_x region `me`, row r. One thread
+// per 16-byte vector of a row; the last CTA raises back[me] in every rank.
+template <typename T>
+__global__ void __launch_bounds__(kP2PThreads)
+p2p_combine_experts_back_kernel(const uint4* __restrict__ y, const float* __restrict__ w,
+                                const int32_t* __restrict__ ids, int E, int topk, int vpr, int world, int me,
+                                int64_t cap, const int64_t* __restrict__ peer_base, P2PLayout lay,
+                                const int32_t* own_counts, uint32_t seq, int32_t* done) {
+  __shared__ int s_last;
+  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t t = gid / vpr;
+  const int v = (int)(gid - t * vpr);
+  if (t < (int64_t)world * cap) {
+    const int src = (int)(t / cap);
+    const int64_t r = t - (int64_t)src * cap;
+    if (r < __ldcg(own_counts + src)) {
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int j = 0; j < topk; ++j) {
+        const int e = __ldg(ids + t * topk + j);
+        if (e < 0 || e >= E) continue;
+        const float wj = __ldg(w + t * topk + j);
+        const uint4 q = __ldg(y + (t * topk + j) * vpr + v);
+        const uint32_t u[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = ElemTraits<T>::unpack2(u[i]);
+          acc[2 * i] = fmaf(wj, f.x, acc[2 * i]);
+          acc[2 * i + 1] = fmaf(wj, f.y, acc[2 * i + 1]);
+        }
+      }
+      uint4 o;
+      o.x = ElemTraits<T>::pack2(acc[0], acc[1]);
+      o.y = ElemTraits<T>::pack2(acc[2], acc[3]);
+      o.z = ElemTraits<T>::pack2(acc[4], acc[5]);
+      o.w = ElemTraits<T>::pack2(acc[6], acc[7]);
+      uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<char*>(peer_base[src]) + lay.back_x);
+      dst[((int64_t)me * cap + r) * vpr + v] = o;
+    }
   }
   __threadfence_system();
   __syncthreads();
@@ -282,9 +334,10 @@ extern "C" int moe_p2p_dispatch(int dtype, const void* hidden_states, const int3
                                 const void* own_base, uint32_t seq, int32_t* scratch, int32_t* tok_rows, int* status,
                                 void* stream) {
   using namespace moe;
-  if (dtype != MOE_DTYPE_BF16 && dtype != MOE_DTYPE_FP16) return MOE_ERR_UNSUPPORTED;
+  if (dtype != MOE_DTYPE_BF16 && dtype != MOE_DTYPE_FP16 && dtype != MOE_DTYPE_E4M3_ROW) return MOE_ERR_UNSUPPORTED;
   if (!p2p_ok(world, me, cap, hidden_size, topk) || experts_per_rank <= 0 || num_tokens < 0 || num_tokens > cap)
     return MOE_ERR_INVALID_ARG;
+  if (dtype == MOE_DTYPE_E4M3_ROW && hidden_size % 128 != 0) return MOE_ERR_BAD_SHAPE;
   if (!peer_bases || !own_base || !scratch || !tok_rows || (num_tokens > 0 && (!hidden_states || !topk_ids ||
                                                                               !topk_weights)))
     return MOE_ERR_INVALID_ARG;
@@ -293,14 +346,12 @@ extern "C" int moe_p2p_dispatch(int dtype, const void* hidden_states, const int3
   const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div(num_tokens * 32, kP2PThreads), 2 * num_sms()));
   const uint32_t* own_ready = reinterpret_cast<const uint32_t*>(static_cast<const char*>(own_base) + l.ready);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (dtype == MOE_DTYPE_BF16)
-    p2p_dispatch_kernel<__nv_bfloat16><<<blocks, kP2PThreads, 0, st>>>(
-        static_cast<const uint4*>(hidden_states), topk_ids, topk_weights, num_tokens, hidden_size, topk,
-        experts_per_rank, world, me, cap, peer_bases, l, seq, scratch, tok_rows, own_ready, status);
-  else
-    p2p_dispatch_kernel<__half><<<blocks, kP2PThreads, 0, st>>>(
-        static_cast<const uint4*>(hidden_states), topk_ids, topk_weights, num_tokens, hidden_size, topk,
-        experts_per_rank, world, me, cap, peer_bases, l, seq, scratch, tok_rows, own_ready, status);
+  // 16-byte vectors per row; a packed e4m3 row (K + K / 32 bytes, rounded up) fits the
+  // K * 2 bytes a recv_x row holds, and is stored at that smaller pitch
+  const int64_t row_vecs = (dtype == MOE_DTYPE_E4M3_ROW ? fp8_row_bytes(hidden_size) : (int64_t)hidden_size * 2) / 16;
+  p2p_dispatch_kernel<<<blocks, kP2PThreads, 0, st>>>(
+      static_cast<const uint4*>(hidden_states), topk_ids, topk_weights, num_tokens, row_vecs, topk, experts_per_rank,
+      world, me, cap, peer_bases, l, seq, scratch, tok_rows, own_ready, status);
   return cudaGetLastError() == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
 }
 
@@ -330,4 +381,36 @@ extern "C" int moe_p2p_copy_recv_ids(const void* own_base, int world, int64_t ca
                          cudaMemcpyDeviceToDevice, static_cast<cudaStream_t>(stream)) == cudaSuccess
              ? MOE_OK
              : MOE_ERR_CUDA;
+}
+
+extern "C" int moe_p2p_combine_experts_back(int dtype, const void* workspace, int num_experts, int hidden_size,
+                                            int intermediate_size, int topk, int world, int me, int64_t cap,
+                                            const int64_t* peer_bases, const void* own_base, uint32_t seq,
+                                            int32_t* scratch, void* stream) {
+  using namespace moe;
+  if (dtype != MOE_DTYPE_BF16 && dtype != MOE_DTYPE_FP16 && dtype != MOE_DTYPE_E4M3_ROW) return MOE_ERR_UNSUPPORTED;
+  if (!p2p_ok(world, me, cap, hidden_size, topk) || num_experts <= 0 || intermediate_size <= 0 || !workspace ||
+      !peer_bases || !own_base || !scratch)
+    return MOE_ERR_INVALID_ARG;
+  const P2PLayout l = p2p_layout(world, cap, hidden_size, topk);
+  const int64_t R = (int64_t)world * cap;
+  // the slot rows the expert path left in its workspace (bf16 for the FP8 path)
+  const size_t y_off = dtype == MOE_DTYPE_E4M3_ROW
+                           ? fp8_yslots_offset(R, num_experts, topk, hidden_size, intermediate_size)
+                           : fused_yslots_offset(R, num_experts, topk, hidden_size, intermediate_size);
+  const uint4* y = reinterpret_cast<const uint4*>(static_cast<const char*>(workspace) + y_off);
+  const char* ob = static_cast<const char*>(own_base);
+  const int vpr = hidden_size / 8;
+  const unsigned blocks = (unsigned)ceil_div(R * vpr, kP2PThreads);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const float* w = reinterpret_cast<const float*>(ob + l.recv_w);
+  const int32_t* ids = reinterpret_cast<const int32_t*>(ob + l.recv_id);
+  const int32_t* cnt = reinterpret_cast<const int32_t*>(ob + l.counts);
+  if (dtype != MOE_DTYPE_FP16)
+    p2p_combine_experts_back_kernel<__nv_bfloat16><<<blocks, kP2PThreads, 0, st>>>(
+        y, w, ids, num_experts, topk, vpr, world, me, cap, peer_bases, l, cnt, seq, scratch);
+  else
+    p2p_combine_experts_back_kernel<__half><<<blocks, kP2PThreads, 0, st>>>(
+        y, w, ids, num_experts, topk, vpr, world, me, cap, peer_bases, l, cnt, seq, scratch);
+  return cudaGetLastError() == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
 }

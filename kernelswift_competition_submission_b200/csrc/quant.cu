@@ -24,7 +24,8 @@ __device__ __forceinline__ float scale_of(float amax) { return amax > 0.f ? amax
 
 template <typename T>
 __global__ void __launch_bounds__(256)
-quantize_rows_kernel(const T* __restrict__ x, int64_t M, int K, uint8_t* __restrict__ q, float* __restrict__ s) {
+quantize_rows_kernel(const T* __restrict__ x, int64_t M, int K, uint8_t* __restrict__ q, int64_t ldq,
+                     float* __restrict__ s, int64_t lds) {
   const int lane = threadIdx.x & 31;
   const int64_t wid = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int nb = K / 128;
@@ -42,8 +43,8 @@ quantize_rows_kernel(const T* __restrict__ x, int64_t M, int K, uint8_t* __restr
   uint32_t packed = 0;
 #pragma unroll
   for (int i = 0; i < 4; ++i) packed |= (uint32_t)to_e4m3(v[i] / sc) << (8 * i);
-  reinterpret_cast<uint32_t*>(q + row * K + b * 128)[lane] = packed;
-  if (lane == 0) s[row * nb + b] = sc;
+  reinterpret_cast<uint32_t*>(q + row * ldq + b * 128)[lane] = packed;
+  if (lane == 0) s[row * lds + b] = sc;
 }
 
 template <typename T>
@@ -78,15 +79,17 @@ quantize_blocks_kernel(const T* __restrict__ w, int R, int C, uint8_t* __restric
 
 }  // namespace
 
-cudaError_t launch_quantize_rows(int dtype, const void* x, int64_t M, int K, uint8_t* q, float* s, cudaStream_t st) {
+cudaError_t launch_quantize_rows(int dtype, const void* x, int64_t M, int K, uint8_t* q, int64_t ldq, float* s,
+                                 int64_t lds, cudaStream_t st) {
   if (M == 0) return cudaSuccess;
   const unsigned blocks = (unsigned)ceil_div(M * (K / 128) * 32, 256);
   if (dtype == MOE_DTYPE_BF16)
-    quantize_rows_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), M, K, q, s);
+    quantize_rows_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), M, K, q, ldq,
+                                                                s, lds);
   else if (dtype == MOE_DTYPE_FP16)
-    quantize_rows_kernel<__half><<<blocks, 256, 0, st>>>(static_cast<const __half*>(x), M, K, q, s);
+    quantize_rows_kernel<__half><<<blocks, 256, 0, st>>>(static_cast<const __half*>(x), M, K, q, ldq, s, lds);
   else
-    quantize_rows_kernel<float><<<blocks, 256, 0, st>>>(static_cast<const float*>(x), M, K, q, s);
+    quantize_rows_kernel<float><<<blocks, 256, 0, st>>>(static_cast<const float*>(x), M, K, q, ldq, s, lds);
   return cudaGetLastError();
 }
 
@@ -100,8 +103,28 @@ extern "C" int moe_quantize_rows_fp8(int dtype, const void* x, int64_t num_rows,
   if (cols % 128 != 0) return MOE_ERR_BAD_SHAPE;
   if (num_rows == 0) return MOE_OK;
   if (!x || !q || !scales || (reinterpret_cast<uintptr_t>(q) & 3u)) return MOE_ERR_INVALID_ARG;
-  const cudaError_t e =
-      launch_quantize_rows(dtype, x, num_rows, cols, static_cast<uint8_t*>(q), scales, static_cast<cudaStream_t>(stream));
+  const cudaError_t e = launch_quantize_rows(dtype, x, num_rows, cols, static_cast<uint8_t*>(q), cols, scales,
+                                            cols / 128, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
+}
+
+extern "C" int64_t moe_fp8_row_bytes(int cols) {
+  if (cols <= 0 || cols % 128 != 0) return -1;
+  return moe::fp8_row_bytes(cols);
+}
+
+extern "C" int moe_quantize_rows_fp8_packed(int dtype, const void* x, int64_t num_rows, int cols, void* rows,
+                                            void* stream) {
+  using namespace moe;
+  if (dtype != MOE_DTYPE_BF16 && dtype != MOE_DTYPE_FP16 && dtype != MOE_DTYPE_FP32) return MOE_ERR_UNSUPPORTED;
+  if (num_rows < 0 || cols <= 0) return MOE_ERR_INVALID_ARG;
+  if (cols % 128 != 0) return MOE_ERR_BAD_SHAPE;
+  if (num_rows == 0) return MOE_OK;
+  if (!x || !rows || (reinterpret_cast<uintptr_t>(rows) & 15u)) return MOE_ERR_INVALID_ARG;
+  const int64_t rb = fp8_row_bytes(cols);
+  uint8_t* r = static_cast<uint8_t*>(rows);
+  const cudaError_t e = launch_quantize_rows(dtype, x, num_rows, cols, r, rb, reinterpret_cast<float*>(r + cols),
+                                            rb / 4, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
 }
 

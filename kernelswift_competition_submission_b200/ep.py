@@ -29,6 +29,14 @@ the same collective steps in the same order, including for empty splits.
 
 ``route_fn`` / ``expert_fn`` default to this package's CUDA ops; the CPU tests
 inject the numpy oracle to check the dispatch/combine logic on gloo ranks.
+
+FP8 w8a8 (``use_fp8_w8a8=True``, e4m3 expert weights with fp32 scales per
+128 x 128 block): each rank quantises its own token rows once, per token per
+128 (``quant_fn``, default ``quantize_rows_fp8_packed``), and the dispatch moves
+the packed e4m3 rows (K codes + K / 128 fp32 scales: 7392 bytes at K = 7168
+instead of 14336 in bf16); the receiving rank runs the FP8 expert path straight
+from those rows and returns bf16 partial rows. The quantisation is per token, so
+every pair sees the same operands as in the single-GPU FP8 path.
 """
 
 from __future__ import annotations
@@ -37,6 +45,12 @@ import ctypes
 
 import torch
 import torch.distributed as dist
+
+
+def _lib_load():
+    from . import _lib
+
+    return _lib.load()
 
 
 def plan_dispatch(ids: torch.Tensor, w: torch.Tensor, experts_per_rank: int, world: int,
@@ -81,7 +95,8 @@ class ExpertParallelMoE:
     def __init__(self, w1_local, w2_local, *, num_experts, topk, num_expert_group=1, topk_group=1,
                  scoring_func="softmax", routed_scaling_factor=1.0, e_score_correction_bias=None,
                  renormalize=True, group=None, route_fn=None, expert_fn=None, chunks=None, reserve_sms=8,
-                 transport="nccl", max_tokens=None):
+                 transport="nccl", max_tokens=None, use_fp8_w8a8=False, w1_scale=None, w2_scale=None,
+                 quant_fn=None):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -91,7 +106,23 @@ class ExpertParallelMoE:
         self.E_local = num_experts // self.world
         if w1_local.shape[0] != self.E_local or w2_local.shape[0] != self.E_local:
             raise ValueError("w1_local / w2_local must hold num_experts / world experts")
+        self.fp8 = bool(use_fp8_w8a8)
+        self.w1s = self.w2s = None
+        if self.fp8:
+            from .ops import _fp8_bytes
+
+            if w1_scale is None or w2_scale is None:
+                raise ValueError("use_fp8_w8a8 needs w1_scale and w2_scale")
+            El, twoN, Kh = w1_local.shape
+            if tuple(w1_scale.shape) != (El, twoN // 128, Kh // 128) or \
+                    tuple(w2_scale.shape) != (El, Kh // 128, twoN // 2 // 128):
+                raise ValueError("use_fp8_w8a8: w1_scale / w2_scale must be [E/G, 2N/128, K/128] / [E/G, K/128, N/128]")
+            w1_local, w2_local = _fp8_bytes(w1_local.contiguous()), _fp8_bytes(w2_local.contiguous())
+            self.w1s = w1_scale.to(torch.float32).contiguous()
+            self.w2s = w2_scale.to(torch.float32).contiguous()
         self.w1, self.w2 = w1_local, w2_local
+        self.hidden = w2_local.shape[1]
+        self.quant_fn = quant_fn or self._quant_cuda
         self.topk = topk
         self.route_kw = dict(topk=topk, renormalize=renormalize, num_expert_group=num_expert_group,
                              topk_group=topk_group, scoring_func=scoring_func,
@@ -100,7 +131,8 @@ class ExpertParallelMoE:
         self.route_fn = route_fn or self._route_cuda
         self.expert_fn = expert_fn or self._experts_cuda
         # routing, EP count, EP pack, align count, align scatter, GEMM1, GEMM2, combine, EP combine
-        self.kernel_launches_per_step = 9
+        # (FP8: + row quantisation, row gather, scale gather)
+        self.kernel_launches_per_step = 12 if self.fp8 else 9
         self._ws = None
         # per-phase CUDA events of each forward when `profile` is set (bench breakdown)
         self.profile = False
@@ -130,9 +162,10 @@ class ExpertParallelMoE:
         self._p2p = None
 
     # ------------------------------------------------------------------ hot-expert replicas
-    def replicate(self, expert_ids, w1_rep, w2_rep):
+    def replicate(self, expert_ids, w1_rep, w2_rep, w1s_rep=None, w2s_rep=None):
         """Keep replicas of ``expert_ids`` (weights w1_rep [R, 2N, K], w2_rep [R, K, N], the
-        same on every rank) on this rank and compute their pairs where the token lives.
+        same on every rank; with FP8 weights also their block scales w1s_rep, w2s_rep) on this
+        rank and compute their pairs where the token lives.
 
         Every rank must call it with the same ids. Pairs routed to a replicated expert then
         never cross the network and spread over all ranks with the tokens, instead of all
@@ -148,6 +181,15 @@ class ExpertParallelMoE:
             raise ValueError("replicate: too many local experts")
         base_w1 = self.w1[: self.E_local]
         base_w2 = self.w2[: self.E_local]
+        if self.fp8:
+            from .ops import _fp8_bytes
+
+            if w1s_rep is None or w2s_rep is None or w1s_rep.shape[0] != len(ids) or w2s_rep.shape[0] != len(ids):
+                raise ValueError("replicate: FP8 weights need one scale block per replicated expert")
+            w1_rep, w2_rep = _fp8_bytes(w1_rep), _fp8_bytes(w2_rep)
+            b1s, b2s = self.w1s[: self.E_local], self.w2s[: self.E_local]
+            self.w1s = torch.cat([b1s, w1s_rep.to(torch.float32)], dim=0).contiguous() if ids else b1s
+            self.w2s = torch.cat([b2s, w2s_rep.to(torch.float32)], dim=0).contiguous() if ids else b2s
         self.w1 = torch.cat([base_w1, w1_rep.to(base_w1.dtype)], dim=0).contiguous() if ids else base_w1
         self.w2 = torch.cat([base_w2, w2_rep.to(base_w2.dtype)], dim=0).contiguous() if ids else base_w2
         emap = [((e // self.E_local) << 16) | (e % self.E_local) for e in range(self.E)]
@@ -161,18 +203,18 @@ class ExpertParallelMoE:
         their weights broadcast from their owners (collective: every rank calls it with its
         own routing sample). Returns the replicated expert ids."""
         hot = self.hot_experts(topk_ids, n)
-        base_w1, base_w2 = self.w1[: self.E_local], self.w2[: self.E_local]
-        w1r = torch.empty((len(hot),) + tuple(base_w1.shape[1:]), dtype=base_w1.dtype, device=base_w1.device)
-        w2r = torch.empty((len(hot),) + tuple(base_w2.shape[1:]), dtype=base_w2.dtype, device=base_w2.device)
+        base = [self.w1[: self.E_local], self.w2[: self.E_local]]
+        if self.fp8:
+            base += [self.w1s[: self.E_local], self.w2s[: self.E_local]]
+        reps = [torch.empty((len(hot),) + tuple(b.shape[1:]), dtype=b.dtype, device=b.device) for b in base]
         for j, e in enumerate(hot):
             owner = e // self.E_local
-            if owner == self.rank:
-                w1r[j].copy_(base_w1[e % self.E_local])
-                w2r[j].copy_(base_w2[e % self.E_local])
             src = dist.get_global_rank(self.group, owner) if self.group is not None else owner
-            dist.broadcast(w1r[j], src=src, group=self.group)
-            dist.broadcast(w2r[j], src=src, group=self.group)
-        self.replicate(hot, w1r, w2r)
+            for b, r in zip(base, reps):
+                if owner == self.rank:
+                    r[j].copy_(b[e % self.E_local])
+                dist.broadcast(r[j], src=src, group=self.group)
+        self.replicate(hot, *reps)
         return hot
 
     def hot_experts(self, topk_ids, n):
@@ -193,6 +235,11 @@ class ExpertParallelMoE:
         return grouped_topk(x, gating, kw["topk"], kw["renormalize"], kw["num_expert_group"], kw["topk_group"],
                             kw["scoring_func"], kw["routed_scaling_factor"], kw["e_score_correction_bias"])
 
+    def _quant_cuda(self, x):
+        from .ops import quantize_rows_fp8_packed
+
+        return quantize_rows_fp8_packed(x)
+
     def _experts_cuda(self, x, w, ids, events=None, out=None, max_ctas=0):
         from .ops import fused_moe_staged, fused_moe_workspace_bytes
 
@@ -201,7 +248,18 @@ class ExpertParallelMoE:
             if events:
                 for e in events:
                     e.record()
-            return torch.empty(0, x.shape[1], dtype=x.dtype, device=x.device) if out is None else out
+            if out is not None:
+                return out
+            return torch.empty(0, self.hidden, dtype=torch.bfloat16 if self.fp8 else x.dtype, device=x.device)
+        if self.fp8:  # x: packed e4m3 rows
+            from .ops import fused_moe_fp8_rows
+
+            need = int(_lib_load().moe_fused_workspace_bytes_fp8(M, self.w1.shape[0], ids.shape[1], self.hidden,
+                                                                 self.w2.shape[2]))
+            if self._ws is None or self._ws.numel() < need:
+                self._ws = torch.empty(int(need * 1.25) + 256, dtype=torch.uint8, device=x.device)
+            return fused_moe_fp8_rows(x, self.hidden, self.w1, self.w1s, self.w2, self.w2s, w, ids, out=out,
+                                      workspace=self._ws, max_ctas=max_ctas)
         need = fused_moe_workspace_bytes(M, self.w1.shape[0], ids.shape[1], x.shape[1], self.w2.shape[2])
         if self._ws is None or self._ws.numel() < need:
             self._ws = torch.empty(int(need * 1.25) + 256, dtype=torch.uint8, device=x.device)
@@ -224,6 +282,8 @@ class ExpertParallelMoE:
             self._marks.append((name, ev))
 
     def forward(self, x: torch.Tensor, gating: torch.Tensor, events=None) -> torch.Tensor:
+        if self.fp8 and x.is_cuda and x.dtype != torch.bfloat16:
+            raise TypeError("use_fp8_w8a8: hidden states must be bf16")
         if x.is_cuda and self.transport == "p2p":
             return self._forward_p2p(x, gating)
         if x.is_cuda and self.chunks > 1 and self.expert_fn == self._experts_cuda:
@@ -237,12 +297,13 @@ class ExpertParallelMoE:
         self._mark("start")
         w, ids = self.route_fn(x, gating)
         self._mark("route")
+        payload = self.quant_fn(x) if self.fp8 else x  # the rows that travel
         if x.is_cuda:
-            send_x, send_meta, send_counts, tok_rows = self._dispatch_cuda(x, w, ids)
+            send_x, send_meta, send_counts, tok_rows = self._dispatch_cuda(payload, w, ids, hidden=K)
         else:  # CPU tensors (gloo tests): the same plan restated with torch ops
             send_tok, send_counts, send_ids, send_w = plan_dispatch(ids, w, self.E_local, self.world,
                                                                     self._expert_map)
-            send_x = x.index_select(0, send_tok)
+            send_x = payload.index_select(0, send_tok)
             send_meta = torch.cat([send_ids, send_w.view(torch.int32)], dim=1).contiguous()
         recv_counts = torch.empty_like(send_counts)
         dist.all_to_all_single(recv_counts, send_counts, group=self.group)
@@ -250,7 +311,7 @@ class ExpertParallelMoE:
         r_split = recv_counts.tolist()
         S, R = int(sum(s_split)), int(sum(r_split))
         send_x, send_meta = send_x[:S], send_meta[:S]
-        recv_x = torch.empty(R, K, dtype=x.dtype, device=x.device)
+        recv_x = torch.empty(R, payload.shape[1], dtype=payload.dtype, device=x.device)
         recv_meta = torch.empty(R, 2 * self.topk, dtype=torch.int32, device=x.device)
         self._mark("plan")
         dist.all_to_all_single(recv_x, send_x, output_split_sizes=r_split, input_split_sizes=s_split,
@@ -296,11 +357,13 @@ class ExpertParallelMoE:
         self._mark("start")
         w, ids = self.route_fn(x, gating)
         self._mark("route")
+        payload = self.quant_fn(x) if self.fp8 else x
+        P = payload.shape[1]
         bounds = [(M * c) // C for c in range(C + 1)]
         packs = []
         for c in range(C):
             t0, t1 = bounds[c], bounds[c + 1]
-            packs.append(self._dispatch_cuda(x[t0:t1], w[t0:t1], ids[t0:t1], tag=c))
+            packs.append(self._dispatch_cuda(payload[t0:t1], w[t0:t1], ids[t0:t1], tag=c, hidden=K))
         # per-chunk row counts, one exchange: send[d, c] rows of chunk c go to rank d
         send_counts = torch.stack([p[2] for p in packs], dim=1).contiguous()  # [world, C] int64
         recv_counts = torch.empty_like(send_counts)
@@ -321,7 +384,7 @@ class ExpertParallelMoE:
             for c in range(C):
                 S, R = sum(s_split[c]), sum(r_split[c])
                 send_x, send_meta = packs[c][0], packs[c][1]
-                rx = self._buf(f"rx{c}", R, K, x.dtype, dev)[:R]
+                rx = self._buf(f"rx{c}", R, P, payload.dtype, dev)[:R]
                 rm = self._buf(f"rm{c}", R, 2 * self.topk, torch.int32, dev)[:R]
                 dist.all_to_all_single(rx, send_x[:S], output_split_sizes=r_split[c], input_split_sizes=s_split[c],
                                        group=self.group)
@@ -341,7 +404,8 @@ class ExpertParallelMoE:
             rids = rm[:, : self.topk].contiguous()
             rw = rm[:, self.topk:].contiguous().view(torch.float32)
             part = self._buf(f"part{c}", R, K, x.dtype, dev)[:R]
-            evs = [torch.cuda.Event(enable_timing=True) for _ in range(5)] if self.profile else None
+            # GEMM-level events: the bf16 stages only (the FP8 path is one library call)
+            evs = [torch.cuda.Event(enable_timing=True) for _ in range(5)] if self.profile and not self.fp8 else None
             self._experts_cuda(rx, rw, rids, events=evs, out=part, max_ctas=max_ctas)
             if evs:
                 self.gemm_log_step.append((evs, rids))
@@ -379,16 +443,19 @@ class ExpertParallelMoE:
         return out
 
     # ------------------------------------------------------------------ CUDA dispatch / combine
-    def _dispatch_cuda(self, x, w, ids, tag=0):
-        """Count, scan and pack with the library's EP kernels (one host-visible output: the counts)."""
+    def _dispatch_cuda(self, x, w, ids, tag=0, hidden=None):
+        """Count, scan and pack with the library's EP kernels (one host-visible output: the counts).
+        x: bf16 / fp16 token rows, or packed e4m3 rows (uint8) of a ``hidden``-wide token."""
         from . import _lib
         from .ops import _DTYPES, _ptr, _stream
 
-        M, K = x.shape
+        M, C = x.shape
+        K = hidden or C
+        dt = _lib.MOE_DTYPE_E4M3_ROW if x.dtype == torch.uint8 else _DTYPES[x.dtype]
         lib = _lib.load()
         cap = max(1, int(lib.moe_ep_send_capacity(M, self.topk, self.world)))
         dev = x.device
-        send_x = self._buf(f"sx{tag}", cap, K, x.dtype, dev)
+        send_x = self._buf(f"sx{tag}", cap, C, x.dtype, dev)
         send_meta = self._buf(f"sm{tag}", cap, 2 * self.topk, torch.int32, dev)
         scratch = self._buf(f"scr{tag}", 2 * self.world + 1, 1, torch.int32, dev)
         offsets = self._buf(f"off{tag}", self.world + 1, 1, torch.int32, dev)
@@ -401,7 +468,7 @@ class ExpertParallelMoE:
         if self._expert_map is None:
             _lib.check(lib.moe_ep_plan(_ptr(ids32), M, self.topk, self.E_local, self.world, _ptr(scratch),
                                        _ptr(offsets), _ptr(counts), st), "moe_ep_plan")
-            _lib.check(lib.moe_ep_pack(_DTYPES[x.dtype], _ptr(xc), _ptr(ids32), _ptr(w32), M, K, self.topk,
+            _lib.check(lib.moe_ep_pack(dt, _ptr(xc), _ptr(ids32), _ptr(w32), M, K, self.topk,
                                        self.E_local, self.world, _ptr(scratch), _ptr(offsets), _ptr(send_x),
                                        _ptr(send_meta), _ptr(tok_rows), st), "moe_ep_pack")
         else:
@@ -410,7 +477,7 @@ class ExpertParallelMoE:
                 emap = self._expert_map = emap.to(dev)
             _lib.check(lib.moe_ep_plan_mapped(_ptr(ids32), M, self.topk, self.E, _ptr(emap), self.world,
                                               _ptr(scratch), _ptr(offsets), _ptr(counts), st), "moe_ep_plan_mapped")
-            _lib.check(lib.moe_ep_pack_mapped(_DTYPES[x.dtype], _ptr(xc), _ptr(ids32), _ptr(w32), M, K, self.topk,
+            _lib.check(lib.moe_ep_pack_mapped(dt, _ptr(xc), _ptr(ids32), _ptr(w32), M, K, self.topk,
                                               self.E, _ptr(emap), self.world, _ptr(scratch), _ptr(offsets),
                                               _ptr(send_x), _ptr(send_meta), _ptr(tok_rows), st),
                        "moe_ep_pack_mapped")
@@ -538,14 +605,16 @@ class ExpertParallelMoE:
         self._mark("start")
         w, ids = self.route_fn(x, gating)
         self._mark("route")
-        xc = x.contiguous()
+        # the rows that travel: the token rows, or their packed e4m3 form (FP8)
+        xc = self.quant_fn(x) if self.fp8 else x.contiguous()
+        dt_rows = _lib.MOE_DTYPE_E4M3_ROW if self.fp8 else dt
         ids32 = ids.to(torch.int32).contiguous()
         w32 = w.to(torch.float32).contiguous()
         tok_rows = self._buf("p2p_tr", max(M, 1), W, torch.int32, dev)[: max(M, 1)]
         pb = _ptr(p["peer_bases"])
         base = p["base"]
         _lib.check(lib.moe_p2p_signal(pb, W, self.rank, 0, cap, K, k, seq, st), "moe_p2p_signal")
-        _lib.check(lib.moe_p2p_dispatch(dt, _ptr(xc), _ptr(ids32), _ptr(w32), M, K, k, self.E_local, W, self.rank,
+        _lib.check(lib.moe_p2p_dispatch(dt_rows, _ptr(xc), _ptr(ids32), _ptr(w32), M, K, k, self.E_local, W, self.rank,
                                         cap, pb, base, seq, _ptr(p["scr_d"]), _ptr(tok_rows), status, st),
                    "moe_p2p_dispatch")
         _lib.check(lib.moe_p2p_wait(base, W, 1, cap, K, k, seq, status, st), "moe_p2p_wait")
@@ -558,23 +627,28 @@ class ExpertParallelMoE:
         R = W * cap
         o = p["offs"]
         E_l, N = self.w1.shape[0], self.w2.shape[2]
-        need = int(lib.moe_fused_workspace_bytes(R, E_l, k, K, N))
+        need = int(lib.moe_fused_workspace_bytes_fp8(R, E_l, k, K, N) if self.fp8 else
+                   lib.moe_fused_workspace_bytes(R, E_l, k, K, N))
         if self._ws is None or self._ws.numel() < need:
             self._ws = torch.empty(int(need * 1.25) + 256, dtype=torch.uint8, device=dev)
         ws, wsn = _ptr(self._ws), self._ws.numel()
-        part = self._buf("p2p_part", R, K, x.dtype, dev)[:R]
-        rx, rid, rw = base + o[4], base + o[5], base + o[6]
-        _lib.check(lib.moe_expert_align_gather(dt, ctypes.c_void_p(rx), ctypes.c_void_p(rid), R, E_l, k, K, N, ws,
-                                               wsn, st), "moe_expert_align_gather")
-        _lib.check(lib.moe_expert_gemm1(dt, _ptr(self.w1), R, E_l, k, K, N, ws, wsn, status, 0, st),
-                   "moe_expert_gemm1")
-        _lib.check(lib.moe_expert_gemm2(dt, _ptr(self.w2), R, E_l, k, K, N, ws, wsn, status, 0, st),
-                   "moe_expert_gemm2")
-        _lib.check(lib.moe_expert_combine(dt, ctypes.c_void_p(rw), ctypes.c_void_p(rid), R, E_l, k, K, N,
-                                          _ptr(part), ws, wsn, st), "moe_expert_combine")
+        rx, rid = base + o[4], base + o[5]
+        if self.fp8:  # GEMMs straight from the received packed rows; the slot rows stay in ws
+            _lib.check(lib.moe_fused_experts_fp8_rows(ctypes.c_void_p(rx), int(lib.moe_fp8_row_bytes(K)),
+                                                      _ptr(self.w1), _ptr(self.w1s), _ptr(self.w2), _ptr(self.w2s),
+                                                      None, ctypes.c_void_p(rid), R, E_l, k, K, N, None, ws, wsn, 0,
+                                                      status, st), "moe_fused_experts_fp8_rows")
+        else:
+            _lib.check(lib.moe_expert_align_gather(dt, ctypes.c_void_p(rx), ctypes.c_void_p(rid), R, E_l, k, K, N,
+                                                   ws, wsn, st), "moe_expert_align_gather")
+            _lib.check(lib.moe_expert_gemm1(dt, _ptr(self.w1), R, E_l, k, K, N, ws, wsn, status, 0, st),
+                       "moe_expert_gemm1")
+            _lib.check(lib.moe_expert_gemm2(dt, _ptr(self.w2), R, E_l, k, K, N, ws, wsn, status, 0, st),
+                       "moe_expert_gemm2")
         self._mark("experts")
-        _lib.check(lib.moe_p2p_combine_back(dt, _ptr(part), K, k, W, self.rank, cap, pb, base, seq,
-                                            _ptr(p["scr_c"]), st), "moe_p2p_combine_back")
+        # top-k combine of each valid received row, stored straight into its source's arena
+        _lib.check(lib.moe_p2p_combine_experts_back(dt_rows, ws, E_l, K, N, k, W, self.rank, cap, pb, base, seq,
+                                                    _ptr(p["scr_c"]), st), "moe_p2p_combine_experts_back")
         _lib.check(lib.moe_p2p_wait(base, W, 2, cap, K, k, seq, status, st), "moe_p2p_wait")
         self._mark("combine_back")
         out = torch.empty(M, K, dtype=x.dtype, device=dev)

@@ -341,6 +341,70 @@ def fused_moe_fp8(hidden_states, w1_q, w1_scale, w2_q, w2_scale, topk_weights, t
     return out
 
 
+def fp8_row_bytes(hidden_size: int) -> int:
+    """Bytes of one packed e4m3 token row: hidden_size codes, then hidden_size / 128 fp32
+    scales, padded to a multiple of 16."""
+    n = int(_lib.load().moe_fp8_row_bytes(hidden_size))
+    if n < 0:
+        raise ValueError(f"fp8_row_bytes: hidden_size {hidden_size} must be a positive multiple of 128")
+    return n
+
+
+def quantize_rows_fp8_packed(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Per token per 128 e4m3 quantisation of x [M, K] into packed rows uint8
+    [M, fp8_row_bytes(K)] (codes, then the K / 128 fp32 scales): the expert-parallel FP8 payload."""
+    dev = _require_cuda("quantize_rows_fp8_packed", x)
+    dt = {torch.bfloat16: _lib.MOE_DTYPE_BF16, torch.float16: _lib.MOE_DTYPE_FP16,
+          torch.float32: _lib.MOE_DTYPE_FP32}[x.dtype]
+    x = x.contiguous()
+    M, K = x.shape
+    rb = fp8_row_bytes(K)
+    if out is None:
+        out = torch.empty(M, rb, dtype=torch.uint8, device=dev)
+    if out.dtype != torch.uint8 or out.shape[0] < M or out.shape[1] != rb or not out.is_contiguous():
+        raise ValueError("quantize_rows_fp8_packed: out must be contiguous uint8 [M, fp8_row_bytes(K)]")
+    _lib.check(_lib.load().moe_quantize_rows_fp8_packed(dt, _ptr(x), M, K, _ptr(out), _stream(dev)),
+               "moe_quantize_rows_fp8_packed")
+    return out[:M]
+
+
+def fused_moe_fp8_rows(rows, hidden_size, w1_q, w1_scale, w2_q, w2_scale, topk_weights, topk_ids, *, out=None,
+                       workspace=None, max_ctas=0):
+    """FP8 expert path from packed e4m3 rows (``quantize_rows_fp8_packed``; rows uint8 [M, >=
+    fp8_row_bytes(K)], row pitch a multiple of 16): the result of ``fused_moe_fp8`` on the
+    tokens those rows were quantised from. Returns bf16 [M, K]."""
+    dev = _require_cuda("fused_moe_fp8_rows", rows, w1_q, w2_q, w1_scale, w2_scale, topk_weights, topk_ids)
+    K = int(hidden_size)
+    if rows.dtype != torch.uint8 or rows.dim() != 2 or rows.stride(1) != 1:
+        raise TypeError("fused_moe_fp8_rows: rows must be uint8 [M, row_bytes] with unit column stride")
+    M = rows.shape[0]
+    w1b, w2b = _fp8_bytes(w1_q.contiguous()), _fp8_bytes(w2_q.contiguous())
+    E, twoN, _ = w1b.shape
+    N = twoN // 2
+    if tuple(w2b.shape) != (E, K, N) or tuple(w1_scale.shape) != (E, twoN // 128, K // 128) or \
+            tuple(w2_scale.shape) != (E, K // 128, N // 128):
+        raise ValueError("fused_moe_fp8_rows: weight / scale shapes do not match")
+    k = topk_ids.shape[1]
+    tw = topk_weights.to(torch.float32).contiguous()
+    ti = topk_ids.to(torch.int32).contiguous()
+    s1 = w1_scale.to(torch.float32).contiguous()
+    s2 = w2_scale.to(torch.float32).contiguous()
+    if out is None:
+        out = torch.empty(M, K, dtype=torch.bfloat16, device=dev)
+    lib = _lib.load()
+    need = int(lib.moe_fused_workspace_bytes_fp8(M, E, k, K, N))
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=dev)
+    if M == 0:
+        return out
+    _lib.check(
+        lib.moe_fused_experts_fp8_rows(_ptr(rows), rows.stride(0), _ptr(w1b), _ptr(s1), _ptr(w2b), _ptr(s2), _ptr(tw),
+                                       _ptr(ti), M, E, k, K, N, _ptr(out), _ptr(workspace), workspace.numel(),
+                                       int(max_ctas), _ptr(status_word(dev)), _stream(dev)),
+        "moe_fused_experts_fp8_rows")
+    return out
+
+
 def fused_moe_staged(hidden_states, w1, w2, topk_weights, topk_ids, *, out=None, workspace=None, events=None,
                      max_ctas=0):
     """``fused_moe`` issued as its four C-ABI stages (same kernels, same order).

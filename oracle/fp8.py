@@ -78,9 +78,16 @@ def dequant_blocks(q, s):
 def moe_experts_fp8_ref(x, w1q, w1s, w2q, w2s, topk_weights, topk_ids):
     """fp32 expert path on dequantised operands; x is quantised per token per 128 here,
     and the SiLU*mul output is quantised the same way before the down projection."""
+    xq, xs = quantize_rows_128(x)
+    return moe_experts_fp8_rows_ref(xq, xs, w1q, w1s, w2q, w2s, topk_weights, topk_ids)
+
+
+def moe_experts_fp8_rows_ref(xq, xs, w1q, w1s, w2q, w2s, topk_weights, topk_ids):
+    """``moe_experts_fp8_ref`` from token rows already quantised (xq e4m3 values [M, K],
+    xs fp32 [M, K/128]): the expert-parallel FP8 payload. Slots with an id outside
+    [0, E) contribute nothing."""
     from .fused_moe import silu
 
-    xq, xs = quantize_rows_128(x)
     xd = dequant_rows(xq, xs)
     w1 = dequant_blocks(w1q, w1s)
     w2 = dequant_blocks(w2q, w2s)

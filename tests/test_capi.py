@@ -123,3 +123,34 @@ def test_router_argument_validation(lib):
     assert call() == _lib.MOE_ERR_INVALID_ARG           # null pointers, caught before any launch
     assert call(M=0) == 0
     assert lib.moe_router_scratch_ints(257) == 3
+
+
+def test_fp8_packed_row_format(lib):
+    # K e4m3 codes + K / 128 fp32 scales, padded to 16 bytes
+    assert lib.moe_fp8_row_bytes(7168) == 7168 + 224
+    assert lib.moe_fp8_row_bytes(128) == 144
+    assert lib.moe_fp8_row_bytes(512) == 528
+    assert lib.moe_fp8_row_bytes(100) == -1 and lib.moe_fp8_row_bytes(0) == -1
+    for K in range(128, 16385, 128):  # a packed row always fits a bf16 row slot of the p2p arena
+        assert lib.moe_fp8_row_bytes(K) <= 2 * K and lib.moe_fp8_row_bytes(K) % 16 == 0
+
+
+def test_fp8_rows_argument_validation(lib):
+    f = lib.moe_fused_experts_fp8_rows
+    rb = lib.moe_fp8_row_bytes(512)
+    args = lambda M, stride, K, mc=0: f(None, stride, None, None, None, None, None, None, M, 8, 2, K, 256, None, None,
+                                        0, mc, None, None)
+    assert args(4, rb - 16, 512) == _lib.MOE_ERR_INVALID_ARG     # pitch shorter than a packed row
+    assert args(4, rb + 8, 512) == _lib.MOE_ERR_INVALID_ARG      # pitch not a multiple of 16
+    assert args(4, rb, 500) == _lib.MOE_ERR_BAD_SHAPE            # K % 128 != 0
+    assert args(4, rb, 512, -1) == _lib.MOE_ERR_INVALID_ARG      # negative grid limit
+    assert args(0, rb, 512) == _lib.MOE_OK                       # no rows: nothing to do
+    assert args(4, rb, 512) == _lib.MOE_ERR_INVALID_ARG          # null pointers
+    q = lib.moe_quantize_rows_fp8_packed
+    assert q(0, None, 4, 500, None, None) == _lib.MOE_ERR_BAD_SHAPE
+    assert q(7, None, 4, 512, None, None) == _lib.MOE_ERR_UNSUPPORTED
+    assert q(0, None, 4, 512, None, None) == _lib.MOE_ERR_INVALID_ARG
+    # the EP pack and p2p dispatch take the packed rows only with K % 128 == 0
+    pack = lib.moe_ep_pack
+    assert pack(_lib.MOE_DTYPE_E4M3_ROW, None, None, None, 4, 520, 2, 4, 2, None, None, None, None, None,
+                None) == _lib.MOE_ERR_BAD_SHAPE

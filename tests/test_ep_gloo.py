@@ -215,3 +215,87 @@ def test_plan_dispatch_with_expert_map_keeps_replicas_home():
     assert counts.tolist() == [1, 3]                    # only token 1's expert 0 leaves for rank 0
     assert tok.tolist() == [1, 0, 1, 2]
     assert lids.tolist() == [[0, -1], [4, 1], [-1, 4], [4, 2]]
+
+
+# ---------------------------------------------------------------- FP8 payload (packed e4m3 rows)
+HID8, INTER8 = 256, 128
+
+
+def _pack_rows(x):
+    """Packed e4m3 rows as the library lays them out: K codes, then K / 128 fp32 scales
+    (padded to 16 bytes), from the oracle's per-token-per-128 quantisation."""
+    from oracle.fp8 import quantize_rows_128
+
+    K = x.shape[1]
+    if x.shape[0] == 0:
+        return torch.zeros(0, K + (K // 32 + 15) // 16 * 16, dtype=torch.uint8)
+    q, s = quantize_rows_128(x.numpy())
+    codes = torch.from_numpy(q).to(torch.float8_e4m3fn).view(torch.uint8)
+    scales = torch.from_numpy(np.ascontiguousarray(s)).view(torch.uint8)
+    pad = (-(codes.shape[1] + scales.shape[1])) % 16
+    return torch.cat([codes, scales, torch.zeros(x.shape[0], pad, dtype=torch.uint8)], dim=1).contiguous()
+
+
+def _unpack_rows(rows, K):
+    q = rows[:, :K].contiguous().view(torch.float8_e4m3fn).float().numpy()
+    s = rows[:, K:K + K // 32].contiguous().view(torch.float32).numpy()
+    return q, s
+
+
+def _worker_fp8(rank, world, port, q, m_per_rank):
+    """FP8 layer on gloo ranks: the packed e4m3 rows travel; each rank's expert stage reads
+    them back and runs the oracle on its own experts' slots."""
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        from datetime import timedelta
+
+        from oracle.fp8 import moe_experts_fp8_ref, moe_experts_fp8_rows_ref, quantize_blocks_128
+
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=30))
+        rng = np.random.default_rng(321)
+        w1 = rng.standard_normal((E, 2 * INTER8, HID8), dtype=np.float32) / np.sqrt(HID8)
+        w2 = rng.standard_normal((E, HID8, INTER8), dtype=np.float32) / np.sqrt(INTER8)
+        w1q, w1s = quantize_blocks_128(w1)
+        w2q, w2s = quantize_blocks_128(w2)
+        el = E // world
+        sl = slice(rank * el, (rank + 1) * el)
+
+        def as_e4m3(a):
+            return torch.from_numpy(np.ascontiguousarray(a)).to(torch.float8_e4m3fn)
+
+        def experts(rows, w, ids, events=None):
+            ids_np = ids.numpy()
+            if rows.shape[0] == 0:
+                return torch.zeros(0, HID8)
+            xq, xs = _unpack_rows(rows, HID8)
+            w_np = np.where(ids_np >= 0, w.numpy(), 0.0).astype(np.float32)
+            return torch.from_numpy(moe_experts_fp8_rows_ref(xq, xs, w1q[sl], w1s[sl], w2q[sl], w2s[sl], w_np,
+                                                             ids_np))
+
+        layer = ExpertParallelMoE(as_e4m3(w1q[sl]), as_e4m3(w2q[sl]), num_experts=E, topk=K_TOP, route_fn=_route,
+                                  expert_fn=experts, use_fp8_w8a8=True, w1_scale=torch.from_numpy(w1s[sl].copy()),
+                                  w2_scale=torch.from_numpy(w2s[sl].copy()), quant_fn=_pack_rows)
+        m = m_per_rank[rank]
+        rng_t = np.random.default_rng(2000 + rank)
+        x = rng_t.standard_normal((m, HID8), dtype=np.float32)
+        g = rng_t.standard_normal((m, E), dtype=np.float32)
+        out = layer.forward(torch.from_numpy(x), torch.from_numpy(g))
+        w, ids = _route(None, torch.from_numpy(g))
+        ref = moe_experts_fp8_ref(x, w1q, w1s, w2q, w2s, w.numpy(), ids.numpy())
+        err = float(np.abs(out.numpy() - ref).max()) if m else 0.0
+        q.put((rank, "ok", err))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        q.put((rank, "error", traceback.format_exc()))
+
+
+@pytest.mark.parametrize("world,m", [(2, [37, 50]), (4, [20, 0, 33, 8])])
+def test_ep_fp8_payload_matches_single_process(world, m):
+    """The packed e4m3 rows survive pack -> all-to-all -> expert stage unchanged: the layer
+    equals the single-process FP8 oracle on the same tokens (fp32 summation order only)."""
+    res = _run(world, m, target=_worker_fp8)
+    assert len(res) == world, res
+    for r, (status, val) in res.items():
+        assert status == "ok", val
+        assert val < 1e-4, f"rank {r} max err {val}"

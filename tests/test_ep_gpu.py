@@ -1,9 +1,14 @@
-"""GPU: the expert-parallel layer over NCCL on 2 GPUs matches the single-GPU layer.
+"""GPU: the expert-parallel layer matches the single-GPU layer.
 
-Runs only when at least two GPUs are visible (skipped on a one-GPU box). Each
-rank owns half the experts and half the tokens; the output of every rank's
-tokens is compared with the single-GPU fused path on the same tokens and
-weights (atol = rtol = 2e-2, the expert-path tolerance).
+World size 2 runs when two GPUs are visible; world size 1 (one rank, the same
+plan / pack / all-to-all / combine path over a one-rank NCCL group) runs on any
+GPU box. Each rank owns 1 / world of the experts and its own tokens; the output
+of every rank's tokens is compared with the single-GPU path on the same tokens
+and weights (bf16: ``moe_layer``; FP8: ``grouped_topk`` + ``fused_moe_fp8``).
+At world size 1 every pair and every combine runs in the same order as in the
+single-GPU path, so the result must be the same bits; at 2 the per-rank partial
+rows are rounded to bf16 before the final sum, so atol = rtol = 2e-2 (the
+expert-path tolerance).
 """
 import os
 import socket
@@ -37,6 +42,8 @@ def _worker(rank, world, port, q, mode):
         dev = torch.device("cuda", rank)
         torch.cuda.set_device(dev)
         dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev, timeout=timedelta(seconds=60))
+        fp8 = mode.startswith("fp8_")
+        how = mode[4:] if fp8 else mode
         gen = torch.Generator(device=dev).manual_seed(5)
         w1 = (torch.randn(E, 2 * INTER, HID, generator=gen, device=dev) / HID ** 0.5).to(torch.bfloat16)
         w2 = (torch.randn(E, HID, INTER, generator=gen, device=dev) / INTER ** 0.5).to(torch.bfloat16)
@@ -46,41 +53,47 @@ def _worker(rank, world, port, q, mode):
         x = torch.randn(m, HID, generator=tg, device=dev).to(torch.bfloat16)
         g = torch.randn(m, E, generator=tg, device=dev)
         el = E // world
-        layer = ExpertParallelMoE(w1[rank * el:(rank + 1) * el].contiguous(), w2[rank * el:(rank + 1) * el].contiguous(),
-                                  num_experts=E, topk=K_TOP, num_expert_group=8, topk_group=4,
-                                  scoring_func="sigmoid", routed_scaling_factor=2.5, e_score_correction_bias=bias,
-                                  chunks=2 if mode == "overlap" else 1)
-        if mode == "replicate":
-            w_, ids_ = pkg.grouped_topk(x, g, K_TOP, True, 8, 4, "sigmoid", 2.5, e_score_correction_bias=bias)
-            hot = layer.rebalance(ids_, 5)  # replica weights broadcast from their owners
-            assert hot == layer.replicated
-        if mode == "p2p":
-            # three steps through the peer-memory transport, batch sizes changing per step and rank
-            # (rows a rank stops using must be cleared in the destination's arena)
-            layer = ExpertParallelMoE(w1[rank * el:(rank + 1) * el].contiguous(),
-                                      w2[rank * el:(rank + 1) * el].contiguous(), num_experts=E, topk=K_TOP,
-                                      num_expert_group=8, topk_group=4, scoring_func="sigmoid",
-                                      routed_scaling_factor=2.5, e_score_correction_bias=bias, transport="p2p",
-                                      max_tokens=400)
-            ok, err = True, 0.0
-            for mm in (m, 120 - 50 * rank, 390):
-                xs = x[:mm] if mm <= m else torch.randn(mm, HID, generator=tg, device=dev).to(torch.bfloat16)
-                gs = torch.randn(mm, E, generator=tg, device=dev)
-                out = layer.forward(xs, gs)
-                ref = pkg.moe_layer(xs, gs, w1, w2, topk=K_TOP, renormalize=True, num_expert_group=8, topk_group=4,
-                                    scoring_func="sigmoid", routed_scaling_factor=2.5, e_score_correction_bias=bias)
-                torch.cuda.synchronize()
-                pkg.check_device_status(dev)
-                ok = ok and torch.allclose(out.float(), ref.float(), atol=2e-2, rtol=2e-2)
-                err = max(err, float((out.float() - ref.float()).abs().max()))
-            layer.close()
+        sl = slice(rank * el, (rank + 1) * el)
+        kw = dict(num_experts=E, topk=K_TOP, num_expert_group=8, topk_group=4, scoring_func="sigmoid",
+                  routed_scaling_factor=2.5, e_score_correction_bias=bias, chunks=2 if how == "overlap" else 1)
+        if how == "p2p":
+            kw.update(transport="p2p", max_tokens=400)
+        if fp8:
+            w1q, w1s = pkg.quantize_weights_fp8(w1)
+            w2q, w2s = pkg.quantize_weights_fp8(w2)
+            kw.update(use_fp8_w8a8=True, w1_scale=w1s[sl].contiguous(), w2_scale=w2s[sl].contiguous())
+            layer = ExpertParallelMoE(w1q[sl].contiguous(), w2q[sl].contiguous(), **kw)
+
+            def ref_fn(xs, gs):
+                w_, ids_ = pkg.grouped_topk(xs, gs, K_TOP, True, 8, 4, "sigmoid", 2.5, e_score_correction_bias=bias)
+                return pkg.fused_moe_fp8(xs, w1q, w1s, w2q, w2s, w_, ids_)
         else:
-            out = layer.forward(x, g)
-            ref = pkg.moe_layer(x, g, w1, w2, topk=K_TOP, renormalize=True, num_expert_group=8, topk_group=4,
-                                scoring_func="sigmoid", routed_scaling_factor=2.5, e_score_correction_bias=bias)
+            layer = ExpertParallelMoE(w1[sl].contiguous(), w2[sl].contiguous(), **kw)
+
+            def ref_fn(xs, gs):
+                return pkg.moe_layer(xs, gs, w1, w2, topk=K_TOP, renormalize=True, num_expert_group=8, topk_group=4,
+                                     scoring_func="sigmoid", routed_scaling_factor=2.5, e_score_correction_bias=bias)
+        if how == "replicate":
+            w_, ids_ = pkg.grouped_topk(x, g, K_TOP, True, 8, 4, "sigmoid", 2.5, e_score_correction_bias=bias)
+            hot = layer.rebalance(ids_, 5)  # replica weights (and FP8 scales) broadcast from their owners
+            assert hot == layer.replicated
+        # p2p: three steps, batch sizes changing per step and rank (rows a rank stops using
+        # must be cleared in the destination's arena)
+        sizes = (m, 120 - 50 * rank, 390) if how == "p2p" else (m,)
+        ok, err = True, 0.0
+        for mm in sizes:
+            xs = x[:mm] if mm <= m else torch.randn(mm, HID, generator=tg, device=dev).to(torch.bfloat16)
+            gs = g[:mm] if mm <= m else torch.randn(mm, E, generator=tg, device=dev)
+            out = layer.forward(xs, gs)
+            ref = ref_fn(xs, gs)
             torch.cuda.synchronize()
-            ok = torch.allclose(out.float(), ref.float(), atol=2e-2, rtol=2e-2)
-            err = float((out.float() - ref.float()).abs().max())
+            pkg.check_device_status(dev)
+            if world == 1:
+                ok = ok and torch.equal(out, ref)
+            else:
+                ok = ok and torch.allclose(out.float(), ref.float(), atol=2e-2, rtol=2e-2)
+            err = max(err, float((out.float() - ref.float()).abs().max()))
+        layer.close()
         q.put((rank, "ok" if ok else "mismatch", err))
         dist.barrier()
         dist.destroy_process_group()
@@ -88,14 +101,18 @@ def _worker(rank, world, port, q, mode):
         q.put((rank, "error", traceback.format_exc()))
 
 
-@pytest.mark.parametrize("mode", ["plain", "overlap", "replicate", "p2p"])
-def test_ep_two_gpus_matches_single_gpu(cuda_device, mode):
+MODES = ["plain", "overlap", "replicate", "p2p", "fp8_plain", "fp8_overlap", "fp8_replicate", "fp8_p2p"]
+
+
+@pytest.mark.parametrize("world", [1, 2])
+@pytest.mark.parametrize("mode", MODES)
+def test_ep_matches_single_gpu(cuda_device, mode, world):
     """plain: one all-to-all each way; overlap: 2 token chunks on a side stream;
-    replicate: the 5 busiest experts replicated on both ranks (their pairs stay home);
-    p2p: dispatch and combine by NVLink stores into the peer's arena, three steps."""
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
-    world = 2
+    replicate: the 5 busiest experts replicated on every rank (their pairs stay home);
+    p2p: dispatch and combine by NVLink stores into the peers' arenas, three steps;
+    fp8_*: the same with e4m3 weights, the packed e4m3 token rows as the payload."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()

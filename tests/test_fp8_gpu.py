@@ -103,3 +103,43 @@ def dsv3_fp8_weights(cuda_device):
     yield w
     del w
     torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("M,K", [(1, 128), (37, 512), (64, 7168)])
+def test_packed_rows_match_quantize_rows(cuda_device, M, K):
+    """Packed e4m3 rows (the expert-parallel FP8 payload) hold the same codes and scales as
+    quantize_rows_fp8: K code bytes, then K / 128 fp32 scales."""
+    from kernelswift_competition_submission_b200 import fp8_row_bytes, quantize_rows_fp8_packed
+
+    gen = torch.Generator().manual_seed(K + M)
+    x = (torch.randn(M, K, generator=gen) * torch.logspace(-2, 1, M)[:, None]).to(torch.bfloat16).to(cuda_device)
+    rows = quantize_rows_fp8_packed(x)
+    rb = fp8_row_bytes(K)
+    assert rows.shape == (M, rb) and rb % 16 == 0 and rb >= K + K // 32
+    q, s = quantize_rows_fp8(x)
+    assert torch.equal(rows[:, :K], q.view(torch.uint8))
+    assert torch.equal(rows[:, K:K + K // 32].contiguous().view(torch.float32), s)
+
+
+@pytest.mark.parametrize("M,E,k,K,N,pad", [(1, 8, 2, 256, 128, 0), (37, 16, 4, 512, 256, 48),
+                                           (300, 8, 2, 384, 128, 16)])
+def test_fp8_rows_path_equals_fused_fp8(cuda_device, M, E, k, K, N, pad):
+    """The expert path started from packed rows (any 16-byte multiple pitch, -1 slots skipped)
+    gives the same bits as fused_moe_fp8 on the tokens those rows came from."""
+    from kernelswift_competition_submission_b200 import fp8_row_bytes, fused_moe_fp8_rows, quantize_rows_fp8_packed
+
+    dev = cuda_device
+    w1q, w1s, w2q, w2s = _fp8_weights(E, K, N, dev, seed=7 * M + E)
+    gen = torch.Generator(device=dev).manual_seed(M + 1)
+    x = torch.randn(M, K, generator=gen, device=dev).to(torch.bfloat16)
+    w, ids = softmax_topk(torch.randn(M, E, generator=gen, device=dev), k)
+    ids = ids.to(torch.int32)
+    ids[::5, -1] = -1  # a skipped slot on every fifth token
+    rb = fp8_row_bytes(K)
+    buf = torch.zeros(M, rb + pad, dtype=torch.uint8, device=dev)
+    buf[:, :rb] = quantize_rows_fp8_packed(x)
+    got = fused_moe_fp8_rows(buf, K, w1q, w1s, w2q, w2s, w, ids)
+    want = fused_moe_fp8(x, w1q, w1s, w2q, w2s, w, ids)
+    torch.cuda.synchronize()
+    check_device_status(dev)
+    assert torch.equal(got, want)
