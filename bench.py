@@ -29,6 +29,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -412,6 +413,16 @@ def run_native(args):
                     "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                     "frac": achieved / peaks["hbm_gbs"], "peak_source": f"{peaks['source']} hbm_gbs",
                     "traffic": None, "bytes_per_launch": layer_bytes, "ms_per_launch": path_ms}
+    elif world > 1 and math.isnan(statistics.mean(gemm1_ms)):
+        # peer-memory transport: no per-GEMM events; rank 0's expert phase (align, GEMM1, GEMM2)
+        path_ms = phases.get("experts", ms_per_step)
+        path_flops = 6.0 * pairs_local * K * N
+        achieved = path_flops / (path_ms / 1e3) / 1e12
+        peak = peaks["bf16_tflops_sustained"]
+        roof = {"kernel": "expert path on rank 0 (align, GEMM1, GEMM2)", "bound": "tensor", "achieved": achieved,
+                "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                "peak_source": f"{peaks['source']} bf16_tflops_sustained", "traffic": None,
+                "flops_per_launch": path_flops, "ms_per_launch": path_ms}
     else:
         g1 = statistics.mean(gemm1_ms)
         g1_flops = 4.0 * pairs_local * K * N

@@ -201,8 +201,10 @@ p2p_combine_back_kernel(const uint4* __restrict__ partial, int K, int world, int
 
 // The expert path's top-k combine fused with the return trip: for received row t
 // (region src = t / cap, row r = t % cap, r < counts[src]) the weighted sum of its k slot
-// rows of y_slots is stored straight into rank src's back_x region `me`, row r. One thread
-// per 16-byte vector of a row; the last CTA raises back[me] in every rank.
+// rows of y_slots is stored straight into rank src's back_x region `me`, row r. A
+// persistent grid strides over the 16-byte vectors of all rows, so each CTA issues its
+// system-scope fence once (a fence per short-lived CTA costs an NVLink round trip each);
+// the last CTA raises back[me] in every rank.
 template <typename T>
 __global__ void __launch_bounds__(kP2PThreads)
 p2p_combine_experts_back_kernel(const uint4* __restrict__ y, const float* __restrict__ w,
@@ -210,35 +212,38 @@ p2p_combine_experts_back_kernel(const uint4* __restrict__ y, const float* __rest
                                 int64_t cap, const int64_t* __restrict__ peer_base, P2PLayout lay,
                                 const int32_t* own_counts, uint32_t seq, int32_t* done) {
   __shared__ int s_last;
-  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int64_t t = gid / vpr;
-  const int v = (int)(gid - t * vpr);
-  if (t < (int64_t)world * cap) {
+  __shared__ int s_cnt[kP2PMaxWorld];
+  for (int i = threadIdx.x; i < world; i += blockDim.x) s_cnt[i] = __ldcg(own_counts + i);
+  __syncthreads();
+  const int64_t total = (int64_t)world * cap * vpr;
+  for (int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; gid < total;
+       gid += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = gid / vpr;
+    const int v = (int)(gid - t * vpr);
     const int src = (int)(t / cap);
     const int64_t r = t - (int64_t)src * cap;
-    if (r < __ldcg(own_counts + src)) {
-      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      for (int j = 0; j < topk; ++j) {
-        const int e = __ldg(ids + t * topk + j);
-        if (e < 0 || e >= E) continue;
-        const float wj = __ldg(w + t * topk + j);
-        const uint4 q = __ldg(y + (t * topk + j) * vpr + v);
-        const uint32_t u[4] = {q.x, q.y, q.z, q.w};
+    if (r >= s_cnt[src]) continue;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j < topk; ++j) {
+      const int e = __ldg(ids + t * topk + j);
+      if (e < 0 || e >= E) continue;
+      const float wj = __ldg(w + t * topk + j);
+      const uint4 q = __ldg(y + (t * topk + j) * vpr + v);
+      const uint32_t u[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 f = ElemTraits<T>::unpack2(u[i]);
-          acc[2 * i] = fmaf(wj, f.x, acc[2 * i]);
-          acc[2 * i + 1] = fmaf(wj, f.y, acc[2 * i + 1]);
-        }
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = ElemTraits<T>::unpack2(u[i]);
+        acc[2 * i] = fmaf(wj, f.x, acc[2 * i]);
+        acc[2 * i + 1] = fmaf(wj, f.y, acc[2 * i + 1]);
       }
-      uint4 o;
-      o.x = ElemTraits<T>::pack2(acc[0], acc[1]);
-      o.y = ElemTraits<T>::pack2(acc[2], acc[3]);
-      o.z = ElemTraits<T>::pack2(acc[4], acc[5]);
-      o.w = ElemTraits<T>::pack2(acc[6], acc[7]);
-      uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<char*>(peer_base[src]) + lay.back_x);
-      dst[((int64_t)me * cap + r) * vpr + v] = o;
     }
+    uint4 o;
+    o.x = ElemTraits<T>::pack2(acc[0], acc[1]);
+    o.y = ElemTraits<T>::pack2(acc[2], acc[3]);
+    o.z = ElemTraits<T>::pack2(acc[4], acc[5]);
+    o.w = ElemTraits<T>::pack2(acc[6], acc[7]);
+    uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<char*>(peer_base[src]) + lay.back_x);
+    dst[((int64_t)me * cap + r) * vpr + v] = o;
   }
   __threadfence_system();
   __syncthreads();
@@ -401,7 +406,7 @@ extern "C" int moe_p2p_combine_experts_back(int dtype, const void* workspace, in
   const uint4* y = reinterpret_cast<const uint4*>(static_cast<const char*>(workspace) + y_off);
   const char* ob = static_cast<const char*>(own_base);
   const int vpr = hidden_size / 8;
-  const unsigned blocks = (unsigned)ceil_div(R * vpr, kP2PThreads);
+  const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div(R * vpr, kP2PThreads), 2 * num_sms()));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const float* w = reinterpret_cast<const float*>(ob + l.recv_w);
   const int32_t* ids = reinterpret_cast<const int32_t*>(ob + l.recv_id);
