@@ -258,8 +258,14 @@ class ExpertParallelMoE:
                                                                  self.w2.shape[2]))
             if self._ws is None or self._ws.numel() < need:
                 self._ws = torch.empty(int(need * 1.25) + 256, dtype=torch.uint8, device=x.device)
-            return fused_moe_fp8_rows(x, self.hidden, self.w1, self.w1s, self.w2, self.w2s, w, ids, out=out,
-                                      workspace=self._ws, max_ctas=max_ctas)
+            if events:  # one library call: the stage events bracket it (no per-GEMM split)
+                events[0].record()
+            y = fused_moe_fp8_rows(x, self.hidden, self.w1, self.w1s, self.w2, self.w2s, w, ids, out=out,
+                                   workspace=self._ws, max_ctas=max_ctas)
+            if events:
+                for e in events[1:]:
+                    e.record()
+            return y
         need = fused_moe_workspace_bytes(M, self.w1.shape[0], ids.shape[1], x.shape[1], self.w2.shape[2])
         if self._ws is None or self._ws.numel() < need:
             self._ws = torch.empty(int(need * 1.25) + 256, dtype=torch.uint8, device=x.device)
