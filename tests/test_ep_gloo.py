@@ -242,9 +242,12 @@ def _unpack_rows(rows, K):
     return q, s
 
 
-def _worker_fp8(rank, world, port, q, m_per_rank):
+def _worker_fp8(rank, world, port, q, cfg):
     """FP8 layer on gloo ranks: the packed e4m3 rows travel; each rank's expert stage reads
-    them back and runs the oracle on its own experts' slots."""
+    them back and runs the oracle on its own experts' slots (and, with n_hot > 0, on the
+    replicas of the n_hot busiest experts, e4m3 weights and block scales broadcast by
+    ``rebalance``)."""
+    m_per_rank, n_hot = cfg
     try:
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
         from datetime import timedelta
@@ -263,22 +266,32 @@ def _worker_fp8(rank, world, port, q, m_per_rank):
         def as_e4m3(a):
             return torch.from_numpy(np.ascontiguousarray(a)).to(torch.float8_e4m3fn)
 
+        holder = {}
+
         def experts(rows, w, ids, events=None):
             ids_np = ids.numpy()
             if rows.shape[0] == 0:
                 return torch.zeros(0, HID8)
             xq, xs = _unpack_rows(rows, HID8)
             w_np = np.where(ids_np >= 0, w.numpy(), 0.0).astype(np.float32)
-            return torch.from_numpy(moe_experts_fp8_rows_ref(xq, xs, w1q[sl], w1s[sl], w2q[sl], w2s[sl], w_np,
-                                                             ids_np))
+            lay = holder["layer"]  # the layer's own expert table (replicas appended by rebalance)
+            lw1 = lay.w1.view(torch.float8_e4m3fn).float().numpy()
+            lw2 = lay.w2.view(torch.float8_e4m3fn).float().numpy()
+            return torch.from_numpy(moe_experts_fp8_rows_ref(xq, xs, lw1, lay.w1s.numpy(), lw2, lay.w2s.numpy(),
+                                                             w_np, ids_np))
 
         layer = ExpertParallelMoE(as_e4m3(w1q[sl]), as_e4m3(w2q[sl]), num_experts=E, topk=K_TOP, route_fn=_route,
                                   expert_fn=experts, use_fp8_w8a8=True, w1_scale=torch.from_numpy(w1s[sl].copy()),
                                   w2_scale=torch.from_numpy(w2s[sl].copy()), quant_fn=_pack_rows)
+        holder["layer"] = layer
         m = m_per_rank[rank]
         rng_t = np.random.default_rng(2000 + rank)
         x = rng_t.standard_normal((m, HID8), dtype=np.float32)
         g = rng_t.standard_normal((m, E), dtype=np.float32)
+        if n_hot:
+            _, ids0 = _route(None, torch.from_numpy(g))
+            hot = layer.rebalance(ids0, n_hot)
+            assert hot == layer.replicated and layer.w1s.shape[0] == el + n_hot
         out = layer.forward(torch.from_numpy(x), torch.from_numpy(g))
         w, ids = _route(None, torch.from_numpy(g))
         ref = moe_experts_fp8_ref(x, w1q, w1s, w2q, w2s, w.numpy(), ids.numpy())
@@ -290,11 +303,12 @@ def _worker_fp8(rank, world, port, q, m_per_rank):
         q.put((rank, "error", traceback.format_exc()))
 
 
-@pytest.mark.parametrize("world,m", [(2, [37, 50]), (4, [20, 0, 33, 8])])
-def test_ep_fp8_payload_matches_single_process(world, m):
+@pytest.mark.parametrize("world,m,n_hot", [(2, [37, 50], 0), (4, [20, 0, 33, 8], 0), (4, [25, 40, 0, 12], 3)])
+def test_ep_fp8_payload_matches_single_process(world, m, n_hot):
     """The packed e4m3 rows survive pack -> all-to-all -> expert stage unchanged: the layer
-    equals the single-process FP8 oracle on the same tokens (fp32 summation order only)."""
-    res = _run(world, m, target=_worker_fp8)
+    equals the single-process FP8 oracle on the same tokens (fp32 summation order only),
+    also with hot experts replicated from their owners' e4m3 weights and scales."""
+    res = _run(world, (m, n_hot), target=_worker_fp8)
     assert len(res) == world, res
     for r, (status, val) in res.items():
         assert status == "ok", val
