@@ -1,4 +1,4 @@
-"""Expert-parallel MoE layer over NCCL (one process per GPU).
+"""Expert-parallel MoE layer (one process per GPU; NCCL all-to-all or NVLink peer stores).
 
 The reference has no multi-device code; this layer is the expert-parallel
 form of its MoE path (``grouped_topk`` routing feeding ``fused_moe``,
@@ -29,6 +29,10 @@ the same collective steps in the same order, including for empty splits.
 
 ``route_fn`` / ``expert_fn`` default to this package's CUDA ops; the CPU tests
 inject the numpy oracle to check the dispatch/combine logic on gloo ranks.
+
+``transport="p2p"`` replaces steps 3 and 5 by NVLink stores into per-rank arenas
+shared through CUDA IPC (``moe_p2p_*``): no NCCL call and no host read of split
+sizes inside a step, and the expert combine is fused with the return stores.
 
 FP8 w8a8 (``use_fp8_w8a8=True``, e4m3 expert weights with fp32 scales per
 128 x 128 block): each rank quantises its own token rows once, per token per
@@ -114,6 +118,8 @@ class ExpertParallelMoE:
             if w1_scale is None or w2_scale is None:
                 raise ValueError("use_fp8_w8a8 needs w1_scale and w2_scale")
             El, twoN, Kh = w1_local.shape
+            if tuple(w2_local.shape) != (El, Kh, twoN // 2) or Kh % 128 or twoN % 256:
+                raise ValueError("use_fp8_w8a8: w1_local [E/G, 2N, K] and w2_local [E/G, K, N], K and N % 128 == 0")
             if tuple(w1_scale.shape) != (El, twoN // 128, Kh // 128) or \
                     tuple(w2_scale.shape) != (El, Kh // 128, twoN // 2 // 128):
                 raise ValueError("use_fp8_w8a8: w1_scale / w2_scale must be [E/G, 2N/128, K/128] / [E/G, K/128, N/128]")
@@ -130,9 +136,6 @@ class ExpertParallelMoE:
                              e_score_correction_bias=e_score_correction_bias)
         self.route_fn = route_fn or self._route_cuda
         self.expert_fn = expert_fn or self._experts_cuda
-        # routing, EP count, EP pack, align count, align scatter, GEMM1, GEMM2, combine, EP combine
-        # (FP8: + row quantisation, row gather, scale gather)
-        self.kernel_launches_per_step = 12 if self.fp8 else 9
         self._ws = None
         # per-phase CUDA events of each forward when `profile` is set (bench breakdown)
         self.profile = False
@@ -160,6 +163,17 @@ class ExpertParallelMoE:
         self.transport = transport
         self.max_tokens = max_tokens  # p2p arena size in tokens per rank (default: the first batch, max over ranks)
         self._p2p = None
+
+    @property
+    def kernel_launches_per_step(self):
+        """This library's kernels launched by one CUDA forward."""
+        if self.transport == "p2p":
+            # routing, signal, dispatch, wait, align count, align scatter, GEMM1, GEMM2,
+            # fused combine + return, wait, EP combine (FP8: + quantise, row gather, scale gather)
+            return 14 if self.fp8 else 11
+        # routing, then per chunk: EP count, EP pack, align count, align scatter, GEMM1, GEMM2,
+        # combine, EP combine (FP8: + quantise once, row and scale gathers per chunk)
+        return (2 + 10 * self.chunks) if self.fp8 else (1 + 8 * self.chunks)
 
     # ------------------------------------------------------------------ hot-expert replicas
     def replicate(self, expert_ids, w1_rep, w2_rep, w1s_rep=None, w2s_rep=None):
