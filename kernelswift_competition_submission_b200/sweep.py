@@ -16,6 +16,9 @@ timed call, median over the calls:
   router         router GEMM fused with grouped_topk, M = 1, 128, 4096, 32768, against the
                  unfused pair (cuBLAS bf16 GEMM + grouped_topk)
   decode_graph   the DeepSeek-V3 bf16 layer at M = 1, 8, 64, eager and as one replayed CUDA graph
+  ep_one_rank    (only when named) the expert-parallel layer over a one-rank NCCL group,
+                 M = 16384, bf16 and FP8, NCCL and peer-arena transports: per-phase times of
+                 one rank (the same rows reach the expert stage through either transport)
 
 Each line carries the algorithmic work (FLOPs = 6 M k K N for the expert path;
 bytes = A 3 K N b_w (+ block scales) + M K b_x + M K 2 + M k 8 + M E 4 with A the
@@ -191,6 +194,56 @@ def sweep_decode_graph(dev, timer, peaks, iters):
               {"experts_hit": A, "eager_ms": eager, "replays": cache.replays})
 
 
+def sweep_ep_one_rank(dev, iters):
+    """ExpertParallelMoE over a one-rank NCCL group at the DeepSeek-V3 shape, M = 16384: mean
+    per-phase CUDA-event times over `iters` forwards after 3 warm-ups, for bf16 and FP8
+    weights and both transports."""
+    import os
+    import socket
+
+    import torch.distributed as dist
+
+    from .ep import ExpertParallelMoE
+
+    if not dist.is_initialized():
+        with socket.socket() as sk:
+            sk.bind(("127.0.0.1", 0))
+            port = sk.getsockname()[1]
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", str(port))
+        dist.init_process_group("nccl", rank=0, world_size=1, device_id=dev)
+    E, k, K, N, M = 256, 8, 7168, 2048, 16384
+    x, g, bias = _dsv3_inputs(M, dev)
+    for fp8 in (False, True):
+        w1, w2 = _weights(E, K, N, dev, seed=43_000)
+        kw = {}
+        if fp8:
+            w1, s1 = ops.quantize_weights_fp8(w1)
+            w2, s2 = ops.quantize_weights_fp8(w2)
+            kw = dict(use_fp8_w8a8=True, w1_scale=s1, w2_scale=s2)
+        torch.cuda.empty_cache()
+        for transport in ("nccl", "p2p"):
+            layer = ExpertParallelMoE(w1, w2, num_experts=E, topk=k, num_expert_group=8, topk_group=4,
+                                      scoring_func="sigmoid", routed_scaling_factor=2.5,
+                                      e_score_correction_bias=bias, transport=transport, chunks=1, **kw)
+            for _ in range(3):
+                layer.forward(x, g)
+            torch.cuda.synchronize()
+            layer.profile, layer.phase_log = True, []
+            for _ in range(iters):
+                layer.forward(x, g)
+            layer.profile = False
+            ph = layer.phase_breakdown()
+            print(json.dumps({"config": "ep_one_rank", "M": M, "dtype": "fp8" if fp8 else "bf16",
+                              "transport": transport, "ms_per_step": sum(ph.values()),
+                              "phases_ms": {n: round(v, 4) for n, v in ph.items()}}), flush=True)
+            layer.close()
+            ops.check_device_status(dev)
+        del w1, w2
+        torch.cuda.empty_cache()
+    dist.destroy_process_group()
+
+
 def sweep_tasks(dev, iters_unused=None):
     """The reference's own task shapes through the drop-in ModelNew modules, timed the way
     its harness times them: per call, host clock around the call and a device synchronise,
@@ -259,7 +312,7 @@ def main():
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--only", nargs="*", default=None,
                     choices=["grouped_topk", "mixtral", "dsv3_bf16", "dsv3_fp8", "tasks", "router",
-                             "decode_graph"])
+                             "decode_graph", "ep_one_rank"])
     a = ap.parse_args()
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
@@ -283,6 +336,8 @@ def main():
         torch.cuda.empty_cache()
     if "dsv3_fp8" in want:
         sweep_dsv3(dev, timer, peaks, a.iters, fp8=True)
+    if "ep_one_rank" in want:  # named only: it sets up a one-rank process group
+        sweep_ep_one_rank(dev, a.iters)
 
 
 if __name__ == "__main__":
