@@ -199,11 +199,14 @@ p2p_combine_back_kernel(const uint4* __restrict__ partial, int K, int world, int
   if (threadIdx.x == 0) *done = 0;
 }
 
+constexpr int kSlotBatch = 8;
+
 // The expert path's top-k combine fused with the return trip: for received row t
 // (region src = t / cap, row r = t % cap, r < counts[src]) the weighted sum of its k slot
 // rows of y_slots is stored straight into rank src's back_x region `me`, row r. A
-// persistent grid strides over the 16-byte vectors of all rows, so each CTA issues its
-// system-scope fence once (a fence per short-lived CTA costs an NVLink round trip each);
+// persistent grid (2 CTAs per SM, all resident) strides over the 16-byte vectors of all rows, so each
+// CTA issues its system-scope fence once (a fence per short-lived CTA costs an NVLink
+// round trip each);
 // the last CTA raises back[me] in every rank.
 template <typename T>
 __global__ void __launch_bounds__(kP2PThreads)
@@ -224,17 +227,31 @@ p2p_combine_experts_back_kernel(const uint4* __restrict__ y, const float* __rest
     const int64_t r = t - (int64_t)src * cap;
     if (r >= s_cnt[src]) continue;
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int j = 0; j < topk; ++j) {
-      const int e = __ldg(ids + t * topk + j);
-      if (e < 0 || e >= E) continue;
-      const float wj = __ldg(w + t * topk + j);
-      const uint4 q = __ldg(y + (t * topk + j) * vpr + v);
-      const uint32_t u[4] = {q.x, q.y, q.z, q.w};
+    // slots in batches of kSlotBatch: every load of a batch is issued before the first FMA
+    // (the threads of a persistent grid get their memory parallelism from here); the FMAs
+    // then run in slot order, as in combine_kernel, so the sums are the same bits
+    for (int j0 = 0; j0 < topk; j0 += kSlotBatch) {
+      uint4 q[kSlotBatch];
+      float wj[kSlotBatch];
+      bool ok[kSlotBatch];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 f = ElemTraits<T>::unpack2(u[i]);
-        acc[2 * i] = fmaf(wj, f.x, acc[2 * i]);
-        acc[2 * i + 1] = fmaf(wj, f.y, acc[2 * i + 1]);
+      for (int b = 0; b < kSlotBatch; ++b) {
+        const int j = j0 + b;
+        const int e = j < topk ? __ldg(ids + t * topk + j) : -1;
+        ok[b] = e >= 0 && e < E;
+        wj[b] = ok[b] ? __ldg(w + t * topk + j) : 0.f;
+        q[b] = ok[b] ? __ldg(y + (t * topk + j) * vpr + v) : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int b = 0; b < kSlotBatch; ++b) {
+        if (!ok[b]) continue;
+        const uint32_t u[4] = {q[b].x, q[b].y, q[b].z, q[b].w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = ElemTraits<T>::unpack2(u[i]);
+          acc[2 * i] = fmaf(wj[b], f.x, acc[2 * i]);
+          acc[2 * i + 1] = fmaf(wj[b], f.y, acc[2 * i + 1]);
+        }
       }
     }
     uint4 o;
