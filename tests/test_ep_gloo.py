@@ -313,3 +313,38 @@ def test_ep_fp8_payload_matches_single_process(world, m, n_hot):
     for r, (status, val) in res.items():
         assert status == "ok", val
         assert val < 1e-4, f"rank {r} max err {val}"
+
+
+def _launch_counts(rank, world, port, q, unused):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        from datetime import timedelta
+
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=30))
+        w1, w2 = _weights()
+        el = E // world
+        w1l, w2l = torch.from_numpy(w1[:el]), torch.from_numpy(w2[:el])
+        w8a, w8b = torch.zeros(el, 256, 128, dtype=torch.uint8), torch.zeros(el, 128, 128, dtype=torch.uint8)
+        s8a, s8b = torch.ones(el, 2, 1), torch.ones(el, 1, 1)
+        got = {}
+        for name, kw, a, b in (("nccl1", dict(chunks=1), w1l, w2l), ("nccl2", dict(chunks=2), w1l, w2l),
+                               ("p2p", dict(transport="p2p"), w1l, w2l),
+                               ("fp8_nccl2", dict(chunks=2, use_fp8_w8a8=True, w1_scale=s8a, w2_scale=s8b), w8a, w8b),
+                               ("fp8_p2p", dict(transport="p2p", use_fp8_w8a8=True, w1_scale=s8a, w2_scale=s8b), w8a,
+                                w8b)):
+            got[name] = ExpertParallelMoE(a, b, num_experts=E, topk=K_TOP, **kw).kernel_launches_per_step
+        q.put((rank, "ok", got))
+        dist.destroy_process_group()
+    except Exception:
+        q.put((rank, "error", traceback.format_exc()))
+
+
+def test_kernel_launch_counts_per_transport():
+    """The launch count the bench reports follows the forward that runs: routing + 8 kernels
+    per token chunk (NCCL, bf16), + quantise once and 2 gathers per chunk (FP8), 11 / 14 kernels
+    through the peer arenas."""
+    res = _run(2, None, target=_launch_counts)
+    assert len(res) == 2, res
+    for r, (status, val) in res.items():
+        assert status == "ok", val
+        assert val == {"nccl1": 9, "nccl2": 17, "p2p": 11, "fp8_nccl2": 22, "fp8_p2p": 14}, val
