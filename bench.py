@@ -15,9 +15,15 @@ expert path -> NCCL all-to-all combine (strong scaling, M fixed).
 
 Reported: tokens/s of the whole job (max over ranks of the CUDA-event time),
 a roofline entry for the dominant kernel (the tcgen05 gate/up GEMM, timed
-with CUDA events on its launch stream), an end-to-end figure through the
-public API with host buffers, the oracle timed on the host cores as a CPU
-baseline, and the SM clocks sampled during the timed region.
+with CUDA events on its launch stream, against the measured burst bf16 rate),
+an end-to-end figure through the public API with host buffers, the oracle
+timed on the host cores as a CPU baseline, and the SM clocks sampled during
+the timed region. At N = 1 also: "parity" (512 sampled rows of the last timed
+step's output against an fp32 restatement of the reference's expert path) and
+"configs" (the other configurations, timed per call: DeepSeek-V3 bf16 at
+M = 1, 64, 512, 4096 and FP8 at M = 1, 8, 32, 128, Mixtral bf16, grouped_topk
+alone, the router GEMM fused with routing, decode-size graph replay and the
+reference's task shapes), each with its roofline fraction.
 
 --impl reference times the reference's CPU implementation of the path (its
 v0 algorithm, restated by the numpy oracle because the reference itself is
@@ -40,6 +46,7 @@ from pathlib import Path
 
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
+sys.path.insert(1, str(ROOT / "tests"))  # torch_ref: fp32 restatement used for the in-bench parity check
 
 METRIC = "MoE-layer tokens/s, DeepSeek-V3 shape (E=256, top-8, K=7168, N=2048), bf16"
 UNIT = "tokens/s"
@@ -68,6 +75,10 @@ def parse():
                     help="expert-parallel: replicate the N busiest experts (from the first batch's routing) on "
                          "every rank")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the per-configuration rows (DeepSeek-V3 bf16 / FP8 token sweeps, Mixtral, routing, "
+                         "task shapes) that a 1-GPU run adds under \"configs\"")
+    ap.add_argument("--config-iters", type=int, default=20, help="timed calls per configuration row")
     ap.add_argument("--e2e-steps", type=int, default=20,
                     help="batches streamed through HostPipeline for the end-to-end figure (fill and drain amortised)")
     return ap.parse_args()
@@ -239,6 +250,232 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------------------------- per-configuration rows (1 GPU)
+class _CallTimer:
+    """Median CUDA-event time of single calls, L2 flushed (a 256 MiB write) before each."""
+
+    def __init__(self, dev):
+        import torch
+
+        self.torch = torch
+        self.flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def median_ms(self, fn, iters, warmup=3):
+        torch = self.torch
+        for _ in range(warmup):
+            fn()
+        ts = []
+        for _ in range(iters):
+            self.flush.fill_(1)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            b.synchronize()
+            ts.append(a.elapsed_time(b))
+        return statistics.median(ts)
+
+
+def _row(name, M, ms, flops, nbytes, peaks, tc_tflops, **extra):
+    """One configuration row: time, throughput and the fraction of the binding roofline
+    (measured HBM copy bandwidth, or the measured burst bf16 tensor rate; e4m3 at twice it)."""
+    t_tc = flops / (tc_tflops * 1e12) if flops else 0.0
+    t_hbm = nbytes / (peaks["hbm_gbs"] * 1e9)
+    d = {"config": name, "tokens": M, "ms": ms, "tokens_per_s": M / (ms / 1e3),
+         "tflops": flops / (ms / 1e3) / 1e12 if flops else None, "gbs": nbytes / (ms / 1e3) / 1e9,
+         "alg_flops": flops, "alg_bytes": nbytes, "bound": "tensor" if t_tc > t_hbm else "hbm",
+         "roofline_frac": max(t_tc, t_hbm) / (ms / 1e3)}
+    d.update(extra)
+    return d
+
+
+def _layer_bytes(ids, E, K, N, M, k, wbytes, scale_bytes=0):
+    import torch
+
+    A = int(torch.unique(ids).numel())
+    return A * (3 * K * N * wbytes + scale_bytes) + M * K * 2 * 2 + M * k * 8 + M * E * 4, A
+
+
+def _dsv3_inputs(M, dev):
+    import torch
+
+    gen = torch.Generator(device=dev).manual_seed(1000 + M)
+    x = torch.randn(M, DSV3["K"], generator=gen, device=dev).to(torch.bfloat16)
+    g = torch.randn(M, 256, generator=gen, device=dev)
+    bias = torch.randn(256, generator=torch.Generator(device=dev).manual_seed(44), device=dev) * 0.01
+    return x, g, bias
+
+
+def config_rows(dev, w1, w2, peaks, iters):
+    """The other configurations of the layer on one GPU, each timed per call (median of
+    `iters` after 3 warm-ups, L2 flushed before each call): grouped_topk alone (M = 128 and
+    32768), Mixtral bf16 (M = 256), the DeepSeek-V3 bf16 layer at M = 1, 64, 512, 4096, the
+    FP8 w8a8 layer at M = 1, 8, 32, 128, and the reference's task shapes through the drop-in
+    modules (the harness's per-call protocol)."""
+    import torch
+
+    from kernelswift_competition_submission_b200 import ops
+
+    timer = _CallTimer(dev)
+    rows = []
+    bf16 = peaks["bf16_tflops"]
+    E, k, K, N = 256, DSV3["topk"], DSV3["K"], DSV3["N"]
+    bias = torch.randn(E, generator=torch.Generator(device=dev).manual_seed(44), device=dev) * 0.01
+    for M in (128, 32768):
+        g = torch.randn(M, E, generator=torch.Generator(device=dev).manual_seed(M), device=dev)
+        ms = timer.median_ms(lambda: ops.grouped_topk(None, g, k, True, 8, 4, "sigmoid", 2.5,
+                                                      e_score_correction_bias=bias), iters)
+        rows.append(_row("grouped_topk", M, ms, 0, M * E * 4 + E * 4 + M * k * 8, peaks, bf16))
+    # Mixtral: E = 8, top-2 softmax, K = 4096, N = 14336
+    Em, km, Km, Nm, Mm = 8, 2, 4096, 14336, 256
+    gm = torch.Generator(device=dev).manual_seed(5000)
+    mw1 = (torch.randn(Em, 2 * Nm, Km, generator=gm, device=dev) / Km ** 0.5).to(torch.bfloat16)
+    mw2 = (torch.randn(Em, Km, Nm, generator=gm, device=dev) / Nm ** 0.5).to(torch.bfloat16)
+    gen = torch.Generator(device=dev).manual_seed(42)
+    mx = torch.randn(Mm, Km, generator=gen, device=dev).to(torch.bfloat16)
+    ml = torch.randn(Mm, Em, generator=gen, device=dev)
+    mout = torch.empty(Mm, Km, dtype=torch.bfloat16, device=dev)
+    mws = torch.empty(ops.fused_moe_workspace_bytes(Mm, Em, km, Km, Nm), dtype=torch.uint8, device=dev)
+
+    def mixtral():
+        w_, i_ = ops.softmax_topk(ml, km)
+        ops.fused_moe(mx, mw1, mw2, w_, i_, out=mout, workspace=mws)
+
+    ms = timer.median_ms(mixtral, iters)
+    nbytes, A = _layer_bytes(ops.softmax_topk(ml, km)[1], Em, Km, Nm, Mm, km, 2)
+    rows.append(_row("mixtral_bf16", Mm, ms, 6.0 * Mm * km * Km * Nm, nbytes, peaks, bf16, experts_hit=A))
+    del mw1, mw2, mws
+    # DeepSeek-V3 bf16 and FP8 token sweeps on the bench's own expert weights
+    w1q, w1s = ops.quantize_weights_fp8(w1)
+    w2q, w2s = ops.quantize_weights_fp8(w2)
+    for fp8, Ms in ((False, (1, 64, 512, 4096)), (True, (1, 8, 32, 128))):
+        for M in Ms:
+            x, g, b_ = _dsv3_inputs(M, dev)
+            out = torch.empty(M, K, dtype=torch.bfloat16, device=dev)
+            lib = ops._lib.load()
+            need = lib.moe_fused_workspace_bytes_fp8(M, E, k, K, N) if fp8 else \
+                lib.moe_fused_workspace_bytes(M, E, k, K, N)
+            ws = torch.empty(int(need), dtype=torch.uint8, device=dev)
+
+            def layer():
+                w_, i_ = ops.grouped_topk(x, g, k, True, 8, 4, "sigmoid", 2.5, e_score_correction_bias=b_)
+                if fp8:
+                    ops.fused_moe(x, w1q, w2q, w_, i_, use_fp8_w8a8=True, w1_scale=w1s, w2_scale=w2s, out=out,
+                                  workspace=ws)
+                else:
+                    ops.fused_moe(x, w1, w2, w_, i_, out=out, workspace=ws)
+
+            ms = timer.median_ms(layer, iters)
+            ids = ops.grouped_topk(x, g, k, True, 8, 4, "sigmoid", 2.5, e_score_correction_bias=b_)[1]
+            scale_bytes = 3 * (K // 128) * (N // 128) * 4 if fp8 else 0
+            nbytes, A = _layer_bytes(ids, E, K, N, M, k, 1 if fp8 else 2, scale_bytes)
+            rows.append(_row("dsv3_fp8" if fp8 else "dsv3_bf16", M, ms, 6.0 * M * k * K * N, nbytes, peaks,
+                             bf16 * (2.0 if fp8 else 1.0), experts_hit=A))
+    del w1q, w2q, w1s, w2s
+    # decode sizes: the bf16 layer eager (one launch per kernel) and replayed as one CUDA graph
+    from kernelswift_competition_submission_b200.graphs import GraphCache
+
+    for M in (1, 8, 64):
+        x, g, b_ = _dsv3_inputs(M, dev)
+
+        def decode(xx, gg):
+            return ops.moe_layer(xx, gg, w1, w2, topk=k, renormalize=True, num_expert_group=8, topk_group=4,
+                                 scoring_func="sigmoid", routed_scaling_factor=2.5, e_score_correction_bias=b_)
+
+        eager = timer.median_ms(lambda: decode(x, g), iters)
+        cache = GraphCache(decode)
+        graph = timer.median_ms(lambda: cache(x, g), iters)
+        ids = ops.grouped_topk(x, g, k, True, 8, 4, "sigmoid", 2.5, e_score_correction_bias=b_)[1]
+        nbytes, A = _layer_bytes(ids, E, K, N, M, k, 2)
+        rows.append(_row("dsv3_bf16_graph", M, graph, 6.0 * M * k * K * N, nbytes, peaks, bf16, experts_hit=A,
+                         eager_ms=eager))
+    # router GEMM fused with grouped_topk against the unfused pair (torch bf16 GEMM + grouped_topk)
+    wg = (torch.randn(E, K, generator=torch.Generator(device=dev).manual_seed(7), device=dev) / K ** 0.5).bfloat16()
+    for M in (1, 128, 4096, 32768):
+        x = torch.randn(M, K, generator=torch.Generator(device=dev).manual_seed(M), device=dev).bfloat16()
+        fused = timer.median_ms(lambda: ops.router_grouped_topk(x, wg, k, True, 8, 4, "sigmoid", 2.5,
+                                                                e_score_correction_bias=bias), iters)
+        unfused = timer.median_ms(lambda: ops.grouped_topk(x, (x @ wg.T).float(), k, True, 8, 4, "sigmoid", 2.5,
+                                                           e_score_correction_bias=bias), iters)
+        rows.append(_row("router_fused", M, fused, 2.0 * M * K * E, E * K * 2 + M * K * 2 + M * k * 8, peaks, bf16,
+                         unfused_ms=unfused))
+    ops.check_device_status(dev)
+    rows += task_shape_rows(dev)
+    torch.cuda.empty_cache()
+    return rows
+
+
+def task_shape_rows(dev):
+    """The reference's own task shapes through the drop-in ModelNew modules, timed the way
+    its harness times them: per call, host clock around the call and a device synchronise,
+    200 warm-up calls, median of 500; graph replay (the modules' forward) and eager."""
+    import importlib.util
+
+    import torch
+
+    def load(name):
+        spec = importlib.util.spec_from_file_location(
+            f"task_{name}", ROOT / "kernelswift_competition_submission_b200" / "tasks" / f"{name}.py")
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        return mod
+
+    def median_call_ms(fn, args):
+        for _ in range(200):
+            fn(*args)
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(500):
+            t0 = time.perf_counter()
+            fn(*args)
+            torch.cuda.synchronize()
+            ts.append((time.perf_counter() - t0) * 1e3)
+        return statistics.median(ts)
+
+    torch.manual_seed(42)
+    rows = []
+    for name in ("grouped_topk", "fused_moe"):
+        mod = load(name)
+        model = mod.ModelNew(*mod.get_init_inputs()).to(dev)
+        args = [t.to(dev) for t in mod.get_inputs()]
+        with torch.no_grad():
+            graph_ms = median_call_ms(model, args)
+            if name == "fused_moe":
+                w1, w2 = model._prepared_weights(args[0].dtype)
+                eager_ms = median_call_ms(lambda a, b: model._forward_eager(a, b, w1, w2), args)
+            else:
+                eager_ms = median_call_ms(model._forward_eager, args)
+        rows.append({"config": f"task_{name}", "tokens": int(args[0].shape[0]), "ms": graph_ms,
+                     "eager_ms": eager_ms, "protocol": "host clock per call + synchronize, median of 500 after 200 "
+                                                       "warm-up calls (the reference harness's protocol)"})
+    return rows
+
+
+def parity_check(x, ids, w, out, w1, w2, fp8_weights=None, rows=512, seed=7):
+    """Sampled rows of the bench's own last output against the fp32 restatement of the
+    reference's expert path (fused_moe/v0/fused_moe.py:141-167) on the same operands;
+    outside the timed region. Tolerance: 2e-2 bf16, 5e-2 FP8 (on dequantised operands)."""
+    import torch
+
+    from torch_ref import experts_rows_fp32, experts_rows_fp8
+
+    M = x.shape[0]
+    gen = torch.Generator(device=x.device).manual_seed(seed)
+    r = torch.randperm(M, generator=gen, device=x.device)[: min(rows, M)].cpu()
+    if fp8_weights is None:
+        ref, tol = experts_rows_fp32(x, w1, w2, w, ids, r), 2e-2
+    else:
+        ref, tol = experts_rows_fp8(x, *fp8_weights, w, ids, r), 5e-2
+    got = out[r.to(x.device)].float()
+    err = (got - ref).abs()
+    ok = bool((err <= tol + tol * ref.abs()).all())
+    return {"rows": int(r.numel()), "experts_covered": int(torch.unique(ids[r.to(x.device)]).numel()),
+            "max_abs_err": float(err.max()), "rel_l2_err": float((got - ref).norm() / ref.norm()),
+            "atol": tol, "rtol": tol, "pass": ok,
+            "reference": "fp32 torch restatement of fused_moe/v0/fused_moe.py:141-167 on sampled rows"
+                         + (" (dequantised e4m3 operands)" if fp8_weights is not None else "")}
+
+
 # ----------------------------------------------------------------------------- GPU run
 def run_native(args):
     import torch
@@ -305,7 +542,7 @@ def run_native(args):
             return ids
 
         layer = None
-        launches_per_step = 6  # grouped_topk, align count, align scatter, gemm1, gemm2, combine
+        launches_per_step = 6  # grouped_topk, align count, align scatter (+ row gather), GEMM1, GEMM2, combine
     else:
         from kernelswift_competition_submission_b200.ep import ExpertParallelMoE
 
@@ -370,11 +607,15 @@ def run_native(args):
     value = M_total * args.steps / (ms / 1e3)
 
     # pairs and distinct experts of this rank's expert path (from the last step's routing)
+    parity = None
     if world == 1:
         w_last, ids_last = ops.grouped_topk(x, g, k, True, DSV3["n_group"], DSV3["topk_group"], "sigmoid",
                                             DSV3["scale"], e_score_correction_bias=bias)
         pairs_local = M * k
         distinct = int(torch.unique(ids_last).numel())
+        # the last timed step's output, checked on sampled rows (outside the timed region)
+        parity = parity_check(x, ids_last, w_last, out, None if args.fp8 else w1, None if args.fp8 else w2,
+                              (w1q, w1s, w2q, w2s) if args.fp8 else None)
     else:
         pairs_local, distinct = layer.local_work()
         layer.profile = False
@@ -400,12 +641,12 @@ def run_native(args):
         else:  # rank 0's expert phase (received rows; no communication inside)
             path_ms = phases.get("experts", ms_per_step)
         path_flops = 6.0 * pairs_local * K * N
-        peak_f8 = 2.0 * peaks["bf16_tflops_sustained"]
+        peak_f8 = 2.0 * peaks["bf16_tflops"]
         if path_flops / (peak_f8 * 1e12) >= layer_bytes / (peaks["hbm_gbs"] * 1e9):
             achieved = path_flops / (path_ms / 1e3) / 1e12
             roof = {"kernel": "FP8 expert path (quantise, align, gather, GEMM1, GEMM2, combine)", "bound": "tensor",
                     "achieved": achieved, "peak": peak_f8, "unit": "TFLOP/s", "frac": achieved / peak_f8,
-                    "peak_source": f"2 x {peaks['source']} bf16_tflops_sustained (e4m3 dense rate)",
+                    "peak_source": f"2 x {peaks['source']} bf16_tflops (burst; e4m3 dense rate)",
                     "traffic": None, "flops_per_launch": path_flops, "ms_per_launch": path_ms}
         else:
             achieved = layer_bytes / (path_ms / 1e3) / 1e9
@@ -418,26 +659,28 @@ def run_native(args):
         path_ms = phases.get("experts", ms_per_step)
         path_flops = 6.0 * pairs_local * K * N
         achieved = path_flops / (path_ms / 1e3) / 1e12
-        peak = peaks["bf16_tflops_sustained"]
+        peak = peaks["bf16_tflops"]
         roof = {"kernel": "expert path on rank 0 (align, GEMM1, GEMM2)", "bound": "tensor", "achieved": achieved,
                 "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                "peak_source": f"{peaks['source']} bf16_tflops_sustained", "traffic": None,
+                "peak_source": f"{peaks['source']} bf16_tflops (burst)", "traffic": None,
                 "flops_per_launch": path_flops, "ms_per_launch": path_ms}
     else:
         g1 = statistics.mean(gemm1_ms)
         g1_flops = 4.0 * pairs_local * K * N
         achieved = g1_flops / (g1 / 1e3) / 1e12
-        peak = peaks["bf16_tflops_sustained"]
+        # the GEMM runs ~12 ms inside ~20 ms steps, not a seconds-long loop: burst peak
+        peak = peaks["bf16_tflops"]
         tr = committed_traffic("moe_gemm1_silu")
         traffic = None
         if tr is not None:
             traffic = tr["bytes_per_pair"] * pairs_local + tr.get("bytes_fixed", 0)
         roof = {"kernel": "moe_gemm1_silu (tcgen05 gate/up GEMM + SiLU*mul)", "bound": "tensor",
                 "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                "peak_source": f"{peaks['source']} bf16_tflops_sustained",
+                "peak_source": f"{peaks['source']} bf16_tflops (burst)",
                 "traffic": traffic, "flops_per_launch": g1_flops, "ms_per_launch": g1,
-                "gemm2_ms_per_launch": statistics.mean(gemm2_ms)}
-    peak_tc = peaks["bf16_tflops_sustained"]
+                "gemm2_ms_per_launch": statistics.mean(gemm2_ms),
+                "frac_of_sustained_peak": achieved / peaks["bf16_tflops_sustained"]}
+    peak_tc = peaks["bf16_tflops"]
 
     result = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -457,6 +700,8 @@ def run_native(args):
         "clocks": clocks,
         "gpu_launches": launches_per_step * args.steps,
     }
+    if parity is not None:
+        result["parity"] = parity
     if world > 1:
         result["config"]["ep_overlap"] = {"chunks": layer.chunks, "reserve_sms": layer.reserve_sms}
         result["config"]["ep_transport"] = layer.transport
@@ -525,6 +770,11 @@ def run_native(args):
                    + ("; per-rank host bytes, value is the whole job" if world > 1 else "")}
     result["e2e"] = e2e
     pkg.check_device_status(dev)
+
+    if world == 1 and not args.fp8 and not args.no_configs and E == 256:
+        del pipe, ohs
+        torch.cuda.empty_cache()
+        result["configs"] = config_rows(dev, w1, w2, peaks, args.config_iters)
 
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, dt, cores = cpu_oracle_tokens_per_s(64)

@@ -16,7 +16,8 @@
  *     detected on the host before any launch. Device-side failures (a bounded
  *     wait that gave up) are recorded in the optional `status` word, a device
  *     int the caller zeroes and reads after synchronising.
- *   - No function allocates device memory; scratch comes from the caller's
+ *   - No function allocates device memory except moe_p2p_alloc (the peer-memory
+ *     arena that other ranks map through CUDA IPC); scratch comes from the caller's
  *     workspace (see moe_fused_workspace_bytes).
  *   - Inputs are never written.
  */
@@ -177,15 +178,24 @@ MOE_API int moe_fused_experts(int dtype, const void* hidden_states, const void* 
                       void* workspace, size_t workspace_bytes, int* status, void* stream);
 
 /*
- * The four stages of moe_fused_experts as separate calls on the same workspace
+ * The stages of moe_fused_experts as separate calls on the same workspace
  * (same arguments as moe_fused_experts), in this order:
  *   moe_expert_align_gather  align stage + gather of each pair's token row into
  *                            expert-sorted order (workspace)
  *   moe_expert_gemm1         tcgen05 gate/up GEMM, SiLU*mul epilogue -> act (workspace)
+ *   then either
+ *   moe_expert_gemm2_combine tcgen05 down GEMM with the top-k weighted sum fused into
+ *                            its epilogue -> out (replaces fused_moe/v0/fused_moe.py:163-167
+ *                            and the reduce kernel fused_moe/v1/fused_moe.py:221-252)
+ *   or
  *   moe_expert_gemm2         tcgen05 down GEMM, per-pair rows -> slot buffer (workspace)
  *   moe_expert_combine       top-k weighted sum of the slot rows -> out
- * moe_fused_experts(...) is exactly these four calls (with max_ctas = 0). They
- * exist so a caller can interleave its own work (events, communication)
+ * Both endings give the same bits: the fused epilogue sums a token's slot rows in slot
+ * order in fp32, exactly as moe_expert_combine does, once all of them are stored. The
+ * separate combine is the faster one at prefill sizes (a token's last slot arrives with
+ * its highest-numbered expert, so the fused sums bunch up in the GEMM's last tiles);
+ * moe_fused_experts(...) runs align_gather, gemm1, gemm2 and combine (max_ctas = 0).
+ * They exist so a caller can interleave its own work (events, communication)
  * between stages. max_ctas limits the persistent GEMM grid (0 = one CTA per
  * SM) so that work on other streams, e.g. collectives, can run beside it.
  */
@@ -193,12 +203,30 @@ MOE_API int moe_expert_align_gather(int dtype, const void* hidden_states, const 
                                     int64_t num_tokens, int num_experts, int topk, int hidden_size,
                                     int intermediate_size, void* workspace, size_t workspace_bytes,
                                     void* stream);
+/* The same expert path without the expert-sorted copy of the token rows (the workspace
+ * region the gather fills is left untouched, so a caller may size it away):
+ * moe_expert_align (the align stage alone), then moe_expert_gemm1_gather, the gate/up
+ * GEMM reading each A row straight from hidden_states (token sorted_pairs[r] / topk) with
+ * cp.async into the tensor-core layout, then either GEMM2 ending. Same bits as
+ * align_gather + gemm1; slower at prefill sizes (the tensor core waits on the cp.async
+ * row copies), so it is the choice for tight memory rather than for speed. */
+MOE_API int moe_expert_align(const int32_t* topk_ids, int64_t num_tokens, int num_experts, int topk,
+                             int hidden_size, int intermediate_size, void* workspace, size_t workspace_bytes,
+                             void* stream);
+MOE_API int moe_expert_gemm1_gather(int dtype, const void* hidden_states, const void* w1, int64_t num_tokens,
+                                    int num_experts, int topk, int hidden_size, int intermediate_size,
+                                    void* workspace, size_t workspace_bytes, int* status, int max_ctas,
+                                    void* stream);
 MOE_API int moe_expert_gemm1(int dtype, const void* w1, int64_t num_tokens, int num_experts, int topk,
                              int hidden_size, int intermediate_size, void* workspace,
                              size_t workspace_bytes, int* status, int max_ctas, void* stream);
 MOE_API int moe_expert_gemm2(int dtype, const void* w2, int64_t num_tokens, int num_experts, int topk,
                              int hidden_size, int intermediate_size, void* workspace,
                              size_t workspace_bytes, int* status, int max_ctas, void* stream);
+MOE_API int moe_expert_gemm2_combine(int dtype, const void* w2, const float* topk_weights,
+                                     const int32_t* topk_ids, int64_t num_tokens, int num_experts, int topk,
+                                     int hidden_size, int intermediate_size, void* out, void* workspace,
+                                     size_t workspace_bytes, int* status, int max_ctas, void* stream);
 MOE_API int moe_expert_combine(int dtype, const float* topk_weights, const int32_t* topk_ids,
                                int64_t num_tokens, int num_experts, int topk, int hidden_size,
                                int intermediate_size, void* out, void* workspace,
@@ -319,26 +347,32 @@ MOE_API int moe_router_grouped_topk(int dtype, const void* hidden_states, const 
                                     void* stream);
 
 /* Expert-parallel dispatch / combine over NVLink peer memory (no reference counterpart;
- * decode-sized batches). Each rank allocates one arena (moe_p2p_arena_bytes, moe_p2p_alloc
- * -> its 64-byte CUDA IPC handle), opens every other rank's handle (moe_p2p_open) and keeps
+ * decode-sized batches). Each rank allocates one arena (moe_p2p_alloc: moe_p2p_arena_bytes
+ * of device memory with its flags and counts zeroed and its id rows set to -1, and its
+ * 64-byte CUDA IPC handle), opens every other rank's handle (moe_p2p_open) and keeps
  * the world base pointers in a device int64 array `peer_bases` (its own at index me).
  * Per step with sequence number seq (1, 2, ...): moe_p2p_signal(which 0: ready),
  * moe_p2p_dispatch (waits for every rank's ready, writes token rows / ids / weights into
  * the destination ranks' arenas, then their disp flags), moe_p2p_wait(which 1) before the
  * local expert path over the world * cap received rows (recv_x, recv_id, recv_w at
  * moe_p2p_arena_offsets[4..6]), moe_p2p_combine_back (returns the partial rows, then back
- * flags), moe_p2p_wait(which 2), then moe_ep_combine over back_x (offset [7]) with the
- * tok_rows the dispatch wrote. scratch: int32 [2 * world + 1] zeroed once (dispatch),
- * int32 [1] zeroed once (combine_back). Waits are bounded (MOE_ERR_TIMEOUT in status).
+ * flags), moe_p2p_wait(which 2), then moe_p2p_reduce (or moe_ep_combine over back_x,
+ * offset [7]) with the tok_rows the dispatch wrote. scratch: int32 [2 * world + 1] zeroed
+ * once (dispatch), int32 [1] zeroed once (combine_back).
+ * Failure: waits are bounded (2 s); one that gives up records MOE_ERR_TIMEOUT in `status`.
+ * Every moe_p2p_* kernel reads `status` first and does nothing once it is set (no waits,
+ * no peer stores, no flags), and moe_p2p_reduce then writes NaN rows, so a failed step
+ * never returns another step's rows. The arenas must then be rebuilt on every rank
+ * (free, alloc, exchange handles) with the status word zeroed before the next step.
  * offsets[9]: ready, disp, back, counts, recv_x, recv_id, recv_w, back_x, total. */
 MOE_API int64_t moe_p2p_arena_bytes(int world, int64_t cap, int hidden_size, int topk);
 MOE_API int moe_p2p_arena_offsets(int world, int64_t cap, int hidden_size, int topk, int64_t* offsets);
-MOE_API int moe_p2p_alloc(size_t bytes, void** base, void* ipc_handle);
+MOE_API int moe_p2p_alloc(int world, int64_t cap, int hidden_size, int topk, void** base, void* ipc_handle);
 MOE_API int moe_p2p_open(const void* ipc_handle, void** base);
 MOE_API int moe_p2p_close(void* base);
 MOE_API int moe_p2p_free(void* base);
 MOE_API int moe_p2p_signal(const int64_t* peer_bases, int world, int me, int which, int64_t cap, int hidden_size,
-                           int topk, uint32_t seq, void* stream);
+                           int topk, uint32_t seq, int* status, void* stream);
 MOE_API int moe_p2p_wait(const void* own_base, int world, int which, int64_t cap, int hidden_size, int topk,
                          uint32_t seq, int* status, void* stream);
 MOE_API int moe_p2p_dispatch(int dtype, const void* hidden_states, const int32_t* topk_ids,
@@ -355,13 +389,18 @@ MOE_API int moe_p2p_dispatch(int dtype, const void* hidden_states, const int32_t
 MOE_API int moe_p2p_combine_experts_back(int dtype, const void* workspace, int num_experts, int hidden_size,
                                          int intermediate_size, int topk, int world, int me, int64_t cap,
                                          const int64_t* peer_bases, const void* own_base, uint32_t seq,
-                                         int32_t* scratch, void* stream);
+                                         int32_t* scratch, int* status, void* stream);
 /* copy of the received expert ids [world * cap, topk] (statistics, tests) */
 MOE_API int moe_p2p_copy_recv_ids(const void* own_base, int world, int64_t cap, int hidden_size, int topk,
                                   int32_t* dst, void* stream);
 MOE_API int moe_p2p_combine_back(int dtype, const void* partial, int hidden_size, int topk, int world, int me,
                                  int64_t cap, const int64_t* peer_bases, const void* own_base, uint32_t seq,
-                                 int32_t* scratch, void* stream);
+                                 int32_t* scratch, int* status, void* stream);
+/* out[t] = sum of the rows the experts' ranks returned for token t (back_x rows named by
+ * tok_rows, fp32 accumulation); NaN rows when `status` holds a failure code. */
+MOE_API int moe_p2p_reduce(int dtype, const void* own_base, const int32_t* tok_rows, int64_t num_tokens,
+                           int hidden_size, int topk, int world, int64_t cap, void* out, const int* status,
+                           void* stream);
 
 /* Expert placement by table instead of contiguous ranges: expert_map int32 [num_experts]
  * holds (rank << 16) | local_id for every expert, so a rank can keep replicas of hot

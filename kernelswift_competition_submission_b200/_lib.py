@@ -53,8 +53,13 @@ SIGNATURES = {
     "moe_fused_experts": (_i32, [_i32, _c_p, _c_p, _c_p, _c_p, _c_p, _i64, _i32, _i32, _i32, _i32, _c_p, _c_p, _sz,
                                  _c_p, _c_p]),
     "moe_expert_align_gather": (_i32, [_i32, _c_p, _c_p, _i64, _i32, _i32, _i32, _i32, _c_p, _sz, _c_p]),
+    "moe_expert_align": (_i32, [_c_p, _i64, _i32, _i32, _i32, _i32, _c_p, _sz, _c_p]),
+    "moe_expert_gemm1_gather": (_i32, [_i32, _c_p, _c_p, _i64, _i32, _i32, _i32, _i32, _c_p, _sz, _c_p, _i32,
+                                       _c_p]),
     "moe_expert_gemm1": (_i32, [_i32, _c_p, _i64, _i32, _i32, _i32, _i32, _c_p, _sz, _c_p, _i32, _c_p]),
     "moe_expert_gemm2": (_i32, [_i32, _c_p, _i64, _i32, _i32, _i32, _i32, _c_p, _sz, _c_p, _i32, _c_p]),
+    "moe_expert_gemm2_combine": (_i32, [_i32, _c_p, _c_p, _c_p, _i64, _i32, _i32, _i32, _i32, _c_p, _c_p, _sz, _c_p,
+                                        _i32, _c_p]),
     "moe_expert_combine": (_i32, [_i32, _c_p, _c_p, _i64, _i32, _i32, _i32, _i32, _c_p, _c_p, _sz, _c_p]),
     "moe_quantize_rows_fp8": (_i32, [_i32, _c_p, _i64, _i32, _c_p, _c_p, _c_p]),
     "moe_quantize_blocks_fp8": (_i32, [_i32, _c_p, _i64, _i32, _i32, _c_p, _c_p, _c_p]),
@@ -73,19 +78,20 @@ SIGNATURES = {
                                        _f32, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p]),
     "moe_p2p_arena_bytes": (_i64, [_i32, _i64, _i32, _i32]),
     "moe_p2p_arena_offsets": (_i32, [_i32, _i64, _i32, _i32, _c_p]),
-    "moe_p2p_alloc": (_i32, [ctypes.c_size_t, _c_p, _c_p]),
+    "moe_p2p_alloc": (_i32, [_i32, _i64, _i32, _i32, _c_p, _c_p]),
     "moe_p2p_open": (_i32, [_c_p, _c_p]),
     "moe_p2p_close": (_i32, [_c_p]),
     "moe_p2p_free": (_i32, [_c_p]),
-    "moe_p2p_signal": (_i32, [_c_p, _i32, _i32, _i32, _i64, _i32, _i32, ctypes.c_uint32, _c_p]),
+    "moe_p2p_signal": (_i32, [_c_p, _i32, _i32, _i32, _i64, _i32, _i32, ctypes.c_uint32, _c_p, _c_p]),
     "moe_p2p_wait": (_i32, [_c_p, _i32, _i32, _i64, _i32, _i32, ctypes.c_uint32, _c_p, _c_p]),
     "moe_p2p_dispatch": (_i32, [_i32, _c_p, _c_p, _c_p, _i64, _i32, _i32, _i32, _i32, _i32, _i64, _c_p, _c_p,
                                 ctypes.c_uint32, _c_p, _c_p, _c_p, _c_p]),
     "moe_p2p_combine_experts_back": (_i32, [_i32, _c_p, _i32, _i32, _i32, _i32, _i32, _i32, _i64, _c_p, _c_p,
-                                            ctypes.c_uint32, _c_p, _c_p]),
+                                            ctypes.c_uint32, _c_p, _c_p, _c_p]),
     "moe_p2p_copy_recv_ids": (_i32, [_c_p, _i32, _i64, _i32, _i32, _c_p, _c_p]),
     "moe_p2p_combine_back": (_i32, [_i32, _c_p, _i32, _i32, _i32, _i32, _i64, _c_p, _c_p, ctypes.c_uint32, _c_p,
-                                    _c_p]),
+                                    _c_p, _c_p]),
+    "moe_p2p_reduce": (_i32, [_i32, _c_p, _c_p, _i64, _i32, _i32, _i32, _i64, _c_p, _c_p, _c_p]),
     "moe_ep_plan_mapped": (_i32, [_c_p, _i64, _i32, _i32, _c_p, _i32, _c_p, _c_p, _c_p, _c_p]),
     "moe_ep_pack_mapped": (_i32, [_i32, _c_p, _c_p, _c_p, _i64, _i32, _i32, _i32, _c_p, _i32, _c_p, _c_p, _c_p, _c_p,
                                   _c_p, _c_p]),

@@ -144,11 +144,11 @@ align_scatter_kernel(const int32_t* __restrict__ ids, int64_t P, int topk, int E
 
 cudaError_t launch_align(const int32_t* topk_ids, int64_t P, int topk, int E, int bm, AlignMeta meta,
                          bool meta_contiguous, int32_t* sorted_pairs, int64_t cap, const void* x_src, void* x_sorted,
-                         int64_t row_bytes, cudaStream_t st) {
-  cudaError_t err;
-  if (meta_contiguous) {
+                         int64_t row_bytes, cudaStream_t st, bool zero_meta) {
+  cudaError_t err = cudaSuccess;
+  if (zero_meta && meta_contiguous) {
     err = cudaMemsetAsync(meta.counts, 0, sizeof(int32_t) * (2 * (size_t)E + 1), st);
-  } else {
+  } else if (zero_meta) {
     err = cudaMemsetAsync(meta.counts, 0, sizeof(int32_t) * E, st);
     if (err == cudaSuccess) err = cudaMemsetAsync(meta.cursor, 0, sizeof(int32_t) * E, st);
     if (err == cudaSuccess) err = cudaMemsetAsync(meta.done, 0, sizeof(int32_t), st);

@@ -28,8 +28,9 @@ int device_is_sm100() {
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 struct FusedLayout {
-  size_t meta, sorted, x_sorted, act, y_slots, total;
+  size_t meta, sorted, x_sorted, act, y_slots, arrivals, total;
   int64_t cap;
+  int64_t n_arrivals;  // [M, n-blocks of the down GEMM] counters of the fused combine
 };
 
 FusedLayout fused_layout(int64_t M, int E, int topk, int K, int N) {
@@ -42,6 +43,8 @@ FusedLayout fused_layout(int64_t M, int E, int topk, int K, int N) {
   l.x_sorted = off; off = align_up(off + 2 * (size_t)l.cap * (size_t)K, 256);
   l.act = off;      off = align_up(off + 2 * (size_t)l.cap * (size_t)N, 256);
   l.y_slots = off;  off = align_up(off + 2 * (size_t)P * (size_t)K, 256);
+  l.n_arrivals = M * ceil_div(K, gemm2_block_n(K));
+  l.arrivals = off; off = align_up(off + sizeof(int32_t) * (size_t)l.n_arrivals, 256);
   l.total = off;
   return l;
 }
@@ -107,6 +110,7 @@ struct Ws {
   void* x_sorted;
   void* act;
   void* y_slots;
+  int32_t* arrivals;
   AlignMeta am;
   FusedLayout l;
 };
@@ -121,6 +125,7 @@ int workspace_views(void* workspace, size_t bytes, int64_t M, int E, int topk, i
   w->x_sorted = ws + w->l.x_sorted;
   w->act = ws + w->l.act;
   w->y_slots = ws + w->l.y_slots;
+  w->arrivals = reinterpret_cast<int32_t*>(ws + w->l.arrivals);
   w->am = align_meta_contiguous(w->meta, E);
   return MOE_OK;
 }
@@ -145,6 +150,40 @@ extern "C" int moe_expert_align_gather(int dtype, const void* hidden_states, con
   return cuda_status(launch_align(topk_ids, num_tokens * topk, topk, num_experts, kBlockM, w.am, true, w.sorted,
                                   w.l.cap, hidden_states, w.x_sorted, (int64_t)hidden_size * 2,
                                   static_cast<cudaStream_t>(stream)));
+}
+
+extern "C" int moe_expert_align(const int32_t* topk_ids, int64_t num_tokens, int num_experts, int topk,
+                                int hidden_size, int intermediate_size, void* workspace, size_t workspace_bytes,
+                                void* stream) {
+  using namespace moe;
+  int rc = validate_experts(MOE_DTYPE_BF16, num_tokens, num_experts, topk, hidden_size, intermediate_size);
+  if (rc != MOE_OK || num_tokens == 0) return rc;
+  if (!topk_ids) return MOE_ERR_INVALID_ARG;
+  if ((rc = check_device_ready()) != MOE_OK) return rc;
+  Ws w;
+  if ((rc = workspace_views(workspace, workspace_bytes, num_tokens, num_experts, topk, hidden_size,
+                            intermediate_size, &w)) != MOE_OK)
+    return rc;
+  return cuda_status(launch_align(topk_ids, num_tokens * topk, topk, num_experts, kBlockM, w.am, true, w.sorted,
+                                  w.l.cap, nullptr, nullptr, 0, static_cast<cudaStream_t>(stream)));
+}
+
+extern "C" int moe_expert_gemm1_gather(int dtype, const void* hidden_states, const void* w1, int64_t num_tokens,
+                                       int num_experts, int topk, int hidden_size, int intermediate_size,
+                                       void* workspace, size_t workspace_bytes, int* status, int max_ctas,
+                                       void* stream) {
+  using namespace moe;
+  int rc = validate_experts(dtype, num_tokens, num_experts, topk, hidden_size, intermediate_size);
+  if (rc != MOE_OK || num_tokens == 0) return rc;
+  if (!hidden_states || !w1 || !aligned16(hidden_states) || !aligned16(w1)) return MOE_ERR_INVALID_ARG;
+  if ((rc = check_device_ready()) != MOE_OK) return rc;
+  Ws w;
+  if ((rc = workspace_views(workspace, workspace_bytes, num_tokens, num_experts, topk, hidden_size,
+                            intermediate_size, &w)) != MOE_OK)
+    return rc;
+  return cuda_status(launch_gemm1_gather(dtype, hidden_states, hidden_size, topk, w.sorted, w.l.cap, w1, num_experts,
+                                         hidden_size, intermediate_size, w.am.block_start, w.act, status, max_ctas,
+                                         static_cast<cudaStream_t>(stream)));
 }
 
 extern "C" int moe_expert_gemm1(int dtype, const void* w1, int64_t num_tokens, int num_experts, int topk,
@@ -196,6 +235,29 @@ extern "C" int moe_expert_combine(int dtype, const float* topk_weights, const in
                                     hidden_size, out, static_cast<cudaStream_t>(stream)));
 }
 
+extern "C" int moe_expert_gemm2_combine(int dtype, const void* w2, const float* topk_weights,
+                                        const int32_t* topk_ids, int64_t num_tokens, int num_experts, int topk,
+                                        int hidden_size, int intermediate_size, void* out, void* workspace,
+                                        size_t workspace_bytes, int* status, int max_ctas, void* stream) {
+  using namespace moe;
+  int rc = validate_experts(dtype, num_tokens, num_experts, topk, hidden_size, intermediate_size);
+  if (rc != MOE_OK || num_tokens == 0) return rc;
+  if (!w2 || !topk_weights || !topk_ids || !out || !aligned16(w2) || !aligned16(out)) return MOE_ERR_INVALID_ARG;
+  if ((rc = check_device_ready()) != MOE_OK) return rc;
+  Ws w;
+  if ((rc = workspace_views(workspace, workspace_bytes, num_tokens, num_experts, topk, hidden_size,
+                            intermediate_size, &w)) != MOE_OK)
+    return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t err = launch_combine_prep(topk_ids, num_tokens, topk, num_experts, hidden_size, w.arrivals,
+                                        w.l.n_arrivals, nullptr, 0, out, st);
+  if (err == cudaSuccess)
+    err = launch_gemm2_combine(dtype, w.act, w.l.cap, w2, num_experts, hidden_size, intermediate_size,
+                               w.am.block_start, w.sorted, w.y_slots, topk_weights, topk_ids, topk, w.arrivals, out,
+                               status, max_ctas, st);
+  return cuda_status(err);
+}
+
 extern "C" int moe_fused_experts(int dtype, const void* hidden_states, const void* w1, const void* w2,
                                  const float* topk_weights, const int32_t* topk_ids, int64_t num_tokens,
                                  int num_experts, int topk, int hidden_size, int intermediate_size, void* out,
@@ -212,6 +274,8 @@ extern "C" int moe_fused_experts(int dtype, const void* hidden_states, const voi
     return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int64_t P = num_tokens * topk;
+  // The measured-fastest stages at every size (the row gather inside GEMM1 and the combine
+  // inside GEMM2's epilogue give the same bits but run slower at prefill sizes).
   cudaError_t err = launch_align(topk_ids, P, topk, num_experts, kBlockM, w.am, true, w.sorted, w.l.cap,
                                  hidden_states, w.x_sorted, (int64_t)hidden_size * 2, st);
   if (err == cudaSuccess)

@@ -8,6 +8,8 @@
 #include "common.cuh"
 #include "moe_internal.h"
 
+#include <algorithm>
+
 namespace moe {
 namespace {
 
@@ -41,7 +43,41 @@ combine_kernel(const uint4* __restrict__ y, const float* __restrict__ w, const i
   out[t * vecs_per_row + v] = o;
 }
 
+// Set-up of the combine fused into the down GEMM (MODE_GEMM2_COMBINE): zeroes the
+// [M, NB] arrival counters and `n_zero` further ints (the align metadata, when the
+// caller folds its memset in here), and writes a zero row to `out` for every token none
+// of whose slots holds an expert in [0, E): no GEMM tile reaches such a token, and the
+// reference's expert loop leaves its output row at zero (fused_moe/v0/fused_moe.py:154-167).
+__global__ void __launch_bounds__(256)
+combine_prep_kernel(const int32_t* __restrict__ ids, int64_t M, int topk, int E, int32_t* __restrict__ arrivals,
+                    int64_t n_arrivals, int32_t* __restrict__ zero_ints, int n_zero, uint4* __restrict__ out,
+                    int vecs_per_row) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (int64_t i = gid; i < n_arrivals; i += stride) arrivals[i] = 0;
+  for (int64_t i = gid; i < n_zero; i += stride) zero_ints[i] = 0;
+  for (int64_t t = gid; t < M; t += stride) {
+    bool any = false;
+    for (int j = 0; j < topk; ++j) {
+      const int e = __ldg(ids + t * topk + j);
+      any |= (e >= 0 && e < E);
+    }
+    if (!any)
+      for (int v = 0; v < vecs_per_row; ++v) out[t * vecs_per_row + v] = make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+
 }  // namespace
+
+cudaError_t launch_combine_prep(const int32_t* topk_ids, int64_t M, int topk, int E, int K, int32_t* arrivals,
+                                int64_t n_arrivals, int32_t* zero_ints, int n_zero, void* out, cudaStream_t st) {
+  const int64_t work = std::max<int64_t>(std::max<int64_t>(n_arrivals, M), n_zero);
+  if (work == 0) return cudaSuccess;
+  const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div(work, 256), 4 * (int64_t)num_sms()));
+  combine_prep_kernel<<<blocks, 256, 0, st>>>(topk_ids, M, topk, E, arrivals, n_arrivals, zero_ints, n_zero,
+                                              static_cast<uint4*>(out), K / 8);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_combine(int dtype, const void* y_slots, const float* topk_weights, const int32_t* topk_ids,
                            int64_t M, int topk, int E, int K, void* out, cudaStream_t st) {

@@ -119,11 +119,17 @@ ep_pack_kernel(const uint4* __restrict__ x, const int32_t* __restrict__ ids, con
 template <typename T>
 __global__ void __launch_bounds__(kEpThreads)
 ep_combine_kernel(const uint4* __restrict__ back, const int32_t* __restrict__ tok_rows, int64_t M, int world,
-                  int vecs_per_row, uint4* __restrict__ out) {
+                  int vecs_per_row, uint4* __restrict__ out, const int* status) {
   const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t t = gid / vecs_per_row;
   const int v = (int)(gid - t * vecs_per_row);
   if (t >= M) return;
+  if (status != nullptr && *reinterpret_cast<const volatile int*>(status) != 0) {
+    // the step's transfers failed (a bounded wait gave up): the rows are not this step's
+    const uint32_t nan2 = ElemTraits<T>::pack2(__int_as_float(0x7fc00000), __int_as_float(0x7fc00000));
+    out[t * vecs_per_row + v] = make_uint4(nan2, nan2, nan2, nan2);
+    return;
+  }
   float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   for (int d = 0; d < world; ++d) {
     const int row = __ldg(tok_rows + t * world + d);
@@ -150,6 +156,21 @@ inline bool ep_args_ok(int64_t M, int topk, int epr, int world) {
 }
 
 }  // namespace
+
+cudaError_t launch_ep_combine(int dtype, const void* back, const int32_t* tok_rows, int64_t M, int K, int world,
+                              void* out, const int* status, cudaStream_t st) {
+  if (M == 0) return cudaSuccess;
+  const int vpr = K / 8;
+  const unsigned blocks = (unsigned)ceil_div(M * vpr, kEpThreads);
+  if (dtype == MOE_DTYPE_BF16)
+    ep_combine_kernel<__nv_bfloat16><<<blocks, kEpThreads, 0, st>>>(static_cast<const uint4*>(back), tok_rows, M,
+                                                                    world, vpr, static_cast<uint4*>(out), status);
+  else
+    ep_combine_kernel<__half><<<blocks, kEpThreads, 0, st>>>(static_cast<const uint4*>(back), tok_rows, M, world, vpr,
+                                                             static_cast<uint4*>(out), status);
+  return cudaGetLastError();
+}
+
 }  // namespace moe
 
 extern "C" int64_t moe_ep_send_capacity(int64_t num_tokens, int topk, int world) {
@@ -256,15 +277,8 @@ extern "C" int moe_ep_combine(int dtype, const void* returned_rows, const int32_
   if (!returned_rows || !tok_rows || !out) return MOE_ERR_INVALID_ARG;
   if ((reinterpret_cast<uintptr_t>(returned_rows) & 15u) || (reinterpret_cast<uintptr_t>(out) & 15u))
     return MOE_ERR_INVALID_ARG;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int vpr = hidden_size / 8;
-  const unsigned blocks = (unsigned)ceil_div(num_tokens * vpr, kEpThreads);
-  if (dtype == MOE_DTYPE_BF16)
-    ep_combine_kernel<__nv_bfloat16><<<blocks, kEpThreads, 0, st>>>(static_cast<const uint4*>(returned_rows),
-                                                                    tok_rows, num_tokens, world, vpr,
-                                                                    static_cast<uint4*>(out));
-  else
-    ep_combine_kernel<__half><<<blocks, kEpThreads, 0, st>>>(static_cast<const uint4*>(returned_rows), tok_rows,
-                                                             num_tokens, world, vpr, static_cast<uint4*>(out));
-  return cudaGetLastError() == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
+  return launch_ep_combine(dtype, returned_rows, tok_rows, num_tokens, hidden_size, world, out, nullptr,
+                           static_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? MOE_OK
+             : MOE_ERR_CUDA;
 }

@@ -4,6 +4,8 @@
 // fused_moe/v0/fused_moe.py:160-163:
 //   GEMM1_SILU : act[r, n]  = silu(x_r . w1[e, n]) * (x_r . w1[e, N + n])     (:160-162)
 //   GEMM2      : y[pair(r)] = act_r . w2[e]^T                                  (:163)
+//   GEMM2_COMBINE: GEMM2, then the top-k weighted sum of :165-167 in the epilogue:
+//               out[t] = sum_j topk_weights[t, j] * y[t * topk + j]
 // Rows r come from the align stage: pairs grouped by expert e in m-blocks of
 // 128 rows (block_start[e] .. block_start[e+1]).
 //
@@ -25,6 +27,16 @@
 // [N+n0, N+n0+BN/2) of the same expert, so gate and up of column n land in
 // the same accumulator row and SiLU*mul needs no extra pass or weight copy.
 //
+// GEMM1_GATHER is GEMM1_SILU with the A tile gathered from the token rows instead of
+// loaded from an expert-sorted copy: warps 2-3 (64 threads) copy, per stage, the 128-byte
+// K slice of each of the tile's 128 rows (token sorted_pairs[r] / topk) with 16-byte
+// cp.async into the 128-byte-swizzled layout the TMA would have written (chunk c of row r
+// at r * 128 + ((c ^ (r & 7)) * 16)). Each thread keeps up to kGatherLag stages in flight;
+// when a stage's copies are complete it fences them for the async proxy (the tensor core
+// reads them) and arrives on the stage's `full` barrier, which also counts the TMA bytes
+// of the B tile; it announces the oldest stage before it waits for a free one, so the
+// MMAs never wait behind that wait. No row copy of the tokens is made anywhere.
+//
 // Tile order: expert-major, then n-block, then m-block fastest, so concurrently
 // running CTAs share the expert's B tile through L2.
 // All mbarrier waits are bounded (common.cuh); on a timeout every role stops,
@@ -37,9 +49,32 @@
 namespace moe {
 namespace {
 
-enum { MODE_GEMM1_SILU = 0, MODE_GEMM2 = 1 };
+enum { MODE_GEMM1_SILU = 0, MODE_GEMM2 = 1, MODE_GEMM2_COMBINE = 2, MODE_GEMM1_GATHER = 3 };
+
+// A rows of MODE_GEMM1_GATHER: row r of the expert-sorted order is token
+// sorted_pairs[r] / topk of x (row pitch ld elements); padding rows (-1) read as zeros.
+struct RowGather {
+  const void* x;
+  int64_t ld;
+  int topk;
+};
+
+// Fused top-k combine of MODE_GEMM2_COMBINE. Every (token, n-block) has an arrival
+// counter; after a warp has stored its 32 slot rows of one tile it counts each row's
+// arrival, and the warp that brings a token's last valid slot of that n-block sums all
+// of that token's slots over the n-block's columns (slot order, fp32 FMAs, one rounding:
+// the arithmetic of combine_kernel, so the output bits do not depend on arrival order).
+struct CombineArgs {
+  const int32_t* ids;      // [M, topk] expert ids; slots outside [0, E) contribute nothing
+  const float* weights;    // [M, topk]
+  int32_t* arrivals;       // [M, NB], zero before the launch
+  void* out;               // [M, n_out]
+  int topk;
+};
 
 constexpr int kThreads = 256;
+constexpr int kGatherThreads = 64;  // warps 2-3 in MODE_GEMM1_GATHER
+constexpr int kGatherRows = kBlockM / (kGatherThreads / 8);  // rows per gather thread (16)
 constexpr int kBK = 64;                    // K elements per stage (128 bytes of 16-bit data)
 constexpr int kATileBytes = kBlockM * kBK * 2;
 
@@ -74,16 +109,111 @@ __device__ __forceinline__ void decode_tile(const int* s_bs, int E, int NB, int 
   mb = s_bs[lo] + (local - nb * nblk);
 }
 
+// Arrival count and, for the rows whose arrival completes their token's n-block, the
+// weighted slot sum (see CombineArgs). Called by a whole epilogue warp after its 32 rows
+// (lane = row) of the tile's columns [nb * BN, nb * BN + BN) are stored to `slots`.
+template <typename T, int BN>
+__device__ __forceinline__ void combine_rows(const CombineArgs& cmb, const T* slots, int my_pair, int E, int NB,
+                                             int nb, int n_out, int lane) {
+  const int topk = cmb.topk;
+  __threadfence();  // this lane's slot stores are visible device-wide before its rows' arrivals count
+  __syncwarp();
+  int tok = 0;
+  bool last = false;
+  if (my_pair >= 0) {
+    tok = my_pair / topk;
+    const int32_t* tid = cmb.ids + (int64_t)tok * topk;
+    int valid = 0;
+    for (int j = 0; j < topk; ++j) {
+      const int e = __ldg(tid + j);
+      valid += (e >= 0 && e < E) ? 1 : 0;
+    }
+    last = atomicAdd(cmb.arrivals + (int64_t)tok * NB + nb, 1) == valid - 1;
+  }
+  uint32_t todo = __ballot_sync(0xffffffffu, last);
+  if (todo == 0u) return;
+  __threadfence();  // the other slots of these tokens were fenced before their arrivals
+  T* out = static_cast<T*>(cmb.out);
+  const int col = nb * BN + lane * 8;                  // this lane's 8 columns (BN = 128: lanes 16-31 idle)
+  const bool col_ok = lane * 8 < BN && col < n_out;    // n_out % 64 == 0: a vector is whole or outside
+  // kRows completed tokens per round with every slot load of the round in flight before the
+  // first FMA (the slot rows come back from L2 / DRAM; one row at a time is latency-bound).
+  // A slot outside [0, E) loads weight 0 and value 0: fma(0, 0, acc) == acc, so the sums are
+  // the bits of combine_kernel, which skips such slots.
+  constexpr int kRows = 4;
+  while (todo) {
+    int t[kRows];
+#pragma unroll
+    for (int q = 0; q < kRows; ++q) {
+      t[q] = -1;
+      if (todo) {
+        const int src = __ffs(todo) - 1;
+        todo &= todo - 1u;
+        t[q] = __shfl_sync(0xffffffffu, tok, src);
+      }
+    }
+    float acc[kRows][8];
+#pragma unroll
+    for (int q = 0; q < kRows; ++q)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[q][i] = 0.f;
+    for (int j0 = 0; j0 < topk; j0 += 8) {
+      uint4 v[kRows][8];
+      float wj[kRows][8];
+#pragma unroll
+      for (int q = 0; q < kRows; ++q) {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int j = j0 + u;
+          const int e = (t[q] >= 0 && j < topk) ? __ldg(cmb.ids + (int64_t)t[q] * topk + j) : -1;
+          const bool ok = col_ok && e >= 0 && e < E;
+          wj[q][u] = ok ? __ldg(cmb.weights + (int64_t)t[q] * topk + j) : 0.f;
+          v[q][u] = ok ? __ldcg(reinterpret_cast<const uint4*>(slots + ((int64_t)t[q] * topk + j) * n_out + col))
+                       : make_uint4(0u, 0u, 0u, 0u);
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < kRows; ++q) {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const uint32_t h[4] = {v[q][u].x, v[q][u].y, v[q][u].z, v[q][u].w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = ElemTraits<T>::unpack2(h[i]);
+            acc[q][2 * i] = fmaf(wj[q][u], f.x, acc[q][2 * i]);
+            acc[q][2 * i + 1] = fmaf(wj[q][u], f.y, acc[q][2 * i + 1]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < kRows; ++q) {
+      if (t[q] < 0 || !col_ok) continue;
+      uint4 o;
+      o.x = ElemTraits<T>::pack2(acc[q][0], acc[q][1]);
+      o.y = ElemTraits<T>::pack2(acc[q][2], acc[q][3]);
+      o.z = ElemTraits<T>::pack2(acc[q][4], acc[q][5]);
+      o.w = ElemTraits<T>::pack2(acc[q][6], acc[q][7]);
+      *reinterpret_cast<uint4*>(out + (int64_t)t[q] * n_out + col) = o;
+    }
+  }
+}
+
 template <typename T, int MODE, int BN, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
 moe_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                 const int32_t* __restrict__ block_start, int E, int k_red, int n_out, int NB,
-                T* __restrict__ out, const int32_t* __restrict__ sorted_pairs, int* status) {
+                T* __restrict__ out, const int32_t* __restrict__ sorted_pairs, int* status, CombineArgs cmb,
+                RowGather gat) {
   using L = SmemLayout<BN, STAGES>;
-  constexpr int BH = (MODE == MODE_GEMM1_SILU) ? BN / 2 : BN;   // rows per B box
+  constexpr bool kGemm1 = MODE == MODE_GEMM1_SILU || MODE == MODE_GEMM1_GATHER;
+  constexpr bool kGather = MODE == MODE_GEMM1_GATHER;
+  constexpr int BH = kGemm1 ? BN / 2 : BN;   // rows per B box
   constexpr uint32_t kTmemCols = 2 * BN;
   constexpr uint32_t kIdesc = idesc_f16(kBlockM, BN, ElemTraits<T>::kFmt);
-  constexpr uint32_t kStageTx = L::kStageBytes;
+  // bytes the TMA delivers per stage: A and B, or B alone when the A rows are gathered
+  constexpr uint32_t kStageTx = kGather ? (uint32_t)L::kBTileBytes : (uint32_t)L::kStageBytes;
+  constexpr int kGatherLag = STAGES - 1;  // unannounced stages a gather thread keeps in flight
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -102,13 +232,16 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
 
   for (int i = threadIdx.x; i <= E; i += kThreads) s_bs[i] = __ldg(block_start + i);
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], kGather ? 1 + kGatherThreads : 1); mbar_init(&empty[s], 1); }
     for (int a = 0; a < 2; ++a) { mbar_init(&tmem_full[a], 1); mbar_init(&tmem_empty[a], 128); }
     mbar_init(mma_done, 1);
     *s_abort = 0;
     fence_mbar_init();
   }
-  if (warp == 0 && lane == 0) { tma_prefetch_desc(&map_a); tma_prefetch_desc(&map_b); }
+  if (warp == 0 && lane == 0) {
+    if constexpr (!kGather) tma_prefetch_desc(&map_a);
+    tma_prefetch_desc(&map_b);
+  }
   if (warp == 2) { tmem_alloc(s_tmem, kTmemCols); tmem_relinquish(); }
   tc_fence_before();
   __syncthreads();
@@ -133,8 +266,8 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
           uint8_t* a_dst = smem + stage * L::kStageBytes;
           uint8_t* b_dst = a_dst + kATileBytes;
           mbar_arrive_expect_tx(&full[stage], kStageTx);
-          tma_load_2d(&map_a, &full[stage], a_dst, kb * kBK, mb * kBlockM);
-          if constexpr (MODE == MODE_GEMM1_SILU) {
+          if constexpr (!kGather) tma_load_2d(&map_a, &full[stage], a_dst, kb * kBK, mb * kBlockM);
+          if constexpr (kGemm1) {
             tma_load_3d(&map_b, &full[stage], b_dst, kb * kBK, nb * BH, 2 * e);
             tma_load_3d(&map_b, &full[stage], b_dst + BH * kBK * 2, kb * kBK, nb * BH, 2 * e + 1);
           } else {
@@ -151,6 +284,50 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
           if ((issued_mask >> s) & 1u) mbar_wait(&full[s], (issued_parity >> s) & 1u, nullptr, nullptr);
       }
     }
+  } else if (kGather && (warp == 2 || warp == 3)) {
+    // ------------------------------------------------ A-row gather (cp.async)
+    const int gt = threadIdx.x - 64;  // 0 .. kGatherThreads - 1
+    const int c = gt & 7;             // 16-byte chunk of the row's 128-byte K slice
+    const int rg = gt >> 3;           // rows rg, rg + 8, ..., rg + 120 (so r & 7 == rg)
+    const uint32_t dst_off = (uint32_t)(rg * 128 + ((c ^ rg) << 4));
+    const T* xb = static_cast<const T*>(gat.x);
+    uint32_t issued = 0, announced = 0;  // k-iterations copied / arrived on `full`
+    bool ok = true;
+    int64_t row_off[kGatherRows];
+    for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+      int e, nb, mb;
+      decode_tile(s_bs, E, NB, tile, e, nb, mb);
+#pragma unroll
+      for (int i = 0; i < kGatherRows; ++i) {
+        const int pair = __ldg(sorted_pairs + (int64_t)mb * kBlockM + rg + 8 * i);
+        row_off[i] = pair >= 0 ? (int64_t)(pair / gat.topk) * gat.ld + c * 8 : -1;
+      }
+      for (int kb = 0; kb < num_kb; ++kb) {
+        // announce the oldest stage in flight as soon as it has landed, before waiting for
+        // the next free stage: the MMAs of a stage must not wait for that wait
+        if (issued - announced >= (uint32_t)kGatherLag) {
+          cp_async_wait_group<kGatherLag - 1>();
+          fence_proxy_async_smem();
+          mbar_arrive(&full[announced % STAGES]);
+          ++announced;
+        }
+        const int stage = (int)(issued % STAGES);
+        const uint32_t phase = (issued / STAGES) & 1u;
+        if (!mbar_wait(&empty[stage], phase ^ 1, status, s_abort)) { ok = false; break; }
+        const uint32_t a_dst = smem_u32(smem + stage * L::kStageBytes) + dst_off;
+#pragma unroll
+        for (int i = 0; i < kGatherRows; ++i) {
+          const bool live = row_off[i] >= 0;
+          cp_async_16(a_dst + i * 1024, live ? xb + row_off[i] + kb * kBK : xb, live ? 16u : 0u);
+        }
+        cp_async_commit();
+        ++issued;
+      }
+    }
+    // every copy lands before the stages are announced (and before the CTA can exit)
+    cp_async_wait_all();
+    fence_proxy_async_smem();
+    for (; announced < issued; ++announced) mbar_arrive(&full[announced % STAGES]);
   } else if (warp == 1) {
     if (lane == 0) {
       // ------------------------------------------------ MMA issuer
@@ -195,7 +372,7 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
     const int ew = warp - 4;
     uint8_t* stage = smem + L::kEpiOffset + ew * kEpiWarpBytes;
     const int st_r = lane >> 3, st_c = lane & 7;
-    constexpr int kGroups = (MODE == MODE_GEMM1_SILU ? BH : BN) / 64;
+    constexpr int kGroups = (kGemm1 ? BH : BN) / 64;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
@@ -207,14 +384,14 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
       const uint32_t t_row = tmem_base + ((uint32_t)(ew * 32) << 16) + (uint32_t)(acc * BN);
       const int64_t row0 = (int64_t)mb * kBlockM + ew * 32;  // first tile row of this warp
       int my_pair = 0;
-      if constexpr (MODE == MODE_GEMM2) my_pair = __ldg(sorted_pairs + row0 + lane);
+      if constexpr (!kGemm1) my_pair = __ldg(sorted_pairs + row0 + lane);
 #pragma unroll 1
       for (int g = 0; g < kGroups; ++g) {
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           const int c = 2 * g + h;  // 32-column chunk
           uint32_t packed[16];
-          if constexpr (MODE == MODE_GEMM1_SILU) {
+          if constexpr (kGemm1) {
             uint32_t gt[32], up[32];
             tmem_ld32(t_row + c * 32, gt);
             tmem_ld32(t_row + BH + c * 32, up);
@@ -248,7 +425,7 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
         for (int it = 0; it < 8; ++it) {
           const int r = 4 * it + st_r;
           const uint4 val = *reinterpret_cast<const uint4*>(stage + r * kEpiPitch + st_c * 16);
-          if constexpr (MODE == MODE_GEMM1_SILU) {
+          if constexpr (kGemm1) {
             T* dst = out + (row0 + r) * (int64_t)n_out + (int64_t)nb * BH + g * 64 + st_c * 8;
             *reinterpret_cast<uint4*>(dst) = val;
           } else {
@@ -260,6 +437,7 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
         }
         __syncwarp();
       }
+      if constexpr (MODE == MODE_GEMM2_COMBINE) combine_rows<T, BN>(cmb, out, my_pair, E, NB, nb, n_out, lane);
       if (++acc == 2) { acc = 0; acc_phase ^= 1; }
     }
   }
@@ -278,7 +456,8 @@ constexpr int kStages = 4;
 template <typename T, int MODE, int BN>
 cudaError_t launch_gemm_t(const CUtensorMap& ma, const CUtensorMap& mb, const int32_t* block_start, int E, int k_red,
                           int n_out, int NB, int64_t rows_cap, void* out, const int32_t* sorted_pairs, int* status,
-                          int max_ctas, cudaStream_t st) {
+                          int max_ctas, cudaStream_t st, const CombineArgs& cmb = CombineArgs{},
+                          const RowGather& gat = RowGather{}) {
   using L = SmemLayout<BN, kStages>;
   auto kern = moe_gemm_kernel<T, MODE, BN, kStages>;
   const int smem = L::bytes(E);
@@ -290,7 +469,7 @@ cudaError_t launch_gemm_t(const CUtensorMap& ma, const CUtensorMap& mb, const in
   const int ctas = (max_ctas > 0 && max_ctas < num_sms()) ? max_ctas : num_sms();
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(ctas, tiles_cap));
   kern<<<grid, kThreads, smem, st>>>(ma, mb, block_start, E, k_red, n_out, NB, static_cast<T*>(out), sorted_pairs,
-                                     status);
+                                     status, cmb, gat);
   return cudaGetLastError();
 }
 
@@ -322,11 +501,16 @@ cudaError_t launch_gemm1_silu(int dtype, const void* x_sorted, int64_t rows_cap,
                                                      status, max_ctas, st);
 }
 
-cudaError_t launch_gemm2_scatter(int dtype, const void* act, int64_t rows_cap, const void* w2, int E, int K, int N,
-                                 const int32_t* block_start, const int32_t* sorted_pairs, int64_t num_pairs,
-                                 void* y_slots, int* status, int max_ctas, cudaStream_t st) {
-  (void)num_pairs;
-  const int BN = (K >= 256) ? 256 : 128;
+int gemm2_block_n(int K) { return (K >= 256) ? 256 : 128; }
+
+namespace {
+
+// GEMM2 (slot rows) or GEMM2_COMBINE (slot rows + fused top-k sum into cmb.out).
+template <int MODE>
+cudaError_t launch_gemm2_mode(int dtype, const void* act, int64_t rows_cap, const void* w2, int E, int K, int N,
+                              const int32_t* block_start, const int32_t* sorted_pairs, void* y_slots, int* status,
+                              int max_ctas, cudaStream_t st, const CombineArgs& cmb) {
+  const int BN = gemm2_block_n(K);
   CUtensorMap ma, mbm;
   const uint64_t a_dims[2] = {(uint64_t)N, (uint64_t)rows_cap};
   const uint64_t a_str[1] = {(uint64_t)N * 2};
@@ -337,16 +521,62 @@ cudaError_t launch_gemm2_scatter(int dtype, const void* act, int64_t rows_cap, c
   const int NB = (int)ceil_div(K, BN);
   if (dtype == MOE_DTYPE_BF16) {
     if (BN == 256)
-      return launch_gemm_t<__nv_bfloat16, MODE_GEMM2, 256>(ma, mbm, block_start, E, N, K, NB, rows_cap, y_slots,
-                                                           sorted_pairs, status, max_ctas, st);
-    return launch_gemm_t<__nv_bfloat16, MODE_GEMM2, 128>(ma, mbm, block_start, E, N, K, NB, rows_cap, y_slots,
-                                                         sorted_pairs, status, max_ctas, st);
+      return launch_gemm_t<__nv_bfloat16, MODE, 256>(ma, mbm, block_start, E, N, K, NB, rows_cap, y_slots,
+                                                     sorted_pairs, status, max_ctas, st, cmb);
+    return launch_gemm_t<__nv_bfloat16, MODE, 128>(ma, mbm, block_start, E, N, K, NB, rows_cap, y_slots,
+                                                   sorted_pairs, status, max_ctas, st, cmb);
   }
   if (BN == 256)
-    return launch_gemm_t<__half, MODE_GEMM2, 256>(ma, mbm, block_start, E, N, K, NB, rows_cap, y_slots, sorted_pairs,
-                                                  status, max_ctas, st);
-  return launch_gemm_t<__half, MODE_GEMM2, 128>(ma, mbm, block_start, E, N, K, NB, rows_cap, y_slots, sorted_pairs,
-                                                status, max_ctas, st);
+    return launch_gemm_t<__half, MODE, 256>(ma, mbm, block_start, E, N, K, NB, rows_cap, y_slots, sorted_pairs,
+                                            status, max_ctas, st, cmb);
+  return launch_gemm_t<__half, MODE, 128>(ma, mbm, block_start, E, N, K, NB, rows_cap, y_slots, sorted_pairs,
+                                          status, max_ctas, st, cmb);
+}
+
+}  // namespace
+
+cudaError_t launch_gemm1_gather(int dtype, const void* x, int64_t x_ld, int topk, const int32_t* sorted_pairs,
+                               int64_t rows_cap, const void* w1, int E, int K, int N, const int32_t* block_start,
+                               void* act, int* status, int max_ctas, cudaStream_t st) {
+  const int BN = (N % 128 == 0) ? 256 : 128;
+  const int BH = BN / 2;
+  CUtensorMap mbm;
+  const uint64_t b_dims[3] = {(uint64_t)K, (uint64_t)N, (uint64_t)2 * E};
+  const uint64_t b_str[2] = {(uint64_t)K * 2, (uint64_t)N * K * 2};
+  if (!make_kmajor_map(&mbm, dtype, w1, 3, b_dims, b_str, (uint32_t)BH)) return cudaErrorInvalidValue;
+  const int NB = N / BH;
+  const RowGather gat{x, x_ld, topk};
+  // the A map is unused in this mode (the rows are gathered); the B map fills its slot
+  if (dtype == MOE_DTYPE_BF16) {
+    if (BN == 256)
+      return launch_gemm_t<__nv_bfloat16, MODE_GEMM1_GATHER, 256>(mbm, mbm, block_start, E, K, N, NB, rows_cap, act,
+                                                                  sorted_pairs, status, max_ctas, st, CombineArgs{},
+                                                                  gat);
+    return launch_gemm_t<__nv_bfloat16, MODE_GEMM1_GATHER, 128>(mbm, mbm, block_start, E, K, N, NB, rows_cap, act,
+                                                                sorted_pairs, status, max_ctas, st, CombineArgs{}, gat);
+  }
+  if (BN == 256)
+    return launch_gemm_t<__half, MODE_GEMM1_GATHER, 256>(mbm, mbm, block_start, E, K, N, NB, rows_cap, act,
+                                                         sorted_pairs, status, max_ctas, st, CombineArgs{}, gat);
+  return launch_gemm_t<__half, MODE_GEMM1_GATHER, 128>(mbm, mbm, block_start, E, K, N, NB, rows_cap, act, sorted_pairs,
+                                                       status, max_ctas, st, CombineArgs{}, gat);
+}
+
+cudaError_t launch_gemm2_scatter(int dtype, const void* act, int64_t rows_cap, const void* w2, int E, int K, int N,
+                                 const int32_t* block_start, const int32_t* sorted_pairs, int64_t num_pairs,
+                                 void* y_slots, int* status, int max_ctas, cudaStream_t st) {
+  (void)num_pairs;
+  return launch_gemm2_mode<MODE_GEMM2>(dtype, act, rows_cap, w2, E, K, N, block_start, sorted_pairs, y_slots, status,
+                                       max_ctas, st, CombineArgs{});
+}
+
+cudaError_t launch_gemm2_combine(int dtype, const void* act, int64_t rows_cap, const void* w2, int E, int K, int N,
+                                 const int32_t* block_start, const int32_t* sorted_pairs, void* y_slots,
+                                 const float* topk_weights, const int32_t* topk_ids, int topk, int32_t* arrivals,
+                                 void* out, int* status, int max_ctas, cudaStream_t st) {
+  const CombineArgs cmb{topk_ids, topk_weights, arrivals, out, topk};
+  return launch_gemm2_mode<MODE_GEMM2_COMBINE>(dtype, act, rows_cap, w2, E, K, N, block_start, sorted_pairs, y_slots,
+                                               status, max_ctas, st, cmb);
 }
 
 }  // namespace moe

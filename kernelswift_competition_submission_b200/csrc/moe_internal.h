@@ -27,9 +27,10 @@ inline AlignMeta align_meta_contiguous(int32_t* meta, int E) {
 // Launches the align stage. When x_src != nullptr the scatter also copies each
 // pair's token row of `row_bytes` bytes from x_src into x_sorted at the pair's
 // padded row (x_sorted row pitch = row_bytes).
+// zero_meta = false: the caller has zeroed counts, cursor and done on `st` already.
 cudaError_t launch_align(const int32_t* topk_ids, int64_t num_pairs, int topk, int E, int block_m, AlignMeta m,
                          bool meta_contiguous, int32_t* sorted_pairs, int64_t sorted_capacity, const void* x_src,
-                         void* x_sorted, int64_t row_bytes, cudaStream_t st);
+                         void* x_sorted, int64_t row_bytes, cudaStream_t st, bool zero_meta = true);
 
 // Weighted sum over the topk slots: out[t] = sum_j w[t, j] * y[t * topk + j]   (elem = bf16 / fp16).
 // Slots whose expert id is outside [0, E) contribute nothing (as in the reference's expert loop).
@@ -42,9 +43,34 @@ cudaError_t launch_combine(int dtype, const void* y_slots, const float* topk_wei
 // max_ctas: persistent grid size limit (0 = one CTA per SM).
 cudaError_t launch_gemm1_silu(int dtype, const void* x_sorted, int64_t rows_cap, const void* w1, int E, int K, int N,
                               const int32_t* block_start, void* act, int* status, int max_ctas, cudaStream_t st);
+// GEMM1 with its A rows gathered from the token rows (x, row pitch x_ld elements): row r
+// of the expert-sorted order is token sorted_pairs[r] / topk, padding rows (-1) are zeros.
+// No expert-sorted copy of the tokens is needed.
+cudaError_t launch_gemm1_gather(int dtype, const void* x, int64_t x_ld, int topk, const int32_t* sorted_pairs,
+                               int64_t rows_cap, const void* w1, int E, int K, int N, const int32_t* block_start,
+                               void* act, int* status, int max_ctas, cudaStream_t st);
 cudaError_t launch_gemm2_scatter(int dtype, const void* act, int64_t rows_cap, const void* w2, int E, int K, int N,
                                  const int32_t* block_start, const int32_t* sorted_pairs, int64_t num_pairs,
                                  void* y_slots, int* status, int max_ctas, cudaStream_t st);
+
+// Down GEMM with the top-k combine fused into its epilogue: slot rows go to y_slots
+// ([M * topk, K], as launch_gemm2_scatter), and the warp that stores a token's last
+// valid slot of an n-block writes out[t, n-block] = sum_j topk_weights[t, j] * y[t*topk+j]
+// (fp32, slot order: the bits of launch_combine). arrivals [M, ceil(K / gemm2_block_n(K))]
+// must be zero: launch_combine_prep does that and writes the rows of tokens without a
+// valid slot.
+int gemm2_block_n(int K);
+cudaError_t launch_gemm2_combine(int dtype, const void* act, int64_t rows_cap, const void* w2, int E, int K, int N,
+                                 const int32_t* block_start, const int32_t* sorted_pairs, void* y_slots,
+                                 const float* topk_weights, const int32_t* topk_ids, int topk, int32_t* arrivals,
+                                 void* out, int* status, int max_ctas, cudaStream_t st);
+cudaError_t launch_combine_prep(const int32_t* topk_ids, int64_t M, int topk, int E, int K, int32_t* arrivals,
+                                int64_t n_arrivals, int32_t* zero_ints, int n_zero, void* out, cudaStream_t st);
+
+// out[t] = sum over d with tok_rows[t, d] >= 0 of back[tok_rows[t, d]] (fp32); when `status`
+// is non-null and holds a failure code, every output element is NaN instead.
+cudaError_t launch_ep_combine(int dtype, const void* back, const int32_t* tok_rows, int64_t M, int K, int world,
+                              void* out, const int* status, cudaStream_t st);
 
 bool make_kmajor_map(CUtensorMap* m, int dtype, const void* base, int rank, const uint64_t* dims,
                      const uint64_t* strides_bytes, uint32_t box_rows);

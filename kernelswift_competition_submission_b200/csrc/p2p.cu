@@ -24,6 +24,13 @@
 //      rank at the row the source wrote it; the last CTA sets back[me] = s there.
 //   5. wait back[*] = s; the source sums its token's returned rows (moe_ep_combine).
 // No NCCL and no host synchronisation on the data path; no multicast objects.
+//
+// Failure: a wait that gives up records MOE_ERR_TIMEOUT in the caller's status word.
+// Every kernel here reads that word first and, once it is set, does nothing: no waits,
+// no stores into other ranks' arenas, no flags. A rank that timed out therefore goes
+// quiet, the ranks waiting on it time out in turn, and moe_p2p_reduce writes NaN rows
+// instead of summing a step whose rows never arrived. The host learns of it from the
+// status word and rebuilds the arenas (collectively) before the next step.
 #include "common.cuh"
 #include "moe_internal.h"
 
@@ -67,6 +74,11 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 // seq numbers wrap modulo 2^32: "reached" means no more than 2^31 behind
 __device__ __forceinline__ bool reached(uint32_t v, uint32_t seq) { return (int32_t)(v - seq) >= 0; }
 
+// Set once a wait of this rank gave up (or any earlier failure was recorded).
+__device__ __forceinline__ bool failed(const int* status) {
+  return status != nullptr && *reinterpret_cast<const volatile int*>(status) != 0;
+}
+
 // Bounded wait (thread-level) until flags[0..world) have all reached seq.
 __device__ bool wait_flags(const uint32_t* flags, int world, uint32_t seq, int* status) {
   const uint64_t t0 = globaltimer_ns();
@@ -83,16 +95,16 @@ __device__ bool wait_flags(const uint32_t* flags, int world, uint32_t seq, int* 
 }
 
 __global__ void p2p_signal_kernel(const int64_t* __restrict__ peer_base, int world, int me, int64_t flag_off,
-                                  uint32_t seq) {
+                                  uint32_t seq, const int* status) {
   const int d = threadIdx.x;
-  if (d < world) {
+  if (d < world && !failed(status)) {
     __threadfence_system();
     st_release_sys(reinterpret_cast<uint32_t*>(peer_base[d] + flag_off) + me, seq);
   }
 }
 
 __global__ void p2p_wait_kernel(const uint32_t* flags, int world, uint32_t seq, int* status) {
-  if (threadIdx.x == 0) wait_flags(flags, world, seq, status);
+  if (threadIdx.x == 0 && !failed(status)) wait_flags(flags, world, seq, status);
 }
 
 // scratch: [world] rows claimed this step | [world] rows used last step | [1] CTAs done
@@ -105,10 +117,11 @@ p2p_dispatch_kernel(const uint4* __restrict__ x, const int32_t* __restrict__ ids
   int32_t* claimed = scratch;
   int32_t* used = scratch + world;
   int32_t* done = scratch + 2 * world;
-  if (threadIdx.x == 0) s_go = wait_flags(own_ready, world, seq, status) ? 1 : 0;
+  if (threadIdx.x == 0) s_go = (!failed(status) && wait_flags(own_ready, world, seq, status)) ? 1 : 0;
   __syncthreads();
+  if (!s_go) return;  // failed: touch no arena and raise no flag (the step's output becomes NaN)
   const int lane = threadIdx.x & 31;
-  if (s_go) {
+  {
     for (int64_t t = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; t < M;
          t += ((int64_t)gridDim.x * blockDim.x) >> 5) {
       uint64_t mask = 0;
@@ -159,7 +172,7 @@ p2p_dispatch_kernel(const uint4* __restrict__ x, const int32_t* __restrict__ ids
     const int d = threadIdx.x;
     const int n = __ldcg(claimed + d);
     char* base = reinterpret_cast<char*>(peer_base[d]);
-    reinterpret_cast<volatile int32_t*>(base + lay.counts)[me] = s_go ? n : 0;
+    reinterpret_cast<volatile int32_t*>(base + lay.counts)[me] = n;
     used[d] = n;
     claimed[d] = 0;
     __threadfence_system();
@@ -173,8 +186,9 @@ p2p_dispatch_kernel(const uint4* __restrict__ x, const int32_t* __restrict__ ids
 __global__ void __launch_bounds__(kP2PThreads)
 p2p_combine_back_kernel(const uint4* __restrict__ partial, int K, int world, int me, int64_t cap,
                         const int64_t* __restrict__ peer_base, P2PLayout lay, const int32_t* own_counts,
-                        uint32_t seq, int32_t* done) {
+                        uint32_t seq, int32_t* done, const int* status) {
   __shared__ int s_last;
+  if (failed(status)) return;
   const int lane = threadIdx.x & 31;
   const int64_t row_vecs = (int64_t)K * 2 / 16;
   for (int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < (int64_t)world * cap;
@@ -213,9 +227,10 @@ __global__ void __launch_bounds__(kP2PThreads)
 p2p_combine_experts_back_kernel(const uint4* __restrict__ y, const float* __restrict__ w,
                                 const int32_t* __restrict__ ids, int E, int topk, int vpr, int world, int me,
                                 int64_t cap, const int64_t* __restrict__ peer_base, P2PLayout lay,
-                                const int32_t* own_counts, uint32_t seq, int32_t* done) {
+                                const int32_t* own_counts, uint32_t seq, int32_t* done, const int* status) {
   __shared__ int s_last;
   __shared__ int s_cnt[kP2PMaxWorld];
+  if (failed(status)) return;
   for (int i = threadIdx.x; i < world; i += blockDim.x) s_cnt[i] = __ldcg(own_counts + i);
   __syncthreads();
   const int64_t total = (int64_t)world * cap * vpr;
@@ -295,13 +310,16 @@ extern "C" int moe_p2p_arena_offsets(int world, int64_t cap, int hidden_size, in
   return MOE_OK;
 }
 
-extern "C" int moe_p2p_alloc(size_t bytes, void** base, void* ipc_handle) {
-  if (!bytes || !base || !ipc_handle) return MOE_ERR_INVALID_ARG;
+extern "C" int moe_p2p_alloc(int world, int64_t cap, int hidden_size, int topk, void** base, void* ipc_handle) {
+  using namespace moe;
+  if (!p2p_ok(world, 0, cap, hidden_size, topk) || !base || !ipc_handle) return MOE_ERR_INVALID_ARG;
+  const P2PLayout l = p2p_layout(world, cap, hidden_size, topk);
   void* p = nullptr;
-  if (cudaMalloc(&p, bytes) != cudaSuccess) return MOE_ERR_CUDA;
-  // flags and counts zero; id rows -1 (no token)
-  if (cudaMemset(p, 0, 1024) != cudaSuccess || cudaMemset(static_cast<char*>(p) + 1024, 0xFF, bytes - 1024) !=
-                                                    cudaSuccess) {
+  if (cudaMalloc(&p, (size_t)l.total) != cudaSuccess) return MOE_ERR_CUDA;
+  // flags and counts [0, recv_x) zero; everything after it 0xFF: id rows -1 (no token)
+  if (cudaMemset(p, 0, (size_t)l.recv_x) != cudaSuccess ||
+      cudaMemset(static_cast<char*>(p) + l.recv_x, 0xFF, (size_t)(l.total - l.recv_x)) != cudaSuccess ||
+      cudaDeviceSynchronize() != cudaSuccess) {
     cudaFree(p);
     return MOE_ERR_CUDA;
   }
@@ -330,12 +348,12 @@ extern "C" int moe_p2p_close(void* base) {
 extern "C" int moe_p2p_free(void* base) { return cudaFree(base) == cudaSuccess ? MOE_OK : MOE_ERR_CUDA; }
 
 extern "C" int moe_p2p_signal(const int64_t* peer_bases, int world, int me, int which, int64_t cap, int hidden_size,
-                              int topk, uint32_t seq, void* stream) {
+                              int topk, uint32_t seq, int* status, void* stream) {
   using namespace moe;
   if (!p2p_ok(world, me, cap, hidden_size, topk) || !peer_bases || which < 0 || which > 2) return MOE_ERR_INVALID_ARG;
   const P2PLayout l = p2p_layout(world, cap, hidden_size, topk);
   const int64_t off = which == 0 ? l.ready : which == 1 ? l.disp : l.back;
-  p2p_signal_kernel<<<1, 64, 0, static_cast<cudaStream_t>(stream)>>>(peer_bases, world, me, off, seq);
+  p2p_signal_kernel<<<1, 64, 0, static_cast<cudaStream_t>(stream)>>>(peer_bases, world, me, off, seq, status);
   return cudaGetLastError() == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
 }
 
@@ -379,7 +397,7 @@ extern "C" int moe_p2p_dispatch(int dtype, const void* hidden_states, const int3
 
 extern "C" int moe_p2p_combine_back(int dtype, const void* partial, int hidden_size, int topk, int world, int me,
                                     int64_t cap, const int64_t* peer_bases, const void* own_base, uint32_t seq,
-                                    int32_t* scratch, void* stream) {
+                                    int32_t* scratch, int* status, void* stream) {
   using namespace moe;
   if (dtype != MOE_DTYPE_BF16 && dtype != MOE_DTYPE_FP16) return MOE_ERR_UNSUPPORTED;
   if (!p2p_ok(world, me, cap, hidden_size, topk) || !partial || !peer_bases || !own_base || !scratch)
@@ -390,7 +408,8 @@ extern "C" int moe_p2p_combine_back(int dtype, const void* partial, int hidden_s
   const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div(rows * 32, kP2PThreads), 2 * num_sms()));
   const int32_t* own_counts = reinterpret_cast<const int32_t*>(static_cast<const char*>(own_base) + l.counts);
   p2p_combine_back_kernel<<<blocks, kP2PThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint4*>(partial), hidden_size, world, me, cap, peer_bases, l, own_counts, seq, scratch);
+      static_cast<const uint4*>(partial), hidden_size, world, me, cap, peer_bases, l, own_counts, seq, scratch,
+      status);
   return cudaGetLastError() == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
 }
 
@@ -408,7 +427,7 @@ extern "C" int moe_p2p_copy_recv_ids(const void* own_base, int world, int64_t ca
 extern "C" int moe_p2p_combine_experts_back(int dtype, const void* workspace, int num_experts, int hidden_size,
                                             int intermediate_size, int topk, int world, int me, int64_t cap,
                                             const int64_t* peer_bases, const void* own_base, uint32_t seq,
-                                            int32_t* scratch, void* stream) {
+                                            int32_t* scratch, int* status, void* stream) {
   using namespace moe;
   if (dtype != MOE_DTYPE_BF16 && dtype != MOE_DTYPE_FP16 && dtype != MOE_DTYPE_E4M3_ROW) return MOE_ERR_UNSUPPORTED;
   if (!p2p_ok(world, me, cap, hidden_size, topk) || num_experts <= 0 || intermediate_size <= 0 || !workspace ||
@@ -430,9 +449,25 @@ extern "C" int moe_p2p_combine_experts_back(int dtype, const void* workspace, in
   const int32_t* cnt = reinterpret_cast<const int32_t*>(ob + l.counts);
   if (dtype != MOE_DTYPE_FP16)
     p2p_combine_experts_back_kernel<__nv_bfloat16><<<blocks, kP2PThreads, 0, st>>>(
-        y, w, ids, num_experts, topk, vpr, world, me, cap, peer_bases, l, cnt, seq, scratch);
+        y, w, ids, num_experts, topk, vpr, world, me, cap, peer_bases, l, cnt, seq, scratch, status);
   else
     p2p_combine_experts_back_kernel<__half><<<blocks, kP2PThreads, 0, st>>>(
-        y, w, ids, num_experts, topk, vpr, world, me, cap, peer_bases, l, cnt, seq, scratch);
+        y, w, ids, num_experts, topk, vpr, world, me, cap, peer_bases, l, cnt, seq, scratch, status);
   return cudaGetLastError() == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
+}
+
+extern "C" int moe_p2p_reduce(int dtype, const void* own_base, const int32_t* tok_rows, int64_t num_tokens,
+                              int hidden_size, int topk, int world, int64_t cap, void* out, const int* status,
+                              void* stream) {
+  using namespace moe;
+  if (dtype != MOE_DTYPE_BF16 && dtype != MOE_DTYPE_FP16) return MOE_ERR_UNSUPPORTED;
+  if (!p2p_ok(world, 0, cap, hidden_size, topk) || num_tokens < 0 || num_tokens > cap || !own_base ||
+      (num_tokens > 0 && (!tok_rows || !out)))
+    return MOE_ERR_INVALID_ARG;
+  if (reinterpret_cast<uintptr_t>(out) & 15u) return MOE_ERR_INVALID_ARG;
+  const P2PLayout l = p2p_layout(world, cap, hidden_size, topk);
+  return launch_ep_combine(dtype, static_cast<const char*>(own_base) + l.back_x, tok_rows, num_tokens, hidden_size,
+                           world, out, status, static_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? MOE_OK
+             : MOE_ERR_CUDA;
 }

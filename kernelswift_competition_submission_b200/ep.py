@@ -163,6 +163,10 @@ class ExpertParallelMoE:
         self.transport = transport
         self.max_tokens = max_tokens  # p2p arena size in tokens per rank (default: the first batch, max over ranks)
         self._p2p = None
+        # p2p failure detection: each forward ends with an asynchronous copy of the device
+        # status word to pinned host memory; a later forward reads it once that copy is done
+        self._p2p_status = None      # (pinned host int32 [1], event) of the last forward
+        self._p2p_failed = 0         # failure code seen; sticky until reset_transport()
 
     @property
     def kernel_launches_per_step(self):
@@ -561,8 +565,8 @@ class ExpertParallelMoE:
             raise ValueError("p2p transport: unsupported shape")
         base = ctypes.c_void_p()
         handle = ctypes.create_string_buffer(64)
-        _lib.check(lib.moe_p2p_alloc(nbytes, ctypes.cast(ctypes.pointer(base), ctypes.c_void_p), handle),
-                   "moe_p2p_alloc")
+        _lib.check(lib.moe_p2p_alloc(self.world, cap, K, self.topk, ctypes.cast(ctypes.pointer(base), ctypes.c_void_p),
+                                     handle), "moe_p2p_alloc")
         handles = [None] * self.world
         dist.all_gather_object(handles, bytes(handle.raw), group=self.group)
         bases = []
@@ -600,10 +604,49 @@ class ExpertParallelMoE:
         lib.moe_p2p_free(ctypes.c_void_p(self._p2p["base"]))
         self._p2p = None
 
+    # ------------------------------------------------------------------ p2p failure handling
+    def _p2p_raise_if_failed(self, block=False):
+        """Raise once a peer-memory step of this rank recorded a device-side failure (a wait
+        that gave up after its 2 s limit). Reads the host copy of the status word that the
+        last forward queued; with ``block`` it waits for that copy, otherwise a copy still in
+        flight is left for a later call. The failure is sticky until ``reset_transport()``."""
+        if not self._p2p_failed and self._p2p_status is not None:
+            host, ev = self._p2p_status
+            if block:
+                ev.synchronize()
+            if ev.query() and int(host[0]):
+                self._p2p_failed = int(host[0])
+        if self._p2p_failed:
+            from . import _lib
+
+            raise RuntimeError(
+                f"expert-parallel peer-memory transport failed on rank {self.rank}: "
+                f"{_lib.status_string(self._p2p_failed)}; the steps since then returned NaN rows. "
+                "Call reset_transport() on every rank to rebuild the arenas.")
+
+    def check_transport(self):
+        """Synchronise with this rank's last peer-memory step and raise if it failed."""
+        self._p2p_raise_if_failed(block=True)
+
+    def reset_transport(self):
+        """Collective (every rank): after a peer-memory failure, zero the status word, unmap
+        and free the arenas; the next forward allocates and exchanges new ones."""
+        from .ops import status_word
+
+        if self._p2p is None and not self._p2p_failed:
+            return
+        torch.cuda.synchronize()
+        dev = torch.device("cuda", torch.cuda.current_device())
+        status_word(dev).zero_()
+        self._p2p_failed = 0
+        self._p2p_status = None
+        self._p2p_release()
+
     def _forward_p2p(self, x, gating):
         from . import _lib
         from .ops import _DTYPES, _ptr, _stream, status_word
 
+        self._p2p_raise_if_failed()
         M, K = x.shape
         dev = x.device
         p = self._p2p
@@ -633,7 +676,7 @@ class ExpertParallelMoE:
         tok_rows = self._buf("p2p_tr", max(M, 1), W, torch.int32, dev)[: max(M, 1)]
         pb = _ptr(p["peer_bases"])
         base = p["base"]
-        _lib.check(lib.moe_p2p_signal(pb, W, self.rank, 0, cap, K, k, seq, st), "moe_p2p_signal")
+        _lib.check(lib.moe_p2p_signal(pb, W, self.rank, 0, cap, K, k, seq, status, st), "moe_p2p_signal")
         _lib.check(lib.moe_p2p_dispatch(dt_rows, _ptr(xc), _ptr(ids32), _ptr(w32), M, K, k, self.E_local, W, self.rank,
                                         cap, pb, base, seq, _ptr(p["scr_d"]), _ptr(tok_rows), status, st),
                    "moe_p2p_dispatch")
@@ -668,14 +711,20 @@ class ExpertParallelMoE:
         self._mark("experts")
         # top-k combine of each valid received row, stored straight into its source's arena
         _lib.check(lib.moe_p2p_combine_experts_back(dt_rows, ws, E_l, K, N, k, W, self.rank, cap, pb, base, seq,
-                                                    _ptr(p["scr_c"]), st), "moe_p2p_combine_experts_back")
+                                                    _ptr(p["scr_c"]), status, st), "moe_p2p_combine_experts_back")
         _lib.check(lib.moe_p2p_wait(base, W, 2, cap, K, k, seq, status, st), "moe_p2p_wait")
         self._mark("combine_back")
         out = torch.empty(M, K, dtype=x.dtype, device=dev)
-        if M:
-            _lib.check(lib.moe_ep_combine(dt, ctypes.c_void_p(base + o[7]), _ptr(tok_rows), M, K, W, _ptr(out), st),
-                       "moe_ep_combine")
+        if M:  # NaN rows if any wait of this step gave up
+            _lib.check(lib.moe_p2p_reduce(dt, base, _ptr(tok_rows), M, K, k, W, cap, _ptr(out), status, st),
+                       "moe_p2p_reduce")
         self._mark("reduce")
+        # the status word, copied to the host behind this step (read by a later forward)
+        if self._p2p_status is None:
+            self._p2p_status = (torch.zeros(1, dtype=torch.int32).pin_memory(), torch.cuda.Event())
+        host, ev = self._p2p_status
+        host.copy_(status_word(dev), non_blocking=True)
+        ev.record()
         if self.profile and self._marks:
             self.phase_log.append(self._marks)
         return out

@@ -7,8 +7,11 @@ set of input tensors (shapes, dtypes, devices and data pointers), captures the
 same call into a CUDA graph right after, and from then on replays the graph:
 one launch. The replay reads whatever the input buffers hold at that moment,
 so new values in the same tensors give new results; any other tensor (a new
-pointer, shape or dtype) takes the eager path again and re-captures. The
-returned tensor is the graph's own output buffer, rewritten by every replay.
+pointer, shape or dtype) takes the eager path again and re-captures. Every call
+returns new tensors, as the reference's ``ModelNew`` does
+(``fused_moe/v1/fused_moe.py:320-341``): a replay copies the graph's own output
+buffers, which the next replay rewrites, into fresh ones (one device copy per
+output), so a result held by the caller never changes under a later call.
 """
 
 from __future__ import annotations
@@ -16,6 +19,12 @@ from __future__ import annotations
 from typing import Callable
 
 import torch
+
+
+def _fresh(out):
+    if isinstance(out, torch.Tensor):
+        return out.clone()
+    return type(out)(_fresh(o) for o in out)
 
 
 class GraphCache:
@@ -38,7 +47,7 @@ class GraphCache:
         if key == self._key and self._graph is not None:
             self._graph.replay()
             self.replays += 1
-            return self._out
+            return _fresh(self._out)
         out = self.fn(*args)  # eager: this call's result, and warm-up of every lazy setup
         dev = next(t.device for t in args if isinstance(t, torch.Tensor))
         side = torch.cuda.Stream(device=dev)

@@ -239,37 +239,56 @@ def fused_moe(
             raise ValueError("use_fp8_w8a8 needs w1_scale and w2_scale")
         return fused_moe_fp8(hidden_states, w1, w1_scale, w2, w2_scale, topk_weights, topk_ids, out=out,
                              workspace=workspace)
-    dev = _require_cuda("fused_moe", hidden_states, w1, w2, topk_weights, topk_ids)
+    a = _expert_args("fused_moe", hidden_states, w1, w2, topk_weights, topk_ids, out, workspace)
+    _lib.check(
+        a.lib.moe_fused_experts(a.dt, _ptr(a.x), _ptr(a.w1), _ptr(a.w2), _ptr(a.tw), _ptr(a.ti), a.M, a.E, a.k, a.K,
+                                a.N, _ptr(a.out), _ptr(a.ws), a.ws.numel(), _ptr(status_word(a.dev)), _stream(a.dev)),
+        "moe_fused_experts")
+    return a.out
+
+
+class _ExpertArgs:
+    __slots__ = ("dev", "dt", "x", "w1", "w2", "tw", "ti", "out", "ws", "M", "E", "k", "K", "N", "lib")
+
+
+def _expert_args(name, hidden_states, w1, w2, topk_weights, topk_ids, out, workspace):
+    """Checks of the bf16 / fp16 expert path (same errors for every entry point), contiguous
+    operands, the output and a workspace of at least moe_fused_workspace_bytes."""
+    a = _ExpertArgs()
+    a.dev = _require_cuda(name, hidden_states, w1, w2, topk_weights, topk_ids)
     dt = hidden_states.dtype
     if dt not in _DTYPES:
-        raise TypeError(f"fused_moe: hidden_states dtype {dt} not supported (bf16 or fp16)")
+        raise TypeError(f"{name}: hidden_states dtype {dt} not supported (bf16 or fp16)")
     if w1.dtype != dt or w2.dtype != dt:
-        raise TypeError("fused_moe: w1/w2 must have the dtype of hidden_states")
+        raise TypeError(f"{name}: w1/w2 must have the dtype of hidden_states")
+    if hidden_states.dim() != 2 or w1.dim() != 3 or topk_ids.dim() != 2:
+        raise ValueError(f"{name}: hidden_states [M, K], w1 [E, 2N, K], w2 [E, K, N], topk_ids [M, topk]")
     M, K = hidden_states.shape
     E, twoN, K1 = w1.shape
     N = twoN // 2
     if K1 != K or tuple(w2.shape) != (E, K, N) or twoN != 2 * N:
-        raise ValueError(f"fused_moe: shape mismatch x{tuple(hidden_states.shape)} w1{tuple(w1.shape)} "
+        raise ValueError(f"{name}: shape mismatch x{tuple(hidden_states.shape)} w1{tuple(w1.shape)} "
                          f"w2{tuple(w2.shape)}")
     k = topk_ids.shape[1]
     if tuple(topk_weights.shape) != (M, k) or topk_ids.shape[0] != M:
-        raise ValueError("fused_moe: topk_weights / topk_ids must be [M, topk]")
-    x = hidden_states.contiguous()
-    w1c = w1.contiguous()
-    w2c = w2.contiguous()
-    tw = topk_weights.to(torch.float32).contiguous()
-    ti = topk_ids.to(torch.int32).contiguous()
+        raise ValueError(f"{name}: topk_weights / topk_ids must be [M, topk]")
+    a.dt, a.M, a.E, a.k, a.K, a.N = _DTYPES[dt], M, E, k, K, N
+    a.x = hidden_states.contiguous()
+    a.w1 = w1.contiguous()
+    a.w2 = w2.contiguous()
+    a.tw = topk_weights.to(torch.float32).contiguous()
+    a.ti = topk_ids.to(torch.int32).contiguous()
     if out is None:
-        out = torch.empty(M, K, dtype=dt, device=dev)
-    lib = _lib.load()
-    need = int(lib.moe_fused_workspace_bytes(M, E, k, K, N))
+        out = torch.empty(M, K, dtype=dt, device=a.dev)
+    elif tuple(out.shape) != (M, K) or out.dtype != dt or not out.is_contiguous() or out.device != a.dev:
+        raise ValueError(f"{name}: out must be a contiguous {dt} [{M}, {K}] tensor on {a.dev}")
+    a.out = out
+    a.lib = _lib.load()
+    need = int(a.lib.moe_fused_workspace_bytes(M, E, k, K, N))
     if workspace is None or workspace.numel() < need:
-        workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=dev)
-    _lib.check(
-        lib.moe_fused_experts(_DTYPES[dt], _ptr(x), _ptr(w1c), _ptr(w2c), _ptr(tw), _ptr(ti), M, E, k, K, N,
-                              _ptr(out), _ptr(workspace), workspace.numel(), _ptr(status_word(dev)), _stream(dev)),
-        "moe_fused_experts")
-    return out
+        workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=a.dev)
+    a.ws = workspace
+    return a
 
 
 def _fp8_bytes(t: torch.Tensor) -> torch.Tensor:
@@ -407,7 +426,9 @@ def fused_moe_fp8_rows(rows, hidden_size, w1_q, w1_scale, w2_q, w2_scale, topk_w
 
 def fused_moe_staged(hidden_states, w1, w2, topk_weights, topk_ids, *, out=None, workspace=None, events=None,
                      max_ctas=0):
-    """``fused_moe`` issued as its four C-ABI stages (same kernels, same order).
+    """``fused_moe`` issued as its four C-ABI stages (align + row gather, gate/up GEMM,
+    down GEMM, top-k combine): the same kernels in the same order, the same argument
+    checks and the same bits as ``fused_moe``.
 
     ``events``: optional list of 5 ``torch.cuda.Event`` recorded on the current
     stream before align, before GEMM1, before GEMM2, before combine and after
@@ -415,40 +436,28 @@ def fused_moe_staged(hidden_states, w1, w2, topk_weights, topk_ids, *, out=None,
     ``max_ctas`` limits the persistent GEMM grids (0 = one CTA per SM), leaving
     SMs for work on other streams such as overlapping collectives.
     """
-    dev = _require_cuda("fused_moe_staged", hidden_states, w1, w2, topk_weights, topk_ids)
-    dt = _DTYPES[hidden_states.dtype]
-    M, K = hidden_states.shape
-    E, twoN, _ = w1.shape
-    N = twoN // 2
-    k = topk_ids.shape[1]
-    lib = _lib.load()
-    need = int(lib.moe_fused_workspace_bytes(M, E, k, K, N))
-    if workspace is None or workspace.numel() < need:
-        workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=dev)
-    if out is None:
-        out = torch.empty(M, K, dtype=hidden_states.dtype, device=dev)
-    st = _stream(dev)
-    ws, wsn, status = _ptr(workspace), workspace.numel(), _ptr(status_word(dev))
-    tw = topk_weights.to(torch.float32).contiguous()
-    ti = topk_ids.to(torch.int32).contiguous()
+    a = _expert_args("fused_moe_staged", hidden_states, w1, w2, topk_weights, topk_ids, out, workspace)
+    lib, dt, M, E, k, K, N = a.lib, a.dt, a.M, a.E, a.k, a.K, a.N
+    st = _stream(a.dev)
+    ws, wsn, status = _ptr(a.ws), a.ws.numel(), _ptr(status_word(a.dev))
     ev = events or [None] * 5
     if ev[0] is not None:
         ev[0].record()
-    _lib.check(lib.moe_expert_align_gather(dt, _ptr(hidden_states), _ptr(ti), M, E, k, K, N, ws, wsn, st),
+    _lib.check(lib.moe_expert_align_gather(dt, _ptr(a.x), _ptr(a.ti), M, E, k, K, N, ws, wsn, st),
                "moe_expert_align_gather")
     if ev[1] is not None:
         ev[1].record()
-    _lib.check(lib.moe_expert_gemm1(dt, _ptr(w1), M, E, k, K, N, ws, wsn, status, max_ctas, st), "moe_expert_gemm1")
+    _lib.check(lib.moe_expert_gemm1(dt, _ptr(a.w1), M, E, k, K, N, ws, wsn, status, max_ctas, st), "moe_expert_gemm1")
     if ev[2] is not None:
         ev[2].record()
-    _lib.check(lib.moe_expert_gemm2(dt, _ptr(w2), M, E, k, K, N, ws, wsn, status, max_ctas, st), "moe_expert_gemm2")
+    _lib.check(lib.moe_expert_gemm2(dt, _ptr(a.w2), M, E, k, K, N, ws, wsn, status, max_ctas, st), "moe_expert_gemm2")
     if ev[3] is not None:
         ev[3].record()
-    _lib.check(lib.moe_expert_combine(dt, _ptr(tw), _ptr(ti), M, E, k, K, N, _ptr(out), ws, wsn, st),
+    _lib.check(lib.moe_expert_combine(dt, _ptr(a.tw), _ptr(a.ti), M, E, k, K, N, _ptr(a.out), ws, wsn, st),
                "moe_expert_combine")
     if ev[4] is not None:
         ev[4].record()
-    return out
+    return a.out
 
 
 def moe_layer(hidden_states, gating_output, w1, w2, *, topk, renormalize=True, num_expert_group=1, topk_group=1,

@@ -49,3 +49,35 @@ def test_grouped_topk_task_replay(cuda_device):
     w2, i2 = (t.clone() for t in model(h, g))
     we, ie = model._forward_eager(h, g)
     assert torch.equal(i2, ie) and torch.equal(w2, we)
+
+
+def test_replay_returns_fresh_tensors(cuda_device):
+    """A result held across a later call (same buffers, new values) keeps its values, as the
+    reference's ModelNew, which allocates its output on every call."""
+    m = _task("fused_moe")
+    model = m.ModelNew(*m.get_init_inputs()).to(cuda_device)
+    gen = torch.Generator(device=cuda_device).manual_seed(5)
+    x = torch.randn(83, 128, generator=gen, device=cuda_device).half()
+    g = torch.randn(83, 8, generator=gen, device=cuda_device)
+    with torch.no_grad():
+        model(x, g)                      # eager + capture
+        a = model(x, g)                  # replay
+        keep = a.clone()
+        x.mul_(2.0)
+        b = model(x, g)                  # replay on new values
+        assert model._graph.replays == 2
+        assert torch.equal(a, keep)
+        assert a.data_ptr() != b.data_ptr()
+        assert not torch.equal(a, b)
+    t = _task("grouped_topk")
+    router = t.ModelNew(8, True, 8, 4, "softmax", 1.0)
+    h = torch.randn(83, 16, generator=gen, device=cuda_device).half()
+    lg = torch.randn(83, 256, generator=gen, device=cuda_device)
+    router(h, lg)
+    w0, i0 = router(h, lg)
+    keep_w, keep_i = w0.clone(), i0.clone()
+    lg.copy_(torch.randn(83, 256, generator=gen, device=cuda_device))
+    w1, i1 = router(h, lg)
+    assert router._graph.replays == 2
+    assert torch.equal(w0, keep_w) and torch.equal(i0, keep_i)
+    assert not torch.equal(i0, i1)

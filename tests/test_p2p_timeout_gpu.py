@@ -15,10 +15,10 @@ pytestmark = pytest.mark.gpu
 def test_unset_flag_times_out_with_status(cuda_device):
     lib = _lib.load()
     world, cap, K, k = 1, 4, 64, 2
-    nbytes = int(lib.moe_p2p_arena_bytes(world, cap, K, k))
     base = ctypes.c_void_p()
     handle = ctypes.create_string_buffer(64)
-    _lib.check(lib.moe_p2p_alloc(nbytes, ctypes.cast(ctypes.pointer(base), ctypes.c_void_p), handle), "alloc")
+    _lib.check(lib.moe_p2p_alloc(world, cap, K, k, ctypes.cast(ctypes.pointer(base), ctypes.c_void_p), handle),
+               "alloc")
     try:
         status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
         torch.cuda.synchronize()
