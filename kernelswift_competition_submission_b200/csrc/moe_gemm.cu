@@ -84,18 +84,16 @@ constexpr int kATileBytes = kBlockM * kBK * 2;
 constexpr int kEpiPitch = 144;
 constexpr int kEpiWarpBytes = 32 * kEpiPitch;
 
-// PAIR: a CTA holds half of each B tile (its peer holds the other half).
-template <int BN, int STAGES, bool PAIR>
+template <int BN, int STAGES>
 struct SmemLayout {
-  static constexpr int kBTileBytes = (PAIR ? BN / 2 : BN) * kBK * 2;
+  static constexpr int kBTileBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kATileBytes + kBTileBytes;
   static constexpr int kEpiOffset = STAGES * kStageBytes;
   static constexpr int kBarOffset = kEpiOffset + 4 * kEpiWarpBytes;
   static constexpr int kNumBars = 2 * STAGES + 5;
   static constexpr int kMiscOffset = kBarOffset + kNumBars * 8;
   static constexpr int kBlockStartOffset = kMiscOffset + 16;
-  // block_start [E + 1], and for PAIR the prefix of pair-blocks per expert [E + 1]
-  static int bytes(int E) { return 1024 + kBlockStartOffset + 4 * (E + 1) * (PAIR ? 2 : 1); }
+  static int bytes(int E) { return 1024 + kBlockStartOffset + 4 * (E + 1); }
 };
 
 __device__ __forceinline__ void decode_tile(const int* s_bs, int E, int NB, int tile, int& e, int& nb, int& mb) {
@@ -109,25 +107,6 @@ __device__ __forceinline__ void decode_tile(const int* s_bs, int E, int NB, int 
   const int local = tile - s_bs[lo] * NB;
   nb = local / nblk;
   mb = s_bs[lo] + (local - nb * nblk);
-}
-
-// CTA-pair tiles: expert e's m-blocks go in pairs, ceil(nblk / 2) pair-blocks per expert
-// (s_pp = their prefix over experts); CTA `cta` of the pair takes m-block
-// s_bs[e] + 2 * pp + cta, which is one of e's own rows only when below s_bs[e + 1] (an
-// odd block count leaves the second CTA's half of the last pair-block outside e: its
-// rows are computed with e's weights and dropped).
-__device__ __forceinline__ void decode_pair_tile(const int* s_bs, const int* s_pp, int E, int NB, int tile, int cta,
-                                                 int& e, int& nb, int& mb) {
-  int lo = 0, hi = E - 1;
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (s_pp[mid] * NB <= tile) lo = mid; else hi = mid - 1;
-  }
-  e = lo;
-  const int npp = s_pp[lo + 1] - s_pp[lo];
-  const int local = tile - s_pp[lo] * NB;
-  nb = local / npp;
-  mb = s_bs[lo] + 2 * (local - nb * npp) + cta;
 }
 
 // Arrival count and, for the rows whose arrival completes their token's n-block, the
@@ -220,23 +199,20 @@ __device__ __forceinline__ void combine_rows(const CombineArgs& cmb, const T* sl
   }
 }
 
-template <typename T, int MODE, int BN, int STAGES, bool PAIR>
+template <typename T, int MODE, int BN, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
 moe_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                 const int32_t* __restrict__ block_start, int E, int k_red, int n_out, int NB,
                 T* __restrict__ out, const int32_t* __restrict__ sorted_pairs, int* status, CombineArgs cmb,
                 RowGather gat) {
-  using L = SmemLayout<BN, STAGES, PAIR>;
+  using L = SmemLayout<BN, STAGES>;
   constexpr bool kGemm1 = MODE == MODE_GEMM1_SILU || MODE == MODE_GEMM1_GATHER;
   constexpr bool kGather = MODE == MODE_GEMM1_GATHER;
-  static_assert(!PAIR || MODE == MODE_GEMM1_SILU || MODE == MODE_GEMM2, "CTA pairs: TMA-fed GEMM1 / GEMM2 only");
-  constexpr int BH = kGemm1 ? BN / 2 : BN;   // rows per B box of the 1-CTA tile (GEMM1: gate, then up)
+  constexpr int BH = kGemm1 ? BN / 2 : BN;   // rows per B box
   constexpr uint32_t kTmemCols = 2 * BN;
-  // PAIR: one 256 x BN MMA over both CTAs (128 rows each; each CTA supplies BN / 2 B rows)
-  constexpr uint32_t kIdesc = idesc_f16(PAIR ? 2 * kBlockM : kBlockM, BN, ElemTraits<T>::kFmt);
-  // bytes the TMA delivers per stage: A and B (both CTAs' for a pair, counted on the
-  // leader's barrier), or B alone when the A rows are gathered
-  constexpr uint32_t kStageTx = kGather ? (uint32_t)L::kBTileBytes : (uint32_t)L::kStageBytes * (PAIR ? 2u : 1u);
+  constexpr uint32_t kIdesc = idesc_f16(kBlockM, BN, ElemTraits<T>::kFmt);
+  // bytes the TMA delivers per stage: A and B, or B alone when the A rows are gathered
+  constexpr uint32_t kStageTx = kGather ? (uint32_t)L::kBTileBytes : (uint32_t)L::kStageBytes;
   constexpr int kGatherLag = STAGES - 1;  // unannounced stages a gather thread keeps in flight
 
   extern __shared__ uint8_t smem_raw[];
@@ -250,18 +226,14 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + L::kMiscOffset);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + L::kMiscOffset + 4);
   int* s_bs = reinterpret_cast<int*>(smem + L::kBlockStartOffset);
-  int* s_pp = s_bs + (E + 1);  // PAIR only
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const uint32_t cta = PAIR ? cluster_ctarank() : 0u;  // 0 = the pair's leader
-  const bool leader = cta == 0;
 
   for (int i = threadIdx.x; i <= E; i += kThreads) s_bs[i] = __ldg(block_start + i);
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], kGather ? 1 + kGatherThreads : 1); mbar_init(&empty[s], 1); }
-    // tmem_empty: every epilogue thread (1 CTA), or one arrival per epilogue warp of both CTAs (pair)
-    for (int a = 0; a < 2; ++a) { mbar_init(&tmem_full[a], 1); mbar_init(&tmem_empty[a], PAIR ? 8 : 128); }
+    for (int a = 0; a < 2; ++a) { mbar_init(&tmem_full[a], 1); mbar_init(&tmem_empty[a], 128); }
     mbar_init(mma_done, 1);
     *s_abort = 0;
     fence_mbar_init();
@@ -270,47 +242,14 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
     if constexpr (!kGather) tma_prefetch_desc(&map_a);
     tma_prefetch_desc(&map_b);
   }
-  if constexpr (PAIR) {
-    if (warp == 2) { tmem_alloc_pair(s_tmem, kTmemCols); tmem_relinquish_pair(); }
-    __syncthreads();  // s_bs complete
-    if (warp == 3) {
-      // s_pp[e] = sum over e' < e of ceil((s_bs[e' + 1] - s_bs[e']) / 2); one warp, E <= 1024
-      const int per = (E + 31) / 32;
-      const int b = lane * per;
-      int local = 0;
-      for (int i = 0; i < per; ++i)
-        if (b + i < E) local += (s_bs[b + i + 1] - s_bs[b + i] + 1) >> 1;
-      int incl = local;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int v = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += v;
-      }
-      int run = incl - local;
-      for (int i = 0; i < per; ++i) {
-        if (b + i < E) {
-          s_pp[b + i] = run;
-          run += (s_bs[b + i + 1] - s_bs[b + i] + 1) >> 1;
-        }
-      }
-      if (lane == 31) s_pp[E] = incl;
-    }
-    tc_fence_before();
-    cluster_sync_all();  // barrier inits, TMEM address and tables visible in both CTAs
-    tc_fence_after();
-  } else {
-    if (warp == 2) { tmem_alloc(s_tmem, kTmemCols); tmem_relinquish(); }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-  }
+  if (warp == 2) { tmem_alloc(s_tmem, kTmemCols); tmem_relinquish(); }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
   const uint32_t tmem_base = *s_tmem;
 
-  const int total_tiles = PAIR ? s_pp[E] * NB : s_bs[E] * NB;
-  const int tile0 = PAIR ? (int)cluster_id_x() : (int)blockIdx.x;
-  const int tile_step = PAIR ? (int)num_clusters_x() : (int)gridDim.x;
+  const int total_tiles = s_bs[E] * NB;
   const int num_kb = (k_red + kBK - 1) / kBK;
-  bool producer_aborted = false;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -319,32 +258,20 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
       uint32_t phase = 0;
       uint32_t issued_mask = 0, issued_parity = 0;
       bool ok = true;
-      for (int tile = tile0; tile < total_tiles && ok; tile += tile_step) {
+      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
         int e, nb, mb;
-        if constexpr (PAIR) decode_pair_tile(s_bs, s_pp, E, NB, tile, (int)cta, e, nb, mb);
-        else decode_tile(s_bs, E, NB, tile, e, nb, mb);
+        decode_tile(s_bs, E, NB, tile, e, nb, mb);
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, status, s_abort)) { ok = false; break; }
           uint8_t* a_dst = smem + stage * L::kStageBytes;
           uint8_t* b_dst = a_dst + kATileBytes;
-          if constexpr (PAIR) {
-            // both CTAs' copies count on the leader's `full`; the leader arms it for both
-            const uint32_t full_leader = mapa_shared(&full[stage], 0);
-            if (leader) mbar_arrive_expect_tx(&full[stage], kStageTx);
-            tma_load_2d_pair(&map_a, full_leader, a_dst, kb * kBK, mb * kBlockM);
-            if constexpr (kGemm1)  // gate rows in the leader, the matching up rows in the peer
-              tma_load_3d_pair(&map_b, full_leader, b_dst, kb * kBK, nb * BH, 2 * e + (int)cta);
-            else
-              tma_load_3d_pair(&map_b, full_leader, b_dst, kb * kBK, nb * BN + (int)cta * (BN / 2), e);
+          mbar_arrive_expect_tx(&full[stage], kStageTx);
+          if constexpr (!kGather) tma_load_2d(&map_a, &full[stage], a_dst, kb * kBK, mb * kBlockM);
+          if constexpr (kGemm1) {
+            tma_load_3d(&map_b, &full[stage], b_dst, kb * kBK, nb * BH, 2 * e);
+            tma_load_3d(&map_b, &full[stage], b_dst + BH * kBK * 2, kb * kBK, nb * BH, 2 * e + 1);
           } else {
-            mbar_arrive_expect_tx(&full[stage], kStageTx);
-            if constexpr (!kGather) tma_load_2d(&map_a, &full[stage], a_dst, kb * kBK, mb * kBlockM);
-            if constexpr (kGemm1) {
-              tma_load_3d(&map_b, &full[stage], b_dst, kb * kBK, nb * BH, 2 * e);
-              tma_load_3d(&map_b, &full[stage], b_dst + BH * kBK * 2, kb * kBK, nb * BH, 2 * e + 1);
-            } else {
-              tma_load_3d(&map_b, &full[stage], b_dst, kb * kBK, nb * BN, e);
-            }
+            tma_load_3d(&map_b, &full[stage], b_dst, kb * kBK, nb * BN, e);
           }
           issued_mask |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
@@ -352,12 +279,9 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
         }
       }
       if (!ok) {
-        producer_aborted = true;
-        // drain: wait (bounded, ignoring the abort flag) for the last copy issued into each
-        // stage; a pair's copies all count on the leader's barriers, so only it can wait
-        if (leader)
-          for (int s = 0; s < STAGES; ++s)
-            if ((issued_mask >> s) & 1u) mbar_wait(&full[s], (issued_parity >> s) & 1u, nullptr, nullptr);
+        // drain: wait (bounded, ignoring the abort flag) for the last copy issued into each stage
+        for (int s = 0; s < STAGES; ++s)
+          if ((issued_mask >> s) & 1u) mbar_wait(&full[s], (issued_parity >> s) & 1u, nullptr, nullptr);
       }
     }
   } else if (kGather && (warp == 2 || warp == 3)) {
@@ -370,7 +294,7 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
     uint32_t issued = 0, announced = 0;  // k-iterations copied / arrived on `full`
     bool ok = true;
     int64_t row_off[kGatherRows];
-    for (int tile = tile0; tile < total_tiles && ok; tile += tile_step) {
+    for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
       int e, nb, mb;
       decode_tile(s_bs, E, NB, tile, e, nb, mb);
 #pragma unroll
@@ -405,14 +329,14 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
     fence_proxy_async_smem();
     for (; announced < issued; ++announced) mbar_arrive(&full[announced % STAGES]);
   } else if (warp == 1) {
-    if (lane == 0 && leader) {
-      // ------------------------------------------------ MMA issuer (a pair's leader issues for both CTAs)
+    if (lane == 0) {
+      // ------------------------------------------------ MMA issuer
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int tile = tile0; tile < total_tiles && ok; tile += tile_step) {
+      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
         if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1, status, s_abort)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
@@ -425,21 +349,17 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k) {
             // +32 bytes along K inside the 128-byte swizzled row = +2 in the address field
-            if constexpr (PAIR) umma_f16_pair(d_tmem, a_desc + 2 * k, b_desc + 2 * k, kIdesc, (kb | k) != 0);
-            else umma_f16(d_tmem, a_desc + 2 * k, b_desc + 2 * k, kIdesc, (kb | k) != 0);
+            umma_f16(d_tmem, a_desc + 2 * k, b_desc + 2 * k, kIdesc, (kb | k) != 0);
           }
-          if constexpr (PAIR) umma_commit_pair_multicast(&empty[stage], 0x3);
-          else umma_commit(&empty[stage]);
+          umma_commit(&empty[stage]);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
         if (!ok) break;
-        if constexpr (PAIR) umma_commit_pair_multicast(&tmem_full[acc], 0x3);
-        else umma_commit(&tmem_full[acc]);
+        umma_commit(&tmem_full[acc]);
         if (++acc == 2) { acc = 0; acc_phase ^= 1; }
       }
       // all MMAs issued by this thread complete before TMEM is freed
-      if constexpr (PAIR) umma_commit_pair(mma_done);
-      else umma_commit(mma_done);
+      umma_commit(mma_done);
       mbar_wait(mma_done, 0, nullptr, nullptr);
     }
   } else if (warp >= 4) {
@@ -455,22 +375,12 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
     constexpr int kGroups = (kGemm1 ? BH : BN) / 64;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = tile0; tile < total_tiles; tile += tile_step) {
+    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
       int e, nb, mb;
-      if constexpr (PAIR) decode_pair_tile(s_bs, s_pp, E, NB, tile, (int)cta, e, nb, mb);
-      else decode_tile(s_bs, E, NB, tile, e, nb, mb);
+      decode_tile(s_bs, E, NB, tile, e, nb, mb);
       // warp-uniform decision: tcgen05.ld below is .sync.aligned
       if (!__all_sync(0xffffffffu, mbar_wait(&tmem_full[acc], acc_phase, status, s_abort))) break;
       tc_fence_after();
-      // PAIR: this CTA's half of a pair-block past the end of e's rows holds nothing to store
-      const bool rows_ok = !PAIR || mb < s_bs[e + 1];
-      if (!rows_ok) {
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(mapa_shared(&tmem_empty[acc], 0));
-        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
-        continue;
-      }
       const uint32_t t_row = tmem_base + ((uint32_t)(ew * 32) << 16) + (uint32_t)(acc * BN);
       const int64_t row0 = (int64_t)mb * kBlockM + ew * 32;  // first tile row of this warp
       int my_pair = 0;
@@ -508,12 +418,7 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
         if (g == kGroups - 1) {
           // accumulator fully read: release it to the MMA warp before the last stores
           tc_fence_before();
-          if constexpr (PAIR) {
-            __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(mapa_shared(&tmem_empty[acc], 0));
-          } else {
-            mbar_arrive(&tmem_empty[acc]);
-          }
+          mbar_arrive(&tmem_empty[acc]);
         }
         __syncwarp();
 #pragma unroll
@@ -537,88 +442,35 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
     }
   }
 
-  if constexpr (PAIR) {
-    if (producer_aborted && !leader) {
-      // the peer cannot watch its own copies land (they count on the leader's barriers):
-      // give copies in flight a bounded grace period before the pair exits
-      const uint64_t t0 = globaltimer_ns();
-      while (globaltimer_ns() - t0 < 2000000ull) {
-      }
-    }
-    tc_fence_before();
-    cluster_sync_all();  // no CTA leaves while its peer may still use its barriers or TMEM
-    if (warp == 2) {
-      tc_fence_after();
-      tmem_dealloc_pair(tmem_base, kTmemCols);
-    }
-  } else {
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 2) {
-      tc_fence_after();
-      tmem_dealloc(tmem_base, kTmemCols);
-    }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
   }
 }
 
 // ---------------------------------------------------------------- host side
-constexpr int kStages = 4;      // 1-CTA tiles: 4 x 48 KB
-constexpr int kPairStages = 6;  // CTA pairs: 6 x 32 KB (A + half of B per CTA)
+constexpr int kStages = 4;
 
-// CTA pairs pay off when experts hold many m-blocks: the pair halves each SM's B-tile
-// traffic through shared memory, but an expert with an odd block count leaves half of
-// its last pair-block idle. Average rows per expert (from the align capacity) decides.
-constexpr int64_t kPairMinRowsPerExpert = 512;
-inline bool use_pairs(int64_t rows_cap, int E) { return rows_cap >= kPairMinRowsPerExpert * (int64_t)E; }
-
-template <typename T, int MODE, int BN, bool PAIR = false>
+template <typename T, int MODE, int BN>
 cudaError_t launch_gemm_t(const CUtensorMap& ma, const CUtensorMap& mb, const int32_t* block_start, int E, int k_red,
                           int n_out, int NB, int64_t rows_cap, void* out, const int32_t* sorted_pairs, int* status,
                           int max_ctas, cudaStream_t st, const CombineArgs& cmb = CombineArgs{},
                           const RowGather& gat = RowGather{}) {
-  constexpr int S = PAIR ? kPairStages : kStages;
-  using L = SmemLayout<BN, S, PAIR>;
-  auto kern = moe_gemm_kernel<T, MODE, BN, S, PAIR>;
+  using L = SmemLayout<BN, kStages>;
+  auto kern = moe_gemm_kernel<T, MODE, BN, kStages>;
   const int smem = L::bytes(E);
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (err != cudaSuccess) return err;
-  const int64_t blocks_cap = rows_cap / kBlockM;
-  if constexpr (!PAIR) {
-    const int64_t tiles_cap = blocks_cap * NB;
-    // persistent grid: one CTA per SM, or fewer when the caller keeps SMs free for
-    // concurrent work (e.g. collectives overlapping the GEMM)
-    const int ctas = (max_ctas > 0 && max_ctas < num_sms()) ? max_ctas : num_sms();
-    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(ctas, tiles_cap));
-    kern<<<grid, kThreads, smem, st>>>(ma, mb, block_start, E, k_red, n_out, NB, static_cast<T*>(out), sorted_pairs,
-                                       status, cmb, gat);
-    return cudaGetLastError();
-  } else {
-    cudaLaunchConfig_t cfg = {};
-    cfg.blockDim = dim3(kThreads, 1, 1);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    // persistent grid of the CTA pairs that can be resident at once (a pair needs two SMs
-    // of one GPC); fewer when the caller keeps SMs free
-    cfg.gridDim = dim3(num_sms(), 1, 1);
-    int resident = 0;
-    if (cudaOccupancyMaxActiveClusters(&resident, kern, &cfg) != cudaSuccess || resident <= 0) {
-      (void)cudaGetLastError();
-      resident = num_sms() / 2;
-    }
-    if (max_ctas > 0) resident = std::min(resident, std::max(1, max_ctas / 2));
-    const int64_t pair_tiles_cap = ((blocks_cap + 1) / 2 + E) * (int64_t)NB;
-    const int clusters = (int)std::max<int64_t>(1, std::min<int64_t>(resident, pair_tiles_cap));
-    cfg.gridDim = dim3(2 * clusters, 1, 1);
-    return cudaLaunchKernelEx(&cfg, kern, ma, mb, block_start, E, k_red, n_out, NB, static_cast<T*>(out),
-                              sorted_pairs, status, cmb, gat);
-  }
+  const int64_t tiles_cap = (rows_cap / kBlockM) * NB;
+  // persistent grid: one CTA per SM, or fewer when the caller keeps SMs free for
+  // concurrent work (e.g. collectives overlapping the GEMM)
+  const int ctas = (max_ctas > 0 && max_ctas < num_sms()) ? max_ctas : num_sms();
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(ctas, tiles_cap));
+  kern<<<grid, kThreads, smem, st>>>(ma, mb, block_start, E, k_red, n_out, NB, static_cast<T*>(out), sorted_pairs,
+                                     status, cmb, gat);
+  return cudaGetLastError();
 }
 
 }  // namespace
@@ -635,13 +487,6 @@ cudaError_t launch_gemm1_silu(int dtype, const void* x_sorted, int64_t rows_cap,
   if (!make_kmajor_map(&ma, dtype, x_sorted, 2, a_dims, a_str, kBlockM)) return cudaErrorInvalidValue;
   if (!make_kmajor_map(&mbm, dtype, w1, 3, b_dims, b_str, (uint32_t)BH)) return cudaErrorInvalidValue;
   const int NB = N / BH;
-  if (BN == 256 && use_pairs(rows_cap, E)) {  // pair: the leader's B half is the gate rows, the peer's the up rows
-    if (dtype == MOE_DTYPE_BF16)
-      return launch_gemm_t<__nv_bfloat16, MODE_GEMM1_SILU, 256, true>(ma, mbm, block_start, E, K, N, NB, rows_cap,
-                                                                      act, nullptr, status, max_ctas, st);
-    return launch_gemm_t<__half, MODE_GEMM1_SILU, 256, true>(ma, mbm, block_start, E, K, N, NB, rows_cap, act,
-                                                             nullptr, status, max_ctas, st);
-  }
   if (dtype == MOE_DTYPE_BF16) {
     if (BN == 256)
       return launch_gemm_t<__nv_bfloat16, MODE_GEMM1_SILU, 256>(ma, mbm, block_start, E, K, N, NB, rows_cap, act,
@@ -672,18 +517,8 @@ cudaError_t launch_gemm2_mode(int dtype, const void* act, int64_t rows_cap, cons
   const uint64_t b_dims[3] = {(uint64_t)N, (uint64_t)K, (uint64_t)E};
   const uint64_t b_str[2] = {(uint64_t)N * 2, (uint64_t)K * N * 2};
   if (!make_kmajor_map(&ma, dtype, act, 2, a_dims, a_str, kBlockM)) return cudaErrorInvalidValue;
-  const int NB = (int)ceil_div(K, BN);
-  if constexpr (MODE == MODE_GEMM2) {
-    if (BN == 256 && use_pairs(rows_cap, E)) {  // pair: each CTA loads 128 of the tile's 256 w2 rows
-      if (!make_kmajor_map(&mbm, dtype, w2, 3, b_dims, b_str, (uint32_t)BN / 2)) return cudaErrorInvalidValue;
-      if (dtype == MOE_DTYPE_BF16)
-        return launch_gemm_t<__nv_bfloat16, MODE, 256, true>(ma, mbm, block_start, E, N, K, NB, rows_cap, y_slots,
-                                                             sorted_pairs, status, max_ctas, st, cmb);
-      return launch_gemm_t<__half, MODE, 256, true>(ma, mbm, block_start, E, N, K, NB, rows_cap, y_slots,
-                                                    sorted_pairs, status, max_ctas, st, cmb);
-    }
-  }
   if (!make_kmajor_map(&mbm, dtype, w2, 3, b_dims, b_str, (uint32_t)BN)) return cudaErrorInvalidValue;
+  const int NB = (int)ceil_div(K, BN);
   if (dtype == MOE_DTYPE_BF16) {
     if (BN == 256)
       return launch_gemm_t<__nv_bfloat16, MODE, 256>(ma, mbm, block_start, E, N, K, NB, rows_cap, y_slots,

@@ -1,14 +1,10 @@
-"""GPU: the expert GEMMs on CTA pairs (tcgen05.mma.cta_group::2, 256-row tiles over two SMs).
+"""GPU: every output row of the expert path at awkward per-expert row counts.
 
-The grouped GEMMs switch to CTA pairs when experts hold many rows (about 4 m-blocks of 128
-or more on average). A pair takes two consecutive m-blocks of one expert; an expert with an
-odd block count leaves the second CTA's half of its last pair-block outside the expert,
-and that half must be computed and dropped, never stored. These cases are checked on every
-row against the fp32 restatement of the reference's expert path
-(fused_moe/v0/fused_moe.py:141-167): experts with no rows, one row, 1, 2 and 3 full
-m-blocks plus one row, and the rest random; bf16 and fp16; hidden sizes with a ragged last
-down-GEMM n-block. The DeepSeek-V3 workload at 32768 tokens (pairs in both GEMMs) is checked
-in test_fused_moe_gpu.py.
+Experts with no rows, one row, 129, 257 and 385 rows (1, 2 and 3 full m-blocks of 128
+plus one row, so the last m-block of each is nearly empty), the rest random; bf16 and
+fp16; hidden sizes with a ragged last down-GEMM n-block. All rows are checked against the
+fp32 restatement of the reference's expert path (fused_moe/v0/fused_moe.py:141-167), and a
+second call must give the same bits.
 """
 import pytest
 import torch
@@ -47,7 +43,7 @@ def _ids_with_shapes(M, E, k, dev, seed):
                                              (2600, 16, 4, 320, 128, torch.bfloat16),
                                              (3000, 8, 2, 256, 384, torch.float16),
                                              (9000, 16, 4, 1024, 512, torch.bfloat16)])
-def test_pair_tiles_all_rows(cuda_device, M, E, k, K, N, dtype):
+def test_all_rows_awkward_counts(cuda_device, M, E, k, K, N, dtype):
     dev = cuda_device
     gen = torch.Generator(device=dev).manual_seed(M + K)
     x = torch.randn(M, K, generator=gen, device=dev).to(dtype)
