@@ -10,7 +10,8 @@ Public API (mirrors the reference's task signatures):
 
 Drop-in task modules with the reference harness contract (``ModelNew``,
 ``get_inputs``, ``get_init_inputs``) live in ``tasks/``; the expert-parallel
-layer is in ``ep``.
+layer is in ``ep``. Importing the package also registers the operators as
+``torch.ops.moe_b200.*`` (``torch_ops``).
 """
 
 from .ops import (  # noqa: F401
@@ -29,6 +30,8 @@ from .ops import (  # noqa: F401
     router_grouped_topk,
     softmax_topk,
 )
+
+from . import torch_ops  # noqa: E402,F401  (registers torch.ops.moe_b200.*)
 
 __all__ = ["grouped_topk", "fused_moe", "fused_moe_fp8", "softmax_topk", "moe_align", "moe_layer",
            "fused_moe_workspace_bytes", "quantize_rows_fp8", "quantize_weights_fp8", "check_device_status",

@@ -166,8 +166,12 @@ cudaError_t launch_align(const int32_t* topk_ids, int64_t P, int topk, int E, in
 }
 
 int num_sms() {
+  static int cache[64];  // per device, 0 = not read yet
   int dev = 0, n = 148;
-  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  if (cudaGetDevice(&dev) != cudaSuccess) return n;
+  if (dev >= 0 && dev < 64 && cache[dev]) return cache[dev];
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
+  if (dev >= 0 && dev < 64) cache[dev] = n;
   return n;
 }
 

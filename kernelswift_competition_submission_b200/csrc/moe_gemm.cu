@@ -461,7 +461,7 @@ cudaError_t launch_gemm_t(const CUtensorMap& ma, const CUtensorMap& mb, const in
   using L = SmemLayout<BN, kStages>;
   auto kern = moe_gemm_kernel<T, MODE, BN, kStages>;
   const int smem = L::bytes(E);
-  cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaError_t err = ensure_smem_limit(reinterpret_cast<const void*>(kern), smem);
   if (err != cudaSuccess) return err;
   const int64_t tiles_cap = (rows_cap / kBlockM) * NB;
   // persistent grid: one CTA per SM, or fewer when the caller keeps SMs free for

@@ -487,7 +487,7 @@ cudaError_t launch_f8_stages(const CUtensorMap& ma, const CUtensorMap& mb, const
   // setmaxnreg.inc waits for registers the block does not own if the launch holds
   // fewer than 384 x 168: never launch such a build.
   if (fa.numRegs != kF8RegsLaunch) return cudaErrorInvalidConfiguration;
-  err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  err = ensure_smem_limit(reinterpret_cast<const void*>(kern), smem);
   if (err != cudaSuccess) return err;
   const int64_t tiles_cap = (rows_cap / kBlockM) * NB;
   const int ctas = (max_ctas > 0 && max_ctas < num_sms()) ? max_ctas : num_sms();

@@ -72,6 +72,10 @@ cudaError_t launch_combine_prep(const int32_t* topk_ids, int64_t M, int topk, in
 cudaError_t launch_ep_combine(int dtype, const void* back, const int32_t* tok_rows, int64_t M, int K, int world,
                               void* out, const int* status, cudaStream_t st);
 
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (function, device) and size.
+cudaError_t ensure_smem_limit(const void* func, int bytes);
+
+// Tensor maps (cuTensorMapEncodeTiled), cached by address, shape, strides and box.
 bool make_kmajor_map(CUtensorMap* m, int dtype, const void* base, int rank, const uint64_t* dims,
                      const uint64_t* strides_bytes, uint32_t box_rows);
 

@@ -202,7 +202,7 @@ cudaError_t launch_router(const CUtensorMap& ma, const CUtensorMap& mb, int64_t 
                           int topk_group, int scoring, int gmode, float scale, float* w, int32_t* ids, int* status,
                           cudaStream_t st) {
   auto kern = router_kernel<T, LPG>;
-  cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kRSmem);
+  cudaError_t err = ensure_smem_limit(reinterpret_cast<const void*>(kern), kRSmem);
   if (err != cudaSuccess) return err;
   if (splits == 1) {
     kern<<<grid, kRThreads, kRSmem, st>>>(ma, mb, M, K, splits, logits, done, bias, topk, renorm, n_group,

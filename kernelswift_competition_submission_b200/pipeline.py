@@ -21,9 +21,50 @@ inputs; only the copies move.
 
 from __future__ import annotations
 
+import os
+from pathlib import Path
 from typing import Callable, Sequence
 
 import torch
+
+
+def parse_cpulist(text: str) -> set[int]:
+    """CPU ids of a sysfs cpulist such as "0-23,96-119"."""
+    cpus: set[int] = set()
+    for part in text.strip().split(","):
+        if not part:
+            continue
+        if "-" in part:
+            a, b = part.split("-", 1)
+            cpus.update(range(int(a), int(b) + 1))
+        else:
+            cpus.add(int(part))
+    return cpus
+
+
+def gpu_local_cpus(device: torch.device | int, sysfs: str | Path = "/sys/bus/pci/devices") -> set[int]:
+    """The host CPUs on the NUMA node the GPU hangs off (its PCI device's local_cpulist);
+    an empty set when the platform does not say."""
+    idx = device if isinstance(device, int) else (device.index or 0)
+    p = torch.cuda.get_device_properties(idx)
+    bdf = f"{p.pci_domain_id:04x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+    f = Path(sysfs) / bdf / "local_cpulist"
+    try:
+        return parse_cpulist(f.read_text())
+    except (OSError, ValueError):
+        return set()
+
+
+def bind_to_gpu_node(device: torch.device | int, sysfs: str | Path = "/sys/bus/pci/devices") -> set[int]:
+    """Restrict this process to the CPUs local to the GPU (intersected with the ones it may
+    use), so pinned host buffers allocated afterwards are placed on that NUMA node by first
+    touch and host<->device copies do not cross the socket link. Returns the CPUs kept (the
+    affinity is left alone when the intersection is empty)."""
+    allowed = os.sched_getaffinity(0)
+    local = gpu_local_cpus(device, sysfs) & allowed
+    if local:
+        os.sched_setaffinity(0, local)
+    return local
 
 
 class HostPipeline:

@@ -1,0 +1,83 @@
+"""fused_moe drop-in with FP8 w8a8 experts: ``ModelNew`` with the reference's constructor,
+parameters and forward signature (``fused_moe/v0/fused_moe.py:99-124,126-167``), running the
+DeepSeek-V3 FP8 recipe: the expert weights are quantised to e4m3 with one fp32 scale per
+128 x 128 block, the token rows per token per 128, and the expert GEMMs run
+tcgen05.mma.kind::f8f6f4 with fp32 block-scale promotion.
+
+The quantised weights are cached and re-made only when a parameter's ``_version`` or
+storage changes (the caching idea of ``fused_moe/v1/fused_moe.py:285-303``, here for the
+FP8 copies). The FP8 kernels need hidden_size and intermediate_size to be multiples of
+128; other shapes raise ``ValueError`` at construction. ``get_init_inputs`` is therefore
+an FP8-capable shape (hidden 256, intermediate 128), not the reference task's.
+"""
+import torch
+import torch.nn as nn
+
+
+def _bootstrap():
+    import os
+    import sys
+
+    here = os.path.dirname(os.path.abspath(__file__))
+    root = os.path.dirname(os.path.dirname(here))
+    if root not in sys.path:
+        sys.path.insert(0, root)
+    import kernelswift_competition_submission_b200 as pkg
+
+    return pkg
+
+
+class ModelNew(nn.Module):
+    def __init__(
+        self,
+        num_experts: int,
+        top_k: int,
+        hidden_size: int,
+        intermediate_size: int,
+        renormalize: bool = True,
+    ):
+        super().__init__()
+        if hidden_size % 128 or intermediate_size % 128:
+            raise ValueError("FP8 experts need hidden_size and intermediate_size to be multiples of 128")
+        self.num_experts = num_experts
+        self.top_k = top_k
+        self.hidden_size = hidden_size
+        self.intermediate_size = intermediate_size
+        self.renormalize = renormalize
+        self.w1 = nn.Parameter(torch.empty(num_experts, 2 * intermediate_size, hidden_size))
+        self.w2 = nn.Parameter(torch.empty(num_experts, hidden_size, intermediate_size))
+        nn.init.normal_(self.w1, std=0.02)
+        nn.init.normal_(self.w2, std=0.02)
+        self._ops = _bootstrap()
+        self._cache = None
+        self.quantizations = 0  # how many times the FP8 weights were (re)made
+
+    def _fp8_weights(self):
+        key = (self.w1.device, self.w1.data_ptr(), self.w1._version, self.w2.data_ptr(), self.w2._version)
+        if self._cache is None or self._cache[0] != key:
+            with torch.no_grad():
+                w1q, w1s = self._ops.quantize_weights_fp8(self.w1.detach().to(torch.bfloat16).contiguous())
+                w2q, w2s = self._ops.quantize_weights_fp8(self.w2.detach().to(torch.bfloat16).contiguous())
+            self._cache = (key, w1q, w1s, w2q, w2s)
+            self.quantizations += 1
+        return self._cache[1:]
+
+    def forward(self, hidden_states: torch.Tensor, router_logits: torch.Tensor) -> torch.Tensor:
+        w1q, w1s, w2q, w2s = self._fp8_weights()
+        w, ids = self._ops.softmax_topk(router_logits, self.top_k, self.renormalize)
+        out = self._ops.fused_moe(hidden_states.to(torch.bfloat16), w1q, w2q, w, ids, use_fp8_w8a8=True,
+                                  w1_scale=w1s, w2_scale=w2s)
+        return out.to(hidden_states.dtype)
+
+
+def get_inputs():
+    # hidden_states: [num_tokens, hidden_size] float16; router_logits: [num_tokens, num_experts] float32
+    num_tokens, hidden_size, num_experts = 83, 256, 8
+    hidden_states = torch.randn(num_tokens, hidden_size, dtype=torch.float16)
+    router_logits = torch.randn(num_tokens, num_experts, dtype=torch.float32)
+    return [hidden_states, router_logits]
+
+
+def get_init_inputs():
+    # num_experts, top_k, hidden_size, intermediate_size (multiples of 128 for FP8)
+    return [8, 2, 256, 128]

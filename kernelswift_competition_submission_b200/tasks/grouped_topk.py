@@ -3,7 +3,9 @@
 Same constructor and forward signature as the reference's ModelNew
 (``grouped_topk/v1/grouped_topk.py:187-235``) and v0 Model
 (``grouped_topk/v0/grouped_topk.py:73-132``); the forward is one launch of the
-warp-per-token sm_100a routing kernel in ``libmoe_b200.so``.
+warp-per-token sm_100a routing kernel in ``libmoe_b200.so``, launched directly: one
+kernel, so a replayed CUDA graph (plus the copies that give each call fresh outputs) only
+adds time here.
 ``get_inputs``/``get_init_inputs`` reproduce the task's CPU inputs
 (``grouped_topk/v0/grouped_topk.py:135-148``).
 """
@@ -42,20 +44,11 @@ class ModelNew(nn.Module):
         self.scoring_func = scoring_func
         self.routed_scaling_factor = routed_scaling_factor
         self._ops = _bootstrap()
-        self._graph = None
 
-    def _forward_eager(self, hidden_states, gating_output):
+    def forward(self, hidden_states: torch.Tensor, gating_output: torch.Tensor):
         return self._ops.grouped_topk(
             hidden_states, gating_output, self.topk, self.renormalize, self.num_expert_group,
             self.topk_group, self.scoring_func, self.routed_scaling_factor)
-
-    def forward(self, hidden_states: torch.Tensor, gating_output: torch.Tensor):
-        # repeated calls on the same buffers replay a CUDA graph of the routing kernel
-        if self._graph is None:
-            from kernelswift_competition_submission_b200.graphs import GraphCache
-
-            self._graph = GraphCache(self._forward_eager)
-        return self._graph(hidden_states, gating_output)
 
 
 def get_inputs():

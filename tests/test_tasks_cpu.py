@@ -78,3 +78,33 @@ def test_weight_cache_invalidates_on_update():
     a3, _ = model._prepared_weights(torch.float16)
     assert a3 is not a1
     torch.testing.assert_close(a3.float(), model.w1.detach().half().float())
+
+
+def test_cpulist_and_gpu_node_binding(tmp_path, monkeypatch):
+    """The NUMA placement of host batches: sysfs cpulist parsing and the affinity
+    restriction to the GPU's local CPUs (a fake sysfs tree and fake device properties)."""
+    import os
+    import types
+
+    import torch
+
+    from kernelswift_competition_submission_b200 import pipeline
+
+    assert pipeline.parse_cpulist("0-3,8,10-11\n") == {0, 1, 2, 3, 8, 10, 11}
+    assert pipeline.parse_cpulist("") == set()
+    dev_dir = tmp_path / "0000:1b:00.0"
+    dev_dir.mkdir()
+    allowed = sorted(os.sched_getaffinity(0))
+    (dev_dir / "local_cpulist").write_text(f"{allowed[0]}-{allowed[0]}\n")
+    props = types.SimpleNamespace(pci_domain_id=0, pci_bus_id=0x1B, pci_device_id=0)
+    monkeypatch.setattr(torch.cuda, "get_device_properties", lambda i: props)
+    before = os.sched_getaffinity(0)
+    try:
+        kept = pipeline.bind_to_gpu_node(0, sysfs=tmp_path)
+        assert kept == {allowed[0]} and os.sched_getaffinity(0) == {allowed[0]}
+    finally:
+        os.sched_setaffinity(0, before)
+    # unknown device: nothing to restrict
+    props.pci_bus_id = 0x2C
+    assert pipeline.bind_to_gpu_node(0, sysfs=tmp_path) == set()
+    assert os.sched_getaffinity(0) == before
