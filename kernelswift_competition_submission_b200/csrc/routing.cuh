@@ -30,6 +30,67 @@ __device__ __forceinline__ unsigned ordered_key(float f) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
+// 64-bit selection key: the value's order-preserving key above the bit-inverted expert
+// index, so one unsigned comparison is the strict order (value descending, index
+// ascending). 0 is below every real candidate (a real key's high word is never 0).
+__device__ __forceinline__ uint64_t route_key(float c, int id) {
+  return ((uint64_t)ordered_key(c) << 32) | (uint64_t)(~(uint32_t)id);
+}
+__device__ __forceinline__ void route_cmpx(uint64_t& a, uint64_t& b) {  // larger key first
+  const uint64_t hi = a > b ? a : b;
+  const uint64_t lo = a > b ? b : a;
+  a = hi;
+  b = lo;
+}
+
+// Top-k selection for 8 candidates per lane (E = 256): the lane's keys sorted by the
+// 19-comparator sorting network for 8 inputs, then per round a warp arg-max of the heads
+// (two redux.sync reductions: the high words, then the low words among the lanes that
+// hold the largest high word) and a pop of the winner's head. The weight of the chosen
+// expert is the lane's score s at that expert, in the unsorted order.
+__device__ __forceinline__ void route_select_sorted8(const float (&c)[8], const float (&s)[8], int e0, int lane,
+                                                     int64_t tok, int topk, int renormalize, float scale,
+                                                     float* __restrict__ out_w, int32_t* __restrict__ out_ids) {
+  uint64_t k[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) k[i] = route_key(c[i], e0 + i);
+  route_cmpx(k[0], k[2]); route_cmpx(k[1], k[3]); route_cmpx(k[4], k[6]); route_cmpx(k[5], k[7]);
+  route_cmpx(k[0], k[4]); route_cmpx(k[1], k[5]); route_cmpx(k[2], k[6]); route_cmpx(k[3], k[7]);
+  route_cmpx(k[0], k[1]); route_cmpx(k[2], k[3]); route_cmpx(k[4], k[5]); route_cmpx(k[6], k[7]);
+  route_cmpx(k[2], k[4]); route_cmpx(k[3], k[5]);
+  route_cmpx(k[1], k[4]); route_cmpx(k[3], k[6]);
+  route_cmpx(k[1], k[2]); route_cmpx(k[3], k[4]); route_cmpx(k[5], k[6]);
+  float my_w = 0.f;
+  int my_id = 0;
+  for (int r = 0; r < topk; ++r) {
+    const uint32_t hi = (uint32_t)(k[0] >> 32);
+    const uint32_t hmax = __reduce_max_sync(0xffffffffu, hi);
+    const uint32_t lmax = __reduce_max_sync(0xffffffffu, hi == hmax ? (uint32_t)k[0] : 0u);
+    const int bi = (int)(~lmax);
+    const int owner = bi >> 3;
+    float ws = 0.f;
+    if (lane == owner) {
+      const int j = bi - e0;  // the winner's score, unsorted order
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ws = (i == j) ? s[i] : ws;
+#pragma unroll
+      for (int i = 0; i < 7; ++i) k[i] = k[i + 1];  // pop the head
+      k[7] = 0;
+    }
+    const float bs = __shfl_sync(0xffffffffu, ws, owner);
+    if (lane == r) { my_w = bs; my_id = bi; }
+  }
+  if (renormalize) {
+    const float tot = route_warp_sum(lane < topk ? my_w : 0.f);
+    my_w = my_w / tot;
+  }
+  if (scale != 1.0f) my_w *= scale;
+  if (lane < topk) {
+    out_w[tok * topk + lane] = my_w;
+    out_ids[tok * topk + lane] = my_id;
+  }
+}
+
 // Register-only variant for the common layouts: E = 32 * VPL (every lane full) and,
 // when groups are masked, groups of whole lanes (LPG = E / n_group / VPL lanes per
 // group, a power of two): a group's top-2 sum (or max) is a per-lane reduction over
@@ -119,6 +180,10 @@ __device__ __forceinline__ void route_token_lanes(const float* row, const float*
     }
   }
 
+  if constexpr (VPL == 8) {
+    route_select_sorted8(c, s, e0, lane, tok, topk, renormalize, scale, out_w, out_ids);
+    return;
+  }
   // sort this lane's candidates: value descending; equal values keep index order
   int id[VPL];
 #pragma unroll
