@@ -390,6 +390,20 @@ MOE_API int moe_p2p_combine_experts_back(int dtype, const void* workspace, int n
                                          int intermediate_size, int topk, int world, int me, int64_t cap,
                                          const int64_t* peer_bases, const void* own_base, uint32_t seq,
                                          int32_t* scratch, int* status, void* stream);
+/* The down GEMM of the local expert path fused with the combine and the return trip: after
+ * moe_expert_align_gather and moe_expert_gemm1 over the world * cap received rows (same
+ * workspace, M = world * cap), the epilogue of the down GEMM sums each received row's slots
+ * of one n-block once all of them are stored (the bits of moe_p2p_combine_experts_back) and
+ * stores the sum straight into the source rank's back_x region `me` over NVLink, so the
+ * return overlaps the tensor-core work; the back flag [me] of a source is raised when its
+ * last row is in, and at once for a source that sent nothing this step. scratch: int32
+ * [world] (zeroed by the call). bf16 / fp16 rows only; the FP8 path keeps
+ * moe_p2p_combine_experts_back. */
+MOE_API int moe_p2p_expert_gemm2_return(int dtype, const void* w2, void* workspace, size_t workspace_bytes,
+                                        int num_experts, int hidden_size, int intermediate_size, int topk,
+                                        int world, int me, int64_t cap, const int64_t* peer_bases,
+                                        const void* own_base, uint32_t seq, int32_t* scratch, int* status,
+                                        int max_ctas, void* stream);
 /* copy of the received expert ids [world * cap, topk] (statistics, tests) */
 MOE_API int moe_p2p_copy_recv_ids(const void* own_base, int world, int64_t cap, int hidden_size, int topk,
                                   int32_t* dst, void* stream);

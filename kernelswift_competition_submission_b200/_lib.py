@@ -88,6 +88,8 @@ SIGNATURES = {
                                 ctypes.c_uint32, _c_p, _c_p, _c_p, _c_p]),
     "moe_p2p_combine_experts_back": (_i32, [_i32, _c_p, _i32, _i32, _i32, _i32, _i32, _i32, _i64, _c_p, _c_p,
                                             ctypes.c_uint32, _c_p, _c_p, _c_p]),
+    "moe_p2p_expert_gemm2_return": (_i32, [_i32, _c_p, _c_p, _sz, _i32, _i32, _i32, _i32, _i32, _i32, _i64, _c_p,
+                                           _c_p, ctypes.c_uint32, _c_p, _c_p, _i32, _c_p]),
     "moe_p2p_copy_recv_ids": (_i32, [_c_p, _i32, _i64, _i32, _i32, _c_p, _c_p]),
     "moe_p2p_combine_back": (_i32, [_i32, _c_p, _i32, _i32, _i32, _i32, _i64, _c_p, _c_p, ctypes.c_uint32, _c_p,
                                     _c_p, _c_p]),

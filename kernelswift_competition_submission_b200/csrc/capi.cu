@@ -258,6 +258,38 @@ extern "C" int moe_expert_gemm2_combine(int dtype, const void* w2, const float* 
   return cuda_status(err);
 }
 
+extern "C" int moe_p2p_expert_gemm2_return(int dtype, const void* w2, void* workspace, size_t workspace_bytes,
+                                           int num_experts, int hidden_size, int intermediate_size, int topk,
+                                           int world, int me, int64_t cap, const int64_t* peer_bases,
+                                           const void* own_base, uint32_t seq, int32_t* scratch, int* status,
+                                           int max_ctas, void* stream) {
+  using namespace moe;
+  if (world <= 0 || world > 64 || me < 0 || me >= world || cap <= 0) return MOE_ERR_INVALID_ARG;
+  const int64_t M = (int64_t)world * cap;  // every received row, as the align and GEMM1 stages saw them
+  int rc = validate_experts(dtype, M, num_experts, topk, hidden_size, intermediate_size);
+  if (rc != MOE_OK) return rc;
+  if (!w2 || !aligned16(w2) || !peer_bases || !own_base || !scratch || max_ctas < 0) return MOE_ERR_INVALID_ARG;
+  if ((rc = check_device_ready()) != MOE_OK) return rc;
+  Ws w;
+  if ((rc = workspace_views(workspace, workspace_bytes, M, num_experts, topk, hidden_size, intermediate_size, &w)) !=
+      MOE_OK)
+    return rc;
+  int64_t offs[9];
+  if (moe_p2p_arena_offsets(world, cap, hidden_size, topk, offs) != MOE_OK) return MOE_ERR_INVALID_ARG;
+  const char* ob = static_cast<const char*>(own_base);
+  const int32_t* own_counts = reinterpret_cast<const int32_t*>(ob + offs[3]);
+  const int32_t* recv_id = reinterpret_cast<const int32_t*>(ob + offs[5]);
+  const float* recv_w = reinterpret_cast<const float*>(ob + offs[6]);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t err = launch_combine_prep(recv_id, M, topk, num_experts, hidden_size, w.arrivals, w.l.n_arrivals,
+                                        scratch, world, nullptr, st);
+  if (err == cudaSuccess)
+    err = launch_gemm2_return(dtype, w.act, w.l.cap, w2, num_experts, hidden_size, intermediate_size,
+                              w.am.block_start, w.sorted, w.y_slots, recv_w, recv_id, topk, w.arrivals, peer_bases,
+                              own_counts, scratch, offs[7], offs[2], cap, me, world, seq, status, max_ctas, st);
+  return cuda_status(err);
+}
+
 extern "C" int moe_fused_experts(int dtype, const void* hidden_states, const void* w1, const void* w2,
                                  const float* topk_weights, const int32_t* topk_ids, int64_t num_tokens,
                                  int num_experts, int topk, int hidden_size, int intermediate_size, void* out,

@@ -44,10 +44,10 @@ combine_kernel(const uint4* __restrict__ y, const float* __restrict__ w, const i
 }
 
 // Set-up of the combine fused into the down GEMM (MODE_GEMM2_COMBINE): zeroes the
-// [M, NB] arrival counters and `n_zero` further ints (the align metadata, when the
-// caller folds its memset in here), and writes a zero row to `out` for every token none
-// of whose slots holds an expert in [0, E): no GEMM tile reaches such a token, and the
-// reference's expert loop leaves its output row at zero (fused_moe/v0/fused_moe.py:154-167).
+// [M, NB] arrival counters and `n_zero` further ints (other per-launch counters), and,
+// when `out` is given, writes a zero row to it for every token none of whose slots holds
+// an expert in [0, E): no GEMM tile reaches such a token, and the reference's expert loop
+// leaves its output row at zero (fused_moe/v0/fused_moe.py:154-167).
 __global__ void __launch_bounds__(256)
 combine_prep_kernel(const int32_t* __restrict__ ids, int64_t M, int topk, int E, int32_t* __restrict__ arrivals,
                     int64_t n_arrivals, int32_t* __restrict__ zero_ints, int n_zero, uint4* __restrict__ out,
@@ -56,6 +56,7 @@ combine_prep_kernel(const int32_t* __restrict__ ids, int64_t M, int topk, int E,
   const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   for (int64_t i = gid; i < n_arrivals; i += stride) arrivals[i] = 0;
   for (int64_t i = gid; i < n_zero; i += stride) zero_ints[i] = 0;
+  if (out == nullptr) return;  // rows returned elsewhere (expert-parallel return mode)
   for (int64_t t = gid; t < M; t += stride) {
     bool any = false;
     for (int j = 0; j < topk; ++j) {

@@ -64,13 +64,34 @@ struct RowGather {
 // arrival, and the warp that brings a token's last valid slot of that n-block sums all
 // of that token's slots over the n-block's columns (slot order, fp32 FMAs, one rounding:
 // the arithmetic of combine_kernel, so the output bits do not depend on arrival order).
+//
+// Return mode (peer_base != nullptr; the expert-parallel layer over peer memory): row t of
+// this launch is received row r = t % cap of source rank src = t / cap, and its sum goes
+// straight into that rank's arena, back_x row me * cap + r (NVLink stores), instead of a
+// local `out`. Every (row, n-block) segment stored counts once in src_done[src]; the warp
+// that completes the source's own_counts[src] * NB segments raises back[me] = seq in that
+// rank's arena (system-scope release after a system fence), and sources that sent no row
+// get their flag at the start. With a failure already recorded in the status word the
+// launch stores nothing into peers and raises no flag.
 struct CombineArgs {
   const int32_t* ids;      // [M, topk] expert ids; slots outside [0, E) contribute nothing
   const float* weights;    // [M, topk]
   int32_t* arrivals;       // [M, NB], zero before the launch
-  void* out;               // [M, n_out]
+  void* out;               // [M, n_out] (local mode)
   int topk;
+  // return mode
+  const int64_t* peer_base;   // [world] arena base of every rank
+  const int32_t* own_counts;  // [world] rows each source sent this step (own arena)
+  int32_t* src_done;          // [world] segments returned per source, zero before the launch
+  int64_t back_off, flag_off; // byte offsets of back_x and of the back flags in an arena
+  int64_t cap;                // rows per source region
+  int me, world;
+  uint32_t seq;
 };
+
+__device__ __forceinline__ void st_release_sys_u32(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 
 constexpr int kThreads = 256;
 constexpr int kGatherThreads = 64;  // warps 2-3 in MODE_GEMM1_GATHER
@@ -114,7 +135,7 @@ __device__ __forceinline__ void decode_tile(const int* s_bs, int E, int NB, int 
 // (lane = row) of the tile's columns [nb * BN, nb * BN + BN) are stored to `slots`.
 template <typename T, int BN>
 __device__ __forceinline__ void combine_rows(const CombineArgs& cmb, const T* slots, int my_pair, int E, int NB,
-                                             int nb, int n_out, int lane) {
+                                             int nb, int n_out, int lane, bool remote_off) {
   const int topk = cmb.topk;
   __threadfence();  // this lane's slot stores are visible device-wide before its rows' arrivals count
   __syncwarp();
@@ -194,7 +215,35 @@ __device__ __forceinline__ void combine_rows(const CombineArgs& cmb, const T* sl
       o.y = ElemTraits<T>::pack2(acc[q][2], acc[q][3]);
       o.z = ElemTraits<T>::pack2(acc[q][4], acc[q][5]);
       o.w = ElemTraits<T>::pack2(acc[q][6], acc[q][7]);
-      *reinterpret_cast<uint4*>(out + (int64_t)t[q] * n_out + col) = o;
+      if (cmb.peer_base == nullptr) {
+        *reinterpret_cast<uint4*>(out + (int64_t)t[q] * n_out + col) = o;
+      } else if (!remote_off) {
+        const int src = (int)(t[q] / cmb.cap);
+        const int64_t r = t[q] - (int64_t)src * cmb.cap;
+        T* dst = reinterpret_cast<T*>(reinterpret_cast<char*>(__ldg(cmb.peer_base + src)) + cmb.back_off);
+        *reinterpret_cast<uint4*>(dst + ((int64_t)cmb.me * cmb.cap + r) * n_out + col) = o;
+      }
+    }
+    if (cmb.peer_base != nullptr && !remote_off) {
+      // these rows' segments of n-block nb are in their sources' arenas: count them, and
+      // raise a source's flag when its last segment is in
+      __threadfence_system();
+      __syncwarp();
+      if (lane == 0) {
+#pragma unroll
+        for (int q = 0; q < kRows; ++q) {
+          if (t[q] < 0) continue;
+          const int src = (int)(t[q] / cmb.cap);
+          const int want = __ldcg(cmb.own_counts + src) * NB;
+          if (atomicAdd(cmb.src_done + src, 1) + 1 == want) {
+            __threadfence_system();
+            st_release_sys_u32(reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(__ldg(cmb.peer_base + src)) +
+                                                           cmb.flag_off) + cmb.me,
+                               cmb.seq);
+          }
+        }
+      }
+      __syncwarp();
     }
   }
 }
@@ -225,6 +274,7 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
   uint64_t* mma_done = bars + 2 * STAGES + 4;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + L::kMiscOffset);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + L::kMiscOffset + 4);
+  volatile int* s_remote_off = reinterpret_cast<volatile int*>(smem + L::kMiscOffset + 8);
   int* s_bs = reinterpret_cast<int*>(smem + L::kBlockStartOffset);
 
   const int warp = threadIdx.x >> 5;
@@ -236,7 +286,21 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
     for (int a = 0; a < 2; ++a) { mbar_init(&tmem_full[a], 1); mbar_init(&tmem_empty[a], 128); }
     mbar_init(mma_done, 1);
     *s_abort = 0;
+    // return mode: a failure already recorded keeps this launch away from the peers' arenas
+    *s_remote_off = (MODE == MODE_GEMM2_COMBINE && cmb.peer_base != nullptr && status != nullptr &&
+                     *reinterpret_cast<volatile int*>(status) != 0) ? 1 : 0;
     fence_mbar_init();
+  }
+  if constexpr (MODE == MODE_GEMM2_COMBINE) {
+    if (cmb.peer_base != nullptr && blockIdx.x == 0 && (int)threadIdx.x < cmb.world &&
+        (status == nullptr || *reinterpret_cast<volatile int*>(status) == 0) &&
+        __ldcg(cmb.own_counts + threadIdx.x) == 0) {
+      // a source that sent no row this step has nothing to wait for
+      __threadfence_system();
+      st_release_sys_u32(reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(__ldg(cmb.peer_base + threadIdx.x)) +
+                                                     cmb.flag_off) + cmb.me,
+                         cmb.seq);
+    }
   }
   if (warp == 0 && lane == 0) {
     if constexpr (!kGather) tma_prefetch_desc(&map_a);
@@ -437,7 +501,8 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
         }
         __syncwarp();
       }
-      if constexpr (MODE == MODE_GEMM2_COMBINE) combine_rows<T, BN>(cmb, out, my_pair, E, NB, nb, n_out, lane);
+      if constexpr (MODE == MODE_GEMM2_COMBINE)
+        combine_rows<T, BN>(cmb, out, my_pair, E, NB, nb, n_out, lane, *s_remote_off != 0);
       if (++acc == 2) { acc = 0; acc_phase ^= 1; }
     }
   }
@@ -570,11 +635,31 @@ cudaError_t launch_gemm2_scatter(int dtype, const void* act, int64_t rows_cap, c
                                        max_ctas, st, CombineArgs{});
 }
 
+cudaError_t launch_gemm2_return(int dtype, const void* act, int64_t rows_cap, const void* w2, int E, int K, int N,
+                                const int32_t* block_start, const int32_t* sorted_pairs, void* y_slots,
+                                const float* recv_w, const int32_t* recv_id, int topk, int32_t* arrivals,
+                                const int64_t* peer_base, const int32_t* own_counts, int32_t* src_done,
+                                int64_t back_off, int64_t flag_off, int64_t cap, int me, int world, uint32_t seq,
+                                int* status, int max_ctas, cudaStream_t st) {
+  CombineArgs cmb{recv_id, recv_w, arrivals, nullptr, topk};
+  cmb.peer_base = peer_base;
+  cmb.own_counts = own_counts;
+  cmb.src_done = src_done;
+  cmb.back_off = back_off;
+  cmb.flag_off = flag_off;
+  cmb.cap = cap;
+  cmb.me = me;
+  cmb.world = world;
+  cmb.seq = seq;
+  return launch_gemm2_mode<MODE_GEMM2_COMBINE>(dtype, act, rows_cap, w2, E, K, N, block_start, sorted_pairs, y_slots,
+                                               status, max_ctas, st, cmb);
+}
+
 cudaError_t launch_gemm2_combine(int dtype, const void* act, int64_t rows_cap, const void* w2, int E, int K, int N,
                                  const int32_t* block_start, const int32_t* sorted_pairs, void* y_slots,
                                  const float* topk_weights, const int32_t* topk_ids, int topk, int32_t* arrivals,
                                  void* out, int* status, int max_ctas, cudaStream_t st) {
-  const CombineArgs cmb{topk_ids, topk_weights, arrivals, out, topk};
+  CombineArgs cmb{topk_ids, topk_weights, arrivals, out, topk};
   return launch_gemm2_mode<MODE_GEMM2_COMBINE>(dtype, act, rows_cap, w2, E, K, N, block_start, sorted_pairs, y_slots,
                                                status, max_ctas, st, cmb);
 }

@@ -64,6 +64,16 @@ cudaError_t launch_gemm2_combine(int dtype, const void* act, int64_t rows_cap, c
                                  const int32_t* block_start, const int32_t* sorted_pairs, void* y_slots,
                                  const float* topk_weights, const int32_t* topk_ids, int topk, int32_t* arrivals,
                                  void* out, int* status, int max_ctas, cudaStream_t st);
+// The same, with each completed row returned into its source rank's arena over peer memory
+// (the expert-parallel layer): received row t = src * cap + r goes to back_x row me * cap + r
+// of rank src, whose back flag [me] is raised (= seq) when all of its rows are in; see
+// CombineArgs in moe_gemm.cu. arrivals [M, NB] and src_done [world] must be zero.
+cudaError_t launch_gemm2_return(int dtype, const void* act, int64_t rows_cap, const void* w2, int E, int K, int N,
+                                const int32_t* block_start, const int32_t* sorted_pairs, void* y_slots,
+                                const float* recv_w, const int32_t* recv_id, int topk, int32_t* arrivals,
+                                const int64_t* peer_base, const int32_t* own_counts, int32_t* src_done,
+                                int64_t back_off, int64_t flag_off, int64_t cap, int me, int world, uint32_t seq,
+                                int* status, int max_ctas, cudaStream_t st);
 cudaError_t launch_combine_prep(const int32_t* topk_ids, int64_t M, int topk, int E, int K, int32_t* arrivals,
                                 int64_t n_arrivals, int32_t* zero_ints, int n_zero, void* out, cudaStream_t st);
 
@@ -104,6 +114,21 @@ cudaError_t launch_gather_scales_t(const float* src, int64_t src_stride, int KB,
 // for the rows the align stage filled; dst rows are row_bytes apart.
 cudaError_t launch_gather_rows(const void* src, int64_t src_stride, int64_t row_bytes, const int32_t* sorted_pairs,
                                const int32_t* block_start, int E, int topk, int64_t cap, void* dst, cudaStream_t st);
+
+// FP8 GEMMs for decode-sized batches (moe_gemm_fp8_swap.cu): 128 weight rows x 32 tokens
+// per tile, with the expert's row counts (align `counts`) choosing the tiles on the device.
+// Same inputs and outputs as launch_fp8_gemm1 / launch_fp8_gemm2. The FP8 path takes them
+// when the experts average no more than kFp8SwapMaxRowsPerExpert rows (fp8_use_swap).
+constexpr int64_t kFp8SwapMaxRowsPerExpert = 16;
+bool fp8_use_swap(int64_t num_pairs, int E);
+cudaError_t launch_fp8_swap_gemm1(const void* xq_sorted, const float* xs_sorted_t, int64_t rows_cap,
+                                  int64_t num_pairs, const void* w1q, const float* w1s, int E, int K, int N,
+                                  const int32_t* counts, const int32_t* block_start, void* actq, float* acts_t,
+                                  int* status, int max_ctas, cudaStream_t st);
+cudaError_t launch_fp8_swap_gemm2(const void* actq, const float* acts_t, int64_t rows_cap, int64_t num_pairs,
+                                  const void* w2q, const float* w2s, int E, int K, int N, const int32_t* counts,
+                                  const int32_t* block_start, const int32_t* sorted_pairs, void* y_slots, int* status,
+                                  int max_ctas, cudaStream_t st);
 
 // Per row, per 128 columns e4m3 quantisation (dtype bf16 / fp16 / fp32 input): row m's codes
 // at q + m * ldq (bytes), its K / 128 scales at s + m * lds (floats).

@@ -172,8 +172,9 @@ class ExpertParallelMoE:
     def kernel_launches_per_step(self):
         """This library's kernels launched by one CUDA forward."""
         if self.transport == "p2p":
-            # routing, signal, dispatch, wait, align count, align scatter, GEMM1, GEMM2,
-            # fused combine + return, wait, EP combine (FP8: + quantise, row gather, scale gather)
+            # routing, signal, dispatch, wait, align count, align scatter, GEMM1, then bf16: set-up of
+            # the fused return + GEMM2 with the combine and return in its epilogue; FP8: GEMM2 +
+            # fused combine-and-return (+ quantise, row gather, scale gather); then wait, reduce
             return 14 if self.fp8 else 11
         # routing, then per chunk: EP count, EP pack, align count, align scatter, GEMM1, GEMM2,
         # combine, EP combine (FP8: + quantise once, row and scale gathers per chunk)
@@ -584,7 +585,7 @@ class ExpertParallelMoE:
             "cap": cap, "K": K, "dtype": dtype, "base": base.value, "bases": bases, "offs": list(offs), "seq": 0,
             "peer_bases": torch.tensor(bases, dtype=torch.int64, device=dev),
             "scr_d": torch.zeros(2 * self.world + 1, dtype=torch.int32, device=dev),
-            "scr_c": torch.zeros(1, dtype=torch.int32, device=dev),
+            "scr_c": torch.zeros(max(1, self.world), dtype=torch.int32, device=dev),
         }
         torch.cuda.synchronize(dev)
         dist.barrier(group=self.group)
@@ -701,17 +702,21 @@ class ExpertParallelMoE:
                                                       _ptr(self.w1), _ptr(self.w1s), _ptr(self.w2), _ptr(self.w2s),
                                                       None, ctypes.c_void_p(rid), R, E_l, k, K, N, None, ws, wsn, 0,
                                                       status, st), "moe_fused_experts_fp8_rows")
+            self._mark("experts")
+            # top-k combine of each valid received row, stored straight into its source's arena
+            _lib.check(lib.moe_p2p_combine_experts_back(dt_rows, ws, E_l, K, N, k, W, self.rank, cap, pb, base, seq,
+                                                        _ptr(p["scr_c"]), status, st), "moe_p2p_combine_experts_back")
         else:
             _lib.check(lib.moe_expert_align_gather(dt, ctypes.c_void_p(rx), ctypes.c_void_p(rid), R, E_l, k, K, N,
                                                    ws, wsn, st), "moe_expert_align_gather")
             _lib.check(lib.moe_expert_gemm1(dt, _ptr(self.w1), R, E_l, k, K, N, ws, wsn, status, 0, st),
                        "moe_expert_gemm1")
-            _lib.check(lib.moe_expert_gemm2(dt, _ptr(self.w2), R, E_l, k, K, N, ws, wsn, status, 0, st),
-                       "moe_expert_gemm2")
-        self._mark("experts")
-        # top-k combine of each valid received row, stored straight into its source's arena
-        _lib.check(lib.moe_p2p_combine_experts_back(dt_rows, ws, E_l, K, N, k, W, self.rank, cap, pb, base, seq,
-                                                    _ptr(p["scr_c"]), status, st), "moe_p2p_combine_experts_back")
+            # the down GEMM's epilogue sums each received row's slots and stores the sum into its
+            # source rank's arena over NVLink while the GEMM still runs (one kernel)
+            _lib.check(lib.moe_p2p_expert_gemm2_return(dt, _ptr(self.w2), ws, wsn, E_l, K, N, k, W, self.rank, cap,
+                                                       pb, base, seq, _ptr(p["scr_c"]), status, 0, st),
+                       "moe_p2p_expert_gemm2_return")
+            self._mark("experts")
         _lib.check(lib.moe_p2p_wait(base, W, 2, cap, K, k, seq, status, st), "moe_p2p_wait")
         self._mark("combine_back")
         out = torch.empty(M, K, dtype=x.dtype, device=dev)
