@@ -54,12 +54,23 @@ cudaError_t fp8_expert_rows(const F8Layout2& l, uint8_t* ws, const uint8_t* q, i
   if (err == cudaSuccess)
     err = launch_gather_scales_t(s, lds, K / 128, sorted, am.block_start, E, topk, l.cap,
                                  reinterpret_cast<float*>(ws + l.xs_s), st);
-  if (err == cudaSuccess)
-    err = launch_fp8_gemm1(ws + l.xq_s, reinterpret_cast<const float*>(ws + l.xs_s), l.cap, w1_q, w1_scale, E, K, N,
-                           am.block_start, ws + l.actq, reinterpret_cast<float*>(ws + l.acts), status, max_ctas, st);
-  if (err == cudaSuccess)
-    err = launch_fp8_gemm2(ws + l.actq, reinterpret_cast<const float*>(ws + l.acts), l.cap, w2_q, w2_scale, E, K, N,
-                           am.block_start, sorted, ws + l.y, status, max_ctas, st);
+  if (fp8_use_swap(P, E)) {  // a few rows per expert: weight rows x 32-token tiles
+    if (err == cudaSuccess)
+      err = launch_fp8_swap_gemm1(ws + l.xq_s, reinterpret_cast<const float*>(ws + l.xs_s), l.cap, P, w1_q, w1_scale,
+                                  E, K, N, am.counts, am.block_start, ws + l.actq,
+                                  reinterpret_cast<float*>(ws + l.acts), status, max_ctas, st);
+    if (err == cudaSuccess)
+      err = launch_fp8_swap_gemm2(ws + l.actq, reinterpret_cast<const float*>(ws + l.acts), l.cap, P, w2_q, w2_scale,
+                                  E, K, N, am.counts, am.block_start, sorted, ws + l.y, status, max_ctas, st);
+  } else {
+    if (err == cudaSuccess)
+      err = launch_fp8_gemm1(ws + l.xq_s, reinterpret_cast<const float*>(ws + l.xs_s), l.cap, w1_q, w1_scale, E, K,
+                             N, am.block_start, ws + l.actq, reinterpret_cast<float*>(ws + l.acts), status, max_ctas,
+                             st);
+    if (err == cudaSuccess)
+      err = launch_fp8_gemm2(ws + l.actq, reinterpret_cast<const float*>(ws + l.acts), l.cap, w2_q, w2_scale, E, K,
+                             N, am.block_start, sorted, ws + l.y, status, max_ctas, st);
+  }
   if (err == cudaSuccess && out)
     err = launch_combine(MOE_DTYPE_BF16, ws + l.y, topk_weights, topk_ids, M, topk, E, K, out, st);
   return err;

@@ -123,6 +123,19 @@ __device__ __forceinline__ void tmem_wait_ld_regs(uint32_t (&r)[32]) {
                : "memory");
 }
 
+// Ties the registers of a second tcgen05.ld to a point after the preceding wait (both asm
+// statements are volatile, so they keep their order): uses of r cannot move above it.
+__device__ __forceinline__ void reg_order32(uint32_t (&r)[32]) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                 "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                 "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
+}
+
 // tot[p0 + i] += (v[2i], v[2i + 1]) * f for i < 16: 32 partial columns into 16 fp32 pairs.
 __device__ __forceinline__ void promote32(float2 (&tot)[64], int p0, const uint32_t (&v)[32], float2 f) {
 #pragma unroll
@@ -331,23 +344,24 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
         tc_fence_after();
         const uint32_t t_addr = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(pb * kF8BN + h * 128);
-        // four 32-column loads, each overlapped with the FMAs of the previous one
+        // the 128 columns in two pairs of 32-column loads, each pair in flight together under
+        // one wait (a wait per load left four load latencies in a row per K block)
         uint32_t va[32], vb[32];
         tmem_ld32(t_addr, va);
-        tmem_wait_ld_regs(va);
         tmem_ld32(t_addr + 32, vb);
-        promote32(tot, 0, va, f_lo);
-        tmem_wait_ld_regs(vb);
-        tmem_ld32(t_addr + 64, va);
-        promote32(tot, 16, vb, f_lo);
         tmem_wait_ld_regs(va);
+        reg_order32(vb);
+        promote32(tot, 0, va, f_lo);
+        promote32(tot, 16, vb, f_lo);
+        tmem_ld32(t_addr + 64, va);
         tmem_ld32(t_addr + 96, vb);
-        promote32(tot, 32, va, f_hi);
-        tmem_wait_ld_regs(vb);
+        tmem_wait_ld_regs(va);
+        reg_order32(vb);
         // the partial is in registers: hand the buffer back before the last FMAs
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&pempty[pb]);
+        promote32(tot, 32, va, f_hi);
         promote32(tot, 48, vb, f_hi);
         if (++pb == 2) { pb = 0; pphase ^= 1; }
       }

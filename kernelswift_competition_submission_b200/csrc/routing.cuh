@@ -91,6 +91,57 @@ __device__ __forceinline__ void route_select_sorted8(const float (&c)[8], const 
   }
 }
 
+// Top-k selection for any VPL: per-lane insertion sort of the candidates (value descending,
+// equal values in index order), then per round a warp arg-max of the heads.
+template <int VPL>
+__device__ __forceinline__ void route_select_insertion(float (&c)[VPL], float (&s)[VPL], int e0, int lane,
+                                                       int64_t tok, int topk, int renormalize, float scale,
+                                                       float* __restrict__ out_w, int32_t* __restrict__ out_ids) {
+  // sort this lane's candidates: value descending; equal values keep index order
+  int id[VPL];
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) id[i] = e0 + i;
+#pragma unroll
+  for (int i = 1; i < VPL; ++i) {
+#pragma unroll
+    for (int j = i; j > 0; --j) {
+      if (c[j] > c[j - 1]) {
+        const float tc = c[j]; c[j] = c[j - 1]; c[j - 1] = tc;
+        const float ts = s[j]; s[j] = s[j - 1]; s[j - 1] = ts;
+        const int ti = id[j]; id[j] = id[j - 1]; id[j - 1] = ti;
+      }
+    }
+  }
+
+  float my_w = 0.f;
+  int my_id = 0;
+  for (int r = 0; r < topk; ++r) {
+    // warp arg-max of the heads in two reductions: the largest value (as an order-preserving
+    // integer key), then the lowest index among the lanes holding it
+    const unsigned kmax = __reduce_max_sync(0xffffffffu, ordered_key(c[0]));
+    const int bi = (int)__reduce_min_sync(0xffffffffu, ordered_key(c[0]) == kmax ? (unsigned)id[0] : 0xffffffffu);
+    const int owner = bi / VPL;
+    const float bs = __shfl_sync(0xffffffffu, s[0], owner);
+    if (lane == owner) {  // pop the head
+#pragma unroll
+      for (int i = 0; i + 1 < VPL; ++i) { c[i] = c[i + 1]; s[i] = s[i + 1]; id[i] = id[i + 1]; }
+      c[VPL - 1] = -INFINITY;
+      id[VPL - 1] = INT_MAX;
+    }
+    if (lane == r) { my_w = bs; my_id = bi; }
+  }
+
+  if (renormalize) {
+    const float tot = route_warp_sum(lane < topk ? my_w : 0.f);
+    my_w = my_w / tot;
+  }
+  if (scale != 1.0f) my_w *= scale;
+  if (lane < topk) {
+    out_w[tok * topk + lane] = my_w;
+    out_ids[tok * topk + lane] = my_id;
+  }
+}
+
 // Register-only variant for the common layouts: E = 32 * VPL (every lane full) and,
 // when groups are masked, groups of whole lanes (LPG = E / n_group / VPL lanes per
 // group, a power of two): a group's top-2 sum (or max) is a per-lane reduction over
@@ -182,52 +233,9 @@ __device__ __forceinline__ void route_token_lanes(const float* row, const float*
 
   if constexpr (VPL == 8) {
     route_select_sorted8(c, s, e0, lane, tok, topk, renormalize, scale, out_w, out_ids);
-    return;
-  }
-  // sort this lane's candidates: value descending; equal values keep index order
-  int id[VPL];
-#pragma unroll
-  for (int i = 0; i < VPL; ++i) id[i] = e0 + i;
-#pragma unroll
-  for (int i = 1; i < VPL; ++i) {
-#pragma unroll
-    for (int j = i; j > 0; --j) {
-      if (c[j] > c[j - 1]) {
-        const float tc = c[j]; c[j] = c[j - 1]; c[j - 1] = tc;
-        const float ts = s[j]; s[j] = s[j - 1]; s[j - 1] = ts;
-        const int ti = id[j]; id[j] = id[j - 1]; id[j - 1] = ti;
-      }
-    }
-  }
-
-  float my_w = 0.f;
-  int my_id = 0;
-  for (int r = 0; r < topk; ++r) {
-    // warp arg-max of the heads in two reductions: the largest value (as an order-preserving
-    // integer key), then the lowest index among the lanes holding it
-    const unsigned kmax = __reduce_max_sync(0xffffffffu, ordered_key(c[0]));
-    const int bi = (int)__reduce_min_sync(0xffffffffu, ordered_key(c[0]) == kmax ? (unsigned)id[0] : 0xffffffffu);
-    const int owner = bi / VPL;
-    const float bs = __shfl_sync(0xffffffffu, s[0], owner);
-    if (lane == owner) {  // pop the head
-#pragma unroll
-      for (int i = 0; i + 1 < VPL; ++i) { c[i] = c[i + 1]; s[i] = s[i + 1]; id[i] = id[i + 1]; }
-      c[VPL - 1] = -INFINITY;
-      id[VPL - 1] = INT_MAX;
-    }
-    if (lane == r) { my_w = bs; my_id = bi; }
-  }
-
-  if (renormalize) {
-    const float tot = route_warp_sum(lane < topk ? my_w : 0.f);
-    my_w = my_w / tot;
-  }
-  if (scale != 1.0f) my_w *= scale;
-  if (lane < topk) {
-    out_w[tok * topk + lane] = my_w;
-    out_ids[tok * topk + lane] = my_id;
+  } else {
+    route_select_insertion<VPL>(c, s, e0, lane, tok, topk, renormalize, scale, out_w, out_ids);
   }
 }
-
 
 }  // namespace moe
