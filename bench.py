@@ -310,8 +310,8 @@ def config_rows(dev, w1, w2, peaks, iters):
     """The other configurations of the layer on one GPU, each timed per call (median of
     `iters` after 3 warm-ups, L2 flushed before each call): grouped_topk alone (M = 128 and
     32768), Mixtral bf16 (M = 256), the DeepSeek-V3 bf16 layer at M = 1, 64, 512, 4096, the
-    FP8 w8a8 layer at M = 1, 8, 32, 128, and the reference's task shapes through the drop-in
-    modules (the harness's per-call protocol)."""
+    FP8 w8a8 layer at M = 1, 8, 32, 128, both at decode sizes also replayed as CUDA graphs, and
+    the reference's task shapes through the drop-in modules (the harness's per-call protocol)."""
     import torch
 
     from kernelswift_competition_submission_b200 import ops
@@ -371,24 +371,29 @@ def config_rows(dev, w1, w2, peaks, iters):
             nbytes, A = _layer_bytes(ids, E, K, N, M, k, 1 if fp8 else 2, scale_bytes)
             rows.append(_row("dsv3_fp8" if fp8 else "dsv3_bf16", M, ms, 6.0 * M * k * K * N, nbytes, peaks,
                              bf16 * (2.0 if fp8 else 1.0), experts_hit=A))
-    del w1q, w2q, w1s, w2s
-    # decode sizes: the bf16 layer eager (one launch per kernel) and replayed as one CUDA graph
+    # decode sizes: the layer eager (one launch per kernel) and replayed as one CUDA graph,
+    # bf16 at M = 1, 8, 64 and FP8 w8a8 at M = 1, 8, 32, 128
     from kernelswift_competition_submission_b200.graphs import GraphCache
 
-    for M in (1, 8, 64):
-        x, g, b_ = _dsv3_inputs(M, dev)
+    for fp8, Ms in ((False, (1, 8, 64)), (True, (1, 8, 32, 128))):
+        for M in Ms:
+            x, g, b_ = _dsv3_inputs(M, dev)
 
-        def decode(xx, gg):
-            return ops.moe_layer(xx, gg, w1, w2, topk=k, renormalize=True, num_expert_group=8, topk_group=4,
-                                 scoring_func="sigmoid", routed_scaling_factor=2.5, e_score_correction_bias=b_)
+            def decode(xx, gg):
+                w_, i_ = ops.grouped_topk(xx, gg, k, True, 8, 4, "sigmoid", 2.5, e_score_correction_bias=b_)
+                if fp8:
+                    return ops.fused_moe_fp8(xx, w1q, w1s, w2q, w2s, w_, i_)
+                return ops.fused_moe(xx, w1, w2, w_, i_)
 
-        eager = timer.median_ms(lambda: decode(x, g), iters)
-        cache = GraphCache(decode)
-        graph = timer.median_ms(lambda: cache(x, g), iters)
-        ids = ops.grouped_topk(x, g, k, True, 8, 4, "sigmoid", 2.5, e_score_correction_bias=b_)[1]
-        nbytes, A = _layer_bytes(ids, E, K, N, M, k, 2)
-        rows.append(_row("dsv3_bf16_graph", M, graph, 6.0 * M * k * K * N, nbytes, peaks, bf16, experts_hit=A,
-                         eager_ms=eager))
+            eager = timer.median_ms(lambda: decode(x, g), iters)
+            cache = GraphCache(decode)
+            graph = timer.median_ms(lambda: cache(x, g), iters)
+            ids = ops.grouped_topk(x, g, k, True, 8, 4, "sigmoid", 2.5, e_score_correction_bias=b_)[1]
+            scale_bytes = 3 * (K // 128) * (N // 128) * 4 if fp8 else 0
+            nbytes, A = _layer_bytes(ids, E, K, N, M, k, 1 if fp8 else 2, scale_bytes)
+            rows.append(_row("dsv3_fp8_graph" if fp8 else "dsv3_bf16_graph", M, graph, 6.0 * M * k * K * N, nbytes,
+                             peaks, bf16 * (2.0 if fp8 else 1.0), experts_hit=A, eager_ms=eager))
+    del w1q, w2q, w1s, w2s
     # router GEMM fused with grouped_topk against the unfused pair (torch bf16 GEMM + grouped_topk)
     wg = (torch.randn(E, K, generator=torch.Generator(device=dev).manual_seed(7), device=dev) / K ** 0.5).bfloat16()
     for M in (1, 128, 4096, 32768):

@@ -237,6 +237,9 @@ MOE_API int moe_expert_combine(int dtype, const float* topk_weights, const int32
  * (no counterpart in the reference, whose path is fp16/bf16/fp32 only):
  *   scale = amax(|block|) / 448 (1.0 for an all-zero block), q = e4m3(x / scale),
  *   rounded to nearest even, saturating at +-448.
+ * scale_fmt MOE_FP8_SCALE_FP32 keeps that fp32 scale; MOE_FP8_SCALE_UE8M0 rounds it
+ * up to the next power of two (an exact UE8M0 code, the block-scale format of
+ * tcgen05's kind::mxf8f6f4 MMA).
  *   moe_quantize_rows_fp8    per row, per 128 columns (activations, per token):
  *                            x [num_rows, cols] -> q uint8 [num_rows, cols],
  *                            scales fp32 [num_rows, cols / 128]
@@ -245,10 +248,12 @@ MOE_API int moe_expert_combine(int dtype, const float* topk_weights, const int32
  *                            [batch, rows, cols], scales fp32 [batch, rows/128, cols/128]
  * dtype: MOE_DTYPE_BF16, MOE_DTYPE_FP16 or MOE_DTYPE_FP32. cols (and rows) % 128 == 0.
  */
+#define MOE_FP8_SCALE_FP32 0
+#define MOE_FP8_SCALE_UE8M0 1
 MOE_API int moe_quantize_rows_fp8(int dtype, const void* x, int64_t num_rows, int cols, void* q,
-                                  float* scales, void* stream);
+                                  float* scales, int scale_fmt, void* stream);
 MOE_API int moe_quantize_blocks_fp8(int dtype, const void* w, int64_t batch, int rows, int cols, void* q,
-                                    float* scales, void* stream);
+                                    float* scales, int scale_fmt, void* stream);
 
 /*
  * Expert computation of the FP8 w8a8 configuration (DeepSeek-V3 recipe; no
@@ -259,23 +264,32 @@ MOE_API int moe_quantize_blocks_fp8(int dtype, const void* w, int64_t batch, int
  *   w2_q, w2_scale e4m3 [E, K, N]  and fp32 [E, K/128, N/128]
  *   out            bf16 [num_tokens, hidden_size]
  * The SiLU*mul output is quantised per row per 128 before the down projection.
- * Both GEMMs run tcgen05.mma.kind::f8f6f4 on the e4m3 operands, one MMA chain per
- * 128-wide K block, and promote each block's fp32 partial sums into the totals
- * with its row and weight scales. Requires hidden_size % 128 == 0 and
- * intermediate_size % 128 == 0.
+ * scale_fmt names the scales of the weights, and the tokens and SiLU*mul rows are
+ * quantised the same way:
+ *   MOE_FP8_SCALE_FP32   any fp32 scales: both GEMMs run tcgen05.mma.kind::f8f6f4,
+ *                        one MMA chain per 128-wide K block, and promote each
+ *                        block's fp32 partial sums into the totals with its row
+ *                        and weight scales.
+ *   MOE_FP8_SCALE_UE8M0  the caller promises every weight scale is a power of two
+ *                        (moe_quantize_blocks_fp8 with MOE_FP8_SCALE_UE8M0): at
+ *                        prefill sizes the GEMMs run kind::mxf8f6f4.block_scale,
+ *                        the tensor cores apply the scales, and one MMA chain
+ *                        covers the whole K (no promotion).
+ * Requires hidden_size % 128 == 0 and intermediate_size % 128 == 0.
  */
 MOE_API size_t moe_fused_workspace_bytes_fp8(int64_t num_tokens, int num_experts, int topk, int hidden_size,
                                              int intermediate_size);
 MOE_API int moe_fused_experts_fp8(const void* hidden_states, const void* w1_q, const float* w1_scale,
                                   const void* w2_q, const float* w2_scale, const float* topk_weights,
                                   const int32_t* topk_ids, int64_t num_tokens, int num_experts, int topk,
-                                  int hidden_size, int intermediate_size, void* out, void* workspace,
-                                  size_t workspace_bytes, int* status, void* stream);
+                                  int hidden_size, int intermediate_size, int scale_fmt, void* out,
+                                  void* workspace, size_t workspace_bytes, int* status, void* stream);
 
 /*
  * FP8 expert path from token rows quantised elsewhere (the expert-parallel FP8
  * payload, MOE_DTYPE_E4M3_ROW): row t is `rows + t * row_stride`, its hidden_size
- * e4m3 codes followed by hidden_size / 128 fp32 scales. row_stride >=
+ * e4m3 codes followed by hidden_size / 128 fp32 scales (powers of two with
+ * MOE_FP8_SCALE_UE8M0, as the weights'). row_stride >=
  * moe_fp8_row_bytes(hidden_size) and a multiple of 16. Same workspace as
  * moe_fused_experts_fp8. topk_ids may hold -1 (slot skipped). With out == NULL
  * the combine is left out and the per-slot rows stay in the workspace, for
@@ -290,12 +304,13 @@ MOE_API int moe_fused_experts_fp8(const void* hidden_states, const void* w1_q, c
  */
 MOE_API int64_t moe_fp8_row_bytes(int hidden_size);
 MOE_API int moe_quantize_rows_fp8_packed(int dtype, const void* x, int64_t num_rows, int cols, void* rows,
-                                         void* stream);
+                                         int scale_fmt, void* stream);
 MOE_API int moe_fused_experts_fp8_rows(const void* rows, int64_t row_stride, const void* w1_q, const float* w1_scale,
                                        const void* w2_q, const float* w2_scale, const float* topk_weights,
                                        const int32_t* topk_ids, int64_t num_tokens, int num_experts, int topk,
-                                       int hidden_size, int intermediate_size, void* out, void* workspace,
-                                       size_t workspace_bytes, int max_ctas, int* status, void* stream);
+                                       int hidden_size, int intermediate_size, int scale_fmt, void* out,
+                                       void* workspace, size_t workspace_bytes, int max_ctas, int* status,
+                                       void* stream);
 
 /*
  * Expert-parallel dispatch / combine (the reference has no multi-device code;

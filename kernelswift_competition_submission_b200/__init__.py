@@ -22,6 +22,7 @@ from .ops import (  # noqa: F401
     fused_moe_fp8_rows,
     fused_moe_workspace_bytes,
     grouped_topk,
+    is_ue8m0,
     moe_align,
     moe_layer,
     quantize_rows_fp8,
@@ -29,10 +30,12 @@ from .ops import (  # noqa: F401
     quantize_weights_fp8,
     router_grouped_topk,
     softmax_topk,
+    weights_scale_format,
 )
 
 from . import torch_ops  # noqa: E402,F401  (registers torch.ops.moe_b200.*)
 
 __all__ = ["grouped_topk", "fused_moe", "fused_moe_fp8", "softmax_topk", "moe_align", "moe_layer",
            "fused_moe_workspace_bytes", "quantize_rows_fp8", "quantize_weights_fp8", "check_device_status",
-           "router_grouped_topk", "fp8_row_bytes", "quantize_rows_fp8_packed", "fused_moe_fp8_rows"]
+           "router_grouped_topk", "fp8_row_bytes", "quantize_rows_fp8_packed", "fused_moe_fp8_rows",
+           "is_ue8m0", "weights_scale_format"]

@@ -33,6 +33,8 @@ MOE_DTYPE_BF16 = 0
 MOE_DTYPE_FP16 = 1
 MOE_DTYPE_FP32 = 2
 MOE_DTYPE_E4M3_ROW = 3
+MOE_FP8_SCALE_FP32 = 0
+MOE_FP8_SCALE_UE8M0 = 1
 
 _c_p = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -61,15 +63,15 @@ SIGNATURES = {
     "moe_expert_gemm2_combine": (_i32, [_i32, _c_p, _c_p, _c_p, _i64, _i32, _i32, _i32, _i32, _c_p, _c_p, _sz, _c_p,
                                         _i32, _c_p]),
     "moe_expert_combine": (_i32, [_i32, _c_p, _c_p, _i64, _i32, _i32, _i32, _i32, _c_p, _c_p, _sz, _c_p]),
-    "moe_quantize_rows_fp8": (_i32, [_i32, _c_p, _i64, _i32, _c_p, _c_p, _c_p]),
-    "moe_quantize_blocks_fp8": (_i32, [_i32, _c_p, _i64, _i32, _i32, _c_p, _c_p, _c_p]),
+    "moe_quantize_rows_fp8": (_i32, [_i32, _c_p, _i64, _i32, _c_p, _c_p, _i32, _c_p]),
+    "moe_quantize_blocks_fp8": (_i32, [_i32, _c_p, _i64, _i32, _i32, _c_p, _c_p, _i32, _c_p]),
     "moe_fused_workspace_bytes_fp8": (_sz, [_i64, _i32, _i32, _i32, _i32]),
-    "moe_fused_experts_fp8": (_i32, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _i64, _i32, _i32, _i32, _i32, _c_p,
-                                     _c_p, _sz, _c_p, _c_p]),
+    "moe_fused_experts_fp8": (_i32, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _i64, _i32, _i32, _i32, _i32, _i32,
+                                     _c_p, _c_p, _sz, _c_p, _c_p]),
     "moe_fp8_row_bytes": (_i64, [_i32]),
-    "moe_quantize_rows_fp8_packed": (_i32, [_i32, _c_p, _i64, _i32, _c_p, _c_p]),
+    "moe_quantize_rows_fp8_packed": (_i32, [_i32, _c_p, _i64, _i32, _c_p, _i32, _c_p]),
     "moe_fused_experts_fp8_rows": (_i32, [_c_p, _i64, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _i64, _i32, _i32, _i32, _i32,
-                                          _c_p, _c_p, _sz, _i32, _c_p, _c_p]),
+                                          _i32, _c_p, _c_p, _sz, _i32, _c_p, _c_p]),
     "moe_ep_send_capacity": (_i64, [_i64, _i32, _i32]),
     "moe_ep_plan": (_i32, [_c_p, _i64, _i32, _i32, _i32, _c_p, _c_p, _c_p, _c_p]),
     "moe_ep_pack": (_i32, [_i32, _c_p, _c_p, _c_p, _i64, _i32, _i32, _i32, _i32, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p]),

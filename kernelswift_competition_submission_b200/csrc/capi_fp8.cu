@@ -43,33 +43,36 @@ F8Layout2 fp8_layout(int64_t M, int E, int topk, int K, int N) {
 cudaError_t fp8_expert_rows(const F8Layout2& l, uint8_t* ws, const uint8_t* q, int64_t ldq, const float* s,
                             int64_t lds, const void* w1_q, const float* w1_scale, const void* w2_q,
                             const float* w2_scale, const float* topk_weights, const int32_t* topk_ids, int64_t M,
-                            int E, int topk, int K, int N, void* out, int max_ctas, int* status, cudaStream_t st) {
+                            int E, int topk, int K, int N, bool ue8m0, void* out, int max_ctas, int* status,
+                            cudaStream_t st) {
   const int64_t P = M * topk;
+  const bool swap = fp8_use_swap(P, E);
   int32_t* meta = reinterpret_cast<int32_t*>(ws + l.meta);
   int32_t* sorted = reinterpret_cast<int32_t*>(ws + l.sorted);
   const AlignMeta am = align_meta_contiguous(meta, E);
   cudaError_t err = launch_align(topk_ids, P, topk, E, kBlockM, am, true, sorted, l.cap, nullptr, nullptr, 0, st);
   if (err == cudaSuccess)
     err = launch_gather_rows(q, ldq, K, sorted, am.block_start, E, topk, l.cap, ws + l.xq_s, st);
+  // the block-scaled GEMMs read the row scales as UE8M0 atoms, the others as fp32
   if (err == cudaSuccess)
-    err = launch_gather_scales_t(s, lds, K / 128, sorted, am.block_start, E, topk, l.cap,
+    err = launch_gather_scales_t(s, lds, K / 128, sorted, am.block_start, E, topk, l.cap, ue8m0 && !swap,
                                  reinterpret_cast<float*>(ws + l.xs_s), st);
-  if (fp8_use_swap(P, E)) {  // a few rows per expert: weight rows x 32-token tiles
+  if (swap) {  // a few rows per expert: weight rows x 32-token tiles
     if (err == cudaSuccess)
       err = launch_fp8_swap_gemm1(ws + l.xq_s, reinterpret_cast<const float*>(ws + l.xs_s), l.cap, P, w1_q, w1_scale,
                                   E, K, N, am.counts, am.block_start, ws + l.actq,
-                                  reinterpret_cast<float*>(ws + l.acts), status, max_ctas, st);
+                                  reinterpret_cast<float*>(ws + l.acts), ue8m0, status, max_ctas, st);
     if (err == cudaSuccess)
       err = launch_fp8_swap_gemm2(ws + l.actq, reinterpret_cast<const float*>(ws + l.acts), l.cap, P, w2_q, w2_scale,
                                   E, K, N, am.counts, am.block_start, sorted, ws + l.y, status, max_ctas, st);
   } else {
     if (err == cudaSuccess)
       err = launch_fp8_gemm1(ws + l.xq_s, reinterpret_cast<const float*>(ws + l.xs_s), l.cap, w1_q, w1_scale, E, K,
-                             N, am.block_start, ws + l.actq, reinterpret_cast<float*>(ws + l.acts), status, max_ctas,
-                             st);
+                             N, am.block_start, ws + l.actq, reinterpret_cast<float*>(ws + l.acts), ue8m0, status,
+                             max_ctas, st);
     if (err == cudaSuccess)
       err = launch_fp8_gemm2(ws + l.actq, reinterpret_cast<const float*>(ws + l.acts), l.cap, w2_q, w2_scale, E, K,
-                             N, am.block_start, sorted, ws + l.y, status, max_ctas, st);
+                             N, am.block_start, sorted, ws + l.y, ue8m0, status, max_ctas, st);
   }
   if (err == cudaSuccess && out)
     err = launch_combine(MOE_DTYPE_BF16, ws + l.y, topk_weights, topk_ids, M, topk, E, K, out, st);
@@ -100,13 +103,15 @@ extern "C" size_t moe_fused_workspace_bytes_fp8(int64_t num_tokens, int num_expe
 extern "C" int moe_fused_experts_fp8(const void* hidden_states, const void* w1_q, const float* w1_scale,
                                      const void* w2_q, const float* w2_scale, const float* topk_weights,
                                      const int32_t* topk_ids, int64_t num_tokens, int num_experts, int topk,
-                                     int hidden_size, int intermediate_size, void* out, void* workspace,
-                                     size_t workspace_bytes, int* status, void* stream) {
+                                     int hidden_size, int intermediate_size, int scale_fmt, void* out,
+                                     void* workspace, size_t workspace_bytes, int* status, void* stream) {
   using namespace moe;
   const int64_t M = num_tokens;
   const int E = num_experts, K = hidden_size, N = intermediate_size;
   const int shape = fp8_shape_ok(M, E, topk, K, N);
   if (shape != MOE_OK) return shape;
+  if (!scale_fmt_ok(scale_fmt)) return MOE_ERR_INVALID_ARG;
+  const bool ue8m0 = scale_fmt == MOE_FP8_SCALE_UE8M0;
   if (M == 0) return MOE_OK;
   if (!hidden_states || !w1_q || !w1_scale || !w2_q || !w2_scale || !topk_weights || !topk_ids || !out || !workspace)
     return MOE_ERR_INVALID_ARG;
@@ -119,10 +124,10 @@ extern "C" int moe_fused_experts_fp8(const void* hidden_states, const void* w1_q
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t err = launch_quantize_rows(MOE_DTYPE_BF16, hidden_states, M, K, ws + l.xq, K,
-                                         reinterpret_cast<float*>(ws + l.xs), K / 128, st);
+                                         reinterpret_cast<float*>(ws + l.xs), K / 128, ue8m0, st);
   if (err == cudaSuccess)
     err = fp8_expert_rows(l, ws, ws + l.xq, K, reinterpret_cast<const float*>(ws + l.xs), K / 128, w1_q, w1_scale,
-                          w2_q, w2_scale, topk_weights, topk_ids, M, E, topk, K, N, out, 0, status, st);
+                          w2_q, w2_scale, topk_weights, topk_ids, M, E, topk, K, N, ue8m0, out, 0, status, st);
   return err == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
 }
 
@@ -130,13 +135,14 @@ extern "C" int moe_fused_experts_fp8_rows(const void* rows, int64_t row_stride, 
                                           const float* w1_scale, const void* w2_q, const float* w2_scale,
                                           const float* topk_weights, const int32_t* topk_ids, int64_t num_tokens,
                                           int num_experts, int topk, int hidden_size, int intermediate_size,
-                                          void* out, void* workspace, size_t workspace_bytes, int max_ctas,
-                                          int* status, void* stream) {
+                                          int scale_fmt, void* out, void* workspace, size_t workspace_bytes,
+                                          int max_ctas, int* status, void* stream) {
   using namespace moe;
   const int64_t M = num_tokens;
   const int E = num_experts, K = hidden_size, N = intermediate_size;
   const int shape = fp8_shape_ok(M, E, topk, K, N);
   if (shape != MOE_OK) return shape;
+  if (!scale_fmt_ok(scale_fmt)) return MOE_ERR_INVALID_ARG;
   if (row_stride < fp8_row_bytes(K) || row_stride % 16 != 0 || max_ctas < 0) return MOE_ERR_INVALID_ARG;
   if (M == 0) return MOE_OK;
   if (!rows || !w1_q || !w1_scale || !w2_q || !w2_scale || !topk_ids || (out && !topk_weights) || !workspace)
@@ -151,7 +157,7 @@ extern "C" int moe_fused_experts_fp8_rows(const void* rows, int64_t row_stride, 
   const uint8_t* r = static_cast<const uint8_t*>(rows);
   const cudaError_t err =
       fp8_expert_rows(l, static_cast<uint8_t*>(workspace), r, row_stride, reinterpret_cast<const float*>(r + K),
-                      row_stride / 4, w1_q, w1_scale, w2_q, w2_scale, topk_weights, topk_ids, M, E, topk, K, N, out,
-                      max_ctas, status, static_cast<cudaStream_t>(stream));
+                      row_stride / 4, w1_q, w1_scale, w2_q, w2_scale, topk_weights, topk_ids, M, E, topk, K, N,
+                      scale_fmt == MOE_FP8_SCALE_UE8M0, out, max_ctas, status, static_cast<cudaStream_t>(stream));
   return err == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
 }

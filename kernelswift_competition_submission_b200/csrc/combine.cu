@@ -4,7 +4,8 @@
 // fused_moe/v1/fused_moe.py:221-252, reduced over the topk slots instead of all
 // experts (the reference's own pending idea, fused_moe/README.md "partial[TOP_K,T,H]").
 // Each thread owns 8 consecutive hidden elements (one 16-byte vector) of a token;
-// slot rows of a token are contiguous, so every load and store is coalesced.
+// slot rows of a token are contiguous, so every load and store is coalesced, and the
+// loads of up to 8 slots are in flight together.
 #include "common.cuh"
 #include "moe_internal.h"
 
@@ -22,17 +23,30 @@ combine_kernel(const uint4* __restrict__ y, const float* __restrict__ w, const i
   const int v = (int)(gid - t * vecs_per_row);
   if (t >= M) return;
   float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  for (int j = 0; j < topk; ++j) {
-    const int e = __ldg(ids + t * topk + j);
-    if (e < 0 || e >= E) continue;
-    const float wj = __ldg(w + t * topk + j);
-    const uint4 q = __ldg(y + (t * topk + j) * vecs_per_row + v);
-    const uint32_t u[4] = {q.x, q.y, q.z, q.w};
+  // slots in batches of 8: every load of a batch is issued before the first FMA; the FMAs
+  // then run in slot order, skipping slots whose expert is outside [0, E)
+  for (int j0 = 0; j0 < topk; j0 += 8) {
+    uint4 q[8];
+    float wj[8];
+    bool ok[8];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 f = ElemTraits<T>::unpack2(u[i]);
-      acc[2 * i] = fmaf(wj, f.x, acc[2 * i]);
-      acc[2 * i + 1] = fmaf(wj, f.y, acc[2 * i + 1]);
+    for (int u = 0; u < 8; ++u) {
+      const int j = j0 + u;
+      const int e = j < topk ? __ldg(ids + t * topk + j) : -1;
+      ok[u] = e >= 0 && e < E;
+      wj[u] = ok[u] ? __ldg(w + t * topk + j) : 0.f;
+      q[u] = ok[u] ? __ldg(y + (t * topk + j) * vecs_per_row + v) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      if (!ok[u]) continue;
+      const uint32_t h[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = ElemTraits<T>::unpack2(h[i]);
+        acc[2 * i] = fmaf(wj[u], f.x, acc[2 * i]);
+        acc[2 * i + 1] = fmaf(wj[u], f.y, acc[2 * i + 1]);
+      }
     }
   }
   uint4 o;

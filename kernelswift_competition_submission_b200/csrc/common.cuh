@@ -238,4 +238,23 @@ template <> struct ElemTraits<__half> {
 
 __host__ __device__ constexpr int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+// ---------------------------------------------------------------- e4m3 block scales
+// Scale of a block whose largest magnitude is amax, so that every code lands in
+// e4m3's +-448: amax / 448 (fp32 scales), or with pow2 the smallest power of two
+// >= amax / 448 (UE8M0 scales: exactly an fp32 exponent, mantissa zero). 1 for an
+// all-zero block.
+__device__ __forceinline__ float fp8_block_scale(float amax, bool pow2) {
+  if (!(amax > 0.f)) return 1.0f;
+  const float t = amax / 448.0f;
+  if (!pow2) return t;
+  uint32_t b = __float_as_uint(t);
+  if (b & 0x7FFFFFu) b = (b & 0xFF800000u) + 0x00800000u;  // up to the next power of two
+  return __uint_as_float(b);
+}
+// The UE8M0 code of a power-of-two scale (its fp32 exponent field), repeated in
+// the four bytes of a word.
+__device__ __forceinline__ uint32_t ue8m0x4(float pow2_scale) {
+  return ((__float_as_uint(pow2_scale) >> 23) & 0xFFu) * 0x01010101u;
+}
+
 }  // namespace moe

@@ -39,6 +39,25 @@
 // (128 x 256 FMAs per 128-wide K block, on the CUDA cores, between a partial's
 // tcgen05.ld and its buffer's release) is as long as the MMAs it has to overlap,
 // and with two buffers the MMA waits for it part of the time.
+//
+// Block-scaled variant (MX = true), for weights whose every scale is a power of
+// two (UE8M0, the block-scale format of tcgen05's kind::mxf8f6f4; DeepSeek's
+// format on Blackwell), with the activations quantised the same way: the tensor
+// cores apply the scales, one MMA chain accumulates the whole K into a single
+// 256-column TMEM accumulator, and there is no promotion.
+//   warp 0      all 32 lanes write the stage's B scale-factor atoms (the UE8M0
+//               codes of the tile's weight blocks) into shared memory; lane 0
+//               loads A, B and the A scale-factor atom (512 B) by TMA.
+//   warp 1      per stage: tcgen05.cp of the A atom (TMEM columns 256-259) and
+//               the two B atoms (260-267), then 4 x tcgen05.mma.kind::mxf8f6f4.
+//               block_scale (M=128, N=256, K=32), K chunk k reading scale byte k.
+//   warps 4-11  wait for the tile's accumulator, read it (128 columns per thread),
+//               hand it back and run the same tile epilogue (act scales are
+//               powers of two, written as scale-factor atoms for GEMM2).
+// A scale-factor atom holds the 128 rows x 4 K chunks of one m-block and K block:
+// row r's code at byte (r % 32) * 16 + (r / 32) * 4 + chunk; tcgen05.cp's
+// 32x128b.warpx4 shape copies it to TMEM lanes r % 32 of every 32-lane quarter,
+// column r / 32, byte = chunk, where the MMA reads it.
 // Rows come from the align stage (pairs grouped by expert, 128-row m-blocks).
 // All mbarrier waits are bounded (common.cuh); the one named barrier of the
 // epilogue is an AND-reduction, so a warp that gave up makes all of them stop.
@@ -63,12 +82,14 @@ constexpr int kF8EpiWarps = 8;
 constexpr int kF8StageRowBytes = 64;         // epilogue staging: 32 rows x 64 B per warp
 constexpr int kF8EpiWarpBytes = 32 * kF8StageRowBytes;
 
-template <int STAGES>
+template <int STAGES, bool MX = false>
 struct F8Smem {
   static constexpr int kEpiOffset = STAGES * kF8Stage;
   static constexpr int kAmaxOffset = kEpiOffset + kF8EpiWarps * kF8EpiWarpBytes;  // [2 tiles][2 halves][128] fp32
   static constexpr int kAScaleOffset = kAmaxOffset + 2 * 2 * 128 * 4;             // [STAGES][128] fp32 row scales
-  static constexpr int kBarOffset = kAScaleOffset + STAGES * 128 * 4;
+                                                                                  // (MX: A scale-factor atoms)
+  static constexpr int kSfbOffset = kAScaleOffset + STAGES * 128 * 4;             // MX: [STAGES][2 atoms][512 B]
+  static constexpr int kBarOffset = kSfbOffset + (MX ? STAGES * 1024 : 0);
   static constexpr int kNumBars = 2 * STAGES + 5;
   static constexpr int kMiscOffset = kBarOffset + kNumBars * 8;
   static constexpr int kTableOffset = kMiscOffset + 16;
@@ -103,6 +124,45 @@ __device__ __forceinline__ void umma_f8(uint32_t d_tmem, uint64_t a_desc, uint64
 // both K-major; the N and M fields sit where they do for kind::f16.
 __host__ __device__ constexpr uint32_t idesc_e4m3(int M, int N) {
   return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// kind::mxf8f6f4.block_scale: D[tmem] (+)= (A * 2^sfa) * (B * 2^sfb)^T per 32-wide K chunk,
+// e4m3 operands, UE8M0 scale factors read from TMEM (sfa, sfb carry the byte of the
+// chunk in their top two bits, as the descriptor's scale-factor ids do).
+__device__ __forceinline__ void umma_mx(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                        uint32_t sfa, uint32_t sfb, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb)
+      : "memory");
+}
+
+// Instruction descriptor of kind::mxf8f6f4.block_scale: A and B e4m3, UE8M0 scale
+// factors, both K-major, scale-factor byte sf of the A and B scale words.
+__host__ __device__ constexpr uint32_t idesc_mx_e4m3(int M, int N, int sf) {
+  return ((uint32_t)sf << 4)               // B scale-factor id
+         | ((uint32_t)(N >> 3) << 17)      // N >> 3
+         | (1u << 23)                      // scale format: UE8M0
+         | ((uint32_t)(M >> 4) << 24)      // M >> 4
+         | ((uint32_t)sf << 29);           // A scale-factor id
+}
+
+// Copies a 32-row x 16-byte shared-memory matrix into TMEM columns [taddr, taddr + 4)
+// of lanes 0-31, replicated into each of the four 32-lane quarters.
+__device__ __forceinline__ void tmem_cp_sf(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
+// Shared-memory descriptor of a scale-factor atom for tcgen05.cp: no swizzle, rows of
+// 16 bytes, 8-row core matrices 128 B apart.
+__device__ __forceinline__ uint64_t smem_desc_sf(const void* p) {
+  const uint64_t addr = smem_u32(p);
+  uint64_t d = (addr >> 4) & 0x3FFFull;  // bits [0,14): start address >> 4
+  d |= (uint64_t)(128 >> 4) << 32;       // bits [32,46): stride byte offset = 128 B
+  d |= 1ull << 46;                       // bits [46,48): descriptor version 1 (sm_100); layout 0: no swizzle
+  return d;
 }
 
 // Byte offset of 16-byte chunk c (0..3) of staged row r (32 rows x 64 B): the
@@ -155,14 +215,14 @@ template <int R> __device__ __forceinline__ void setmaxnreg_inc() {
   asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(R));
 }
 
-template <int MODE, int STAGES>
+template <int MODE, int STAGES, bool MX>
 __global__ void __launch_bounds__(kF8Threads, 1)
 moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                     const __grid_constant__ CUtensorMap map_sa, const float* __restrict__ b_scale,
                     const int32_t* __restrict__ block_start, int E, int k_red, int n_out, int NB,
                     void* __restrict__ out, float* __restrict__ out_scale, int64_t out_scale_stride,
                     const int32_t* __restrict__ sorted_pairs, int* status) {
-  using L = F8Smem<STAGES>;
+  using L = F8Smem<STAGES, MX>;
   constexpr int kBatch = 1;  // K blocks whose row scales the epilogue reads at once (measured: 1 is fastest)
   constexpr uint32_t kTmemCols = 2 * kF8BN;
   constexpr uint32_t kIdesc = idesc_e4m3(kBlockM, kF8BN);
@@ -171,8 +231,8 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
   uint64_t* empty = full + STAGES;
-  uint64_t* pfull = full + 2 * STAGES;  // partial accumulator b holds a finished K block
-  uint64_t* pempty = pfull + 2;         // partial accumulator b has been promoted
+  uint64_t* pfull = full + 2 * STAGES;  // partial accumulator b holds a finished K block (MX: [0] tile done)
+  uint64_t* pempty = pfull + 2;         // partial accumulator b has been promoted (MX: [0] tile read out)
   uint64_t* mma_done = pfull + 4;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + L::kMiscOffset);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + L::kMiscOffset + 4);
@@ -183,8 +243,9 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
 
   for (int i = threadIdx.x; i <= E; i += kF8Threads) s_bs[i] = __ldg(block_start + i);
   if (threadIdx.x == 0) {
-    // a stage is free once its MMAs finished (commit) and every epilogue warp read its row scales
-    for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1 + kF8EpiWarps); }
+    // a stage is free once its MMAs finished (commit) and every epilogue warp read its row
+    // scales (MX: once its MMAs and scale-factor copies finished)
+    for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], MX ? 1 : 1 + kF8EpiWarps); }
     for (int b = 0; b < 2; ++b) { mbar_init(&pfull[b], 1); mbar_init(&pempty[b], kF8EpiWarps); }
     mbar_init(mma_done, 1);
     *s_abort = 0;
@@ -202,7 +263,81 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
   // refuses to launch unless the kernel was compiled to exactly 168 registers per thread).
   if (warp < 4) {
     setmaxnreg_dec<kF8RegsLow>();
-  if (warp == 0) {
+  if (warp == 0 && MX) {
+    // ------------------------------------------------ TMA producer + B scale-factor atoms (MX)
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t issued_mask = 0, issued_parity = 0;
+    bool ok = true;
+    const int kb128 = (k_red + 127) / 128;
+    for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+      int e, nb, mb;
+      decode_tile_f8(s_bs, E, NB, tile, e, nb, mb);
+      // the weight blocks of the tile's B rows: GEMM1 rows [gate | up | gate | up] x 64 come
+      // from one gate and one up block; GEMM2's 256 rows from two consecutive row blocks
+      const float* sw_lo;
+      const float* sw_hi;
+      if constexpr (MODE == F8_GEMM1) {
+        const int nrb = 2 * (n_out / 128);
+        sw_lo = b_scale + ((int64_t)e * nrb + nb) * kb128;
+        sw_hi = b_scale + ((int64_t)e * nrb + n_out / 128 + nb) * kb128;
+      } else {
+        const int nblk = (n_out + 127) / 128;
+        sw_lo = b_scale + ((int64_t)e * nblk + 2 * nb) * kb128;
+        sw_hi = b_scale + ((int64_t)e * nblk + min(2 * nb + 1, nblk - 1)) * kb128;
+      }
+      const float wl_r0 = lane < kb128 ? __ldg(sw_lo + lane) : 1.f;
+      const float wl_r1 = lane + 32 < kb128 ? __ldg(sw_lo + lane + 32) : 1.f;
+      const float wh_r0 = lane < kb128 ? __ldg(sw_hi + lane) : 1.f;
+      const float wh_r1 = lane + 32 < kb128 ? __ldg(sw_hi + lane + 32) : 1.f;
+      for (int kb = 0; kb < num_kb; ++kb) {
+        const bool got = mbar_wait(&empty[stage], phase ^ 1, status, s_abort);
+        if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+        float wl, wh;
+        if (kb < 64) {
+          wl = __shfl_sync(0xffffffffu, kb < 32 ? wl_r0 : wl_r1, kb & 31);
+          wh = __shfl_sync(0xffffffffu, kb < 32 ? wh_r0 : wh_r1, kb & 31);
+        } else {
+          wl = __ldg(sw_lo + kb);
+          wh = __ldg(sw_hi + kb);
+        }
+        const uint32_t cl = ue8m0x4(wl), ch = ue8m0x4(wh);
+        // atom words: column r / 32 of 16-byte row r % 32; GEMM1 rows 0-63 gate, 64-127 up
+        uint4* sfb = reinterpret_cast<uint4*>(smem + L::kSfbOffset + stage * 1024);
+        if constexpr (MODE == F8_GEMM1) {
+          sfb[lane] = make_uint4(cl, cl, ch, ch);
+          sfb[32 + lane] = make_uint4(cl, cl, ch, ch);
+        } else {
+          sfb[lane] = make_uint4(cl, cl, cl, cl);
+          sfb[32 + lane] = make_uint4(ch, ch, ch, ch);
+        }
+        fence_proxy_async_smem();  // generic writes -> the async proxy of tcgen05.cp
+        __syncwarp();
+        if (lane == 0) {
+          uint8_t* a_dst = smem + stage * kF8Stage;
+          uint8_t* b_dst = a_dst + kF8ATile;
+          mbar_arrive_expect_tx(&full[stage], kF8Stage + kBlockM * 4);
+          tma_load_2d(&map_a, &full[stage], a_dst, kb * kF8BK, mb * kBlockM);
+          tma_load_2d(&map_sa, &full[stage], smem + L::kAScaleOffset + stage * kBlockM * 4, mb * kBlockM, kb);
+          if constexpr (MODE == F8_GEMM1) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              tma_load_3d(&map_b, &full[stage], b_dst + q * 64 * kF8BK, kb * kF8BK, nb * 128 + (q >> 1) * 64,
+                          2 * e + (q & 1));
+          } else {
+            tma_load_3d(&map_b, &full[stage], b_dst, kb * kF8BK, nb * kF8BN, e);
+          }
+        }
+        issued_mask |= 1u << stage;
+        issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+      }
+    }
+    if (!ok && lane == 0) {  // let the copies in flight land before the CTA exits
+      for (int s = 0; s < STAGES; ++s)
+        if ((issued_mask >> s) & 1u) mbar_wait(&full[s], (issued_parity >> s) & 1u, nullptr, nullptr);
+    }
+  } else if (warp == 0) {
     if (lane == 0) {
       // ------------------------------------------------ TMA producer
       int stage = 0;
@@ -237,6 +372,41 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
         for (int s = 0; s < STAGES; ++s)
           if ((issued_mask >> s) & 1u) mbar_wait(&full[s], (issued_parity >> s) & 1u, nullptr, nullptr);
       }
+    }
+  } else if (warp == 1 && MX) {
+    if (lane == 0) {
+      // ------------------------------------------------ MMA issuer (MX): whole K into one accumulator
+      int stage = 0;
+      uint32_t phase = 0, aphase = 0;
+      bool ok = true;
+      const uint32_t sfa_t = tmem_base + (uint32_t)kF8BN, sfb_t = sfa_t + 4;
+      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+        if (!mbar_wait(&pempty[0], aphase ^ 1, status, s_abort)) break;  // previous tile read out
+        tc_fence_after();
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, status, s_abort)) { ok = false; break; }
+          tc_fence_after();
+          const uint8_t* a_src = smem + stage * kF8Stage;
+          const uint64_t a_desc = smem_desc_sw128(a_src);
+          const uint64_t b_desc = smem_desc_sw128(a_src + kF8ATile);
+          const uint8_t* sfb = smem + L::kSfbOffset + stage * 1024;
+          // issued by this thread ahead of the MMAs, which then read them in order
+          tmem_cp_sf(sfa_t, smem_desc_sf(smem + L::kAScaleOffset + stage * kBlockM * 4));
+          tmem_cp_sf(sfb_t, smem_desc_sf(sfb));
+          tmem_cp_sf(sfb_t + 4, smem_desc_sf(sfb + 512));
+#pragma unroll
+          for (int k = 0; k < kF8BK / 32; ++k)
+            umma_mx(tmem_base, a_desc + 2 * k, b_desc + 2 * k, idesc_mx_e4m3(kBlockM, kF8BN, k),
+                    sfa_t + ((uint32_t)k << 30), sfb_t + ((uint32_t)k << 30), (kb | k) != 0);
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        umma_commit(&pfull[0]);
+        aphase ^= 1;
+      }
+      umma_commit(mma_done);
+      mbar_wait(mma_done, 0, nullptr, nullptr);
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -285,18 +455,56 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
       int e, nb, mb;
       decode_tile_f8(s_bs, E, NB, tile, e, nb, mb);
       const int64_t grow = (int64_t)mb * kBlockM + row;
+      // totals as fp32 pairs: column 2j in .x, 2j + 1 in .y (packed FMA, two columns per instruction)
+      float2 tot[64];
+      bool cols_live = true;
+      if constexpr (MODE == F8_GEMM2) cols_live = (2 * nb + h) * 128 < n_out;
+      if constexpr (MX) {
+        // the MMAs applied the scales: read the finished accumulator and hand it back
+        bool got = mbar_wait(&pfull[0], pphase, status, s_abort);
+        got = __all_sync(0xffffffffu, got);
+        if (got) {
+          tc_fence_after();
+          const uint32_t t_addr = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(h * 128);
+          uint32_t va[32], vb[32];
+          tmem_ld32(t_addr, va);
+          tmem_ld32(t_addr + 32, vb);
+          tmem_wait_ld_regs(va);
+          reg_order32(vb);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            tot[i] = make_float2(__uint_as_float(va[2 * i]), __uint_as_float(va[2 * i + 1]));
+            tot[16 + i] = make_float2(__uint_as_float(vb[2 * i]), __uint_as_float(vb[2 * i + 1]));
+          }
+          tmem_ld32(t_addr + 64, va);
+          tmem_ld32(t_addr + 96, vb);
+          tmem_wait_ld_regs(va);
+          reg_order32(vb);
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&pempty[0]);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            tot[32 + i] = make_float2(__uint_as_float(va[2 * i]), __uint_as_float(va[2 * i + 1]));
+            tot[48 + i] = make_float2(__uint_as_float(vb[2 * i]), __uint_as_float(vb[2 * i + 1]));
+          }
+          pphase ^= 1;
+        } else {
+          ok = false;
+#pragma unroll
+          for (int j = 0; j < 64; ++j) tot[j] = make_float2(0.f, 0.f);
+        }
+      } else {
       // weight scales of the tile's K blocks: lane i holds blocks i and i + 32 (a shuffle
       // broadcasts block kb); blocks from 64 on are read per block
       const float* sw_lo;
       const float* sw_hi;
-      bool cols_live = true;
       if constexpr (MODE == F8_GEMM1) {
         const int nrb = 2 * (n_out / 128);  // w1 row blocks per expert: gate blocks, then up blocks
         sw_lo = b_scale + ((int64_t)e * nrb + nb) * kb128;
         sw_hi = b_scale + ((int64_t)e * nrb + n_out / 128 + nb) * kb128;
       } else {
         const int cblk = 2 * nb + h;
-        cols_live = cblk * 128 < n_out;
         sw_lo = b_scale + ((int64_t)e * ((n_out + 127) / 128) + (cols_live ? cblk : 0)) * kb128;
         sw_hi = sw_lo;
       }
@@ -304,8 +512,6 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
       const float wl_r1 = lane + 32 < kb128 ? __ldg(sw_lo + lane + 32) : 0.f;
       const float wh_r0 = lane < kb128 ? __ldg(sw_hi + lane) : 0.f;
       const float wh_r1 = lane + 32 < kb128 ? __ldg(sw_hi + lane + 32) : 0.f;
-      // totals as fp32 pairs: column 2j in .x, 2j + 1 in .y (packed FMA, two columns per instruction)
-      float2 tot[64];
 #pragma unroll
       for (int j = 0; j < 64; ++j) tot[j] = make_float2(0.f, 0.f);
       float sa_q[kBatch];
@@ -365,6 +571,7 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
         promote32(tot, 48, vb, f_hi);
         if (++pb == 2) { pb = 0; pphase ^= 1; }
       }
+      }  // promotion
       if constexpr (MODE == F8_GEMM1) {
         // act for the 64 channels nb * 128 + 64 h + j, quantised per row per 128 channels
         // gate channel pairs in tot[0..31], the matching up pairs in tot[32..63]
@@ -379,8 +586,14 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
         ok = named_bar_and(1, 32 * kF8EpiWarps, ok);
         if (!ok) break;
         amax = fmaxf(amax, s_amax[(tpar * 2 + (h ^ 1)) * 128 + row]);
-        const float sc = amax > 0.f ? amax / 448.0f : 1.0f;
-        if (h == 0) out_scale[(int64_t)nb * out_scale_stride + grow] = sc;  // [channel blocks][rows]
+        const float sc = fp8_block_scale(amax, MX);
+        if (h == 0) {  // [channel blocks][rows]; MX: the rows of an m-block as a scale-factor atom
+          if constexpr (MX)
+            reinterpret_cast<uint32_t*>(out_scale)[(int64_t)nb * out_scale_stride + (int64_t)mb * kBlockM + lane * 4 +
+                                                   quad] = ue8m0x4(sc);
+          else
+            out_scale[(int64_t)nb * out_scale_stride + grow] = sc;
+        }
         uint32_t q[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
@@ -469,16 +682,23 @@ gather_rows_kernel(const uint8_t* __restrict__ src, int64_t src_stride, int64_t 
 
 // Transposed gather of per-row scales: dst[kb * cap + r] = src[(sorted_pairs[r] / topk) * src_stride + kb]
 // for the rows the align stage filled (0 for padding rows), so the 128 scales of one m-block
-// and K block are 512 contiguous bytes (one TMA box).
+// and K block are 512 contiguous bytes (one TMA box). ue8m0: those 512 bytes are the m-block's
+// scale-factor atom instead (row r's UE8M0 code, four times, in word (r % 32) * 4 + r / 32).
 __global__ void __launch_bounds__(256)
 gather_scales_t_kernel(const float* __restrict__ src, int64_t src_stride, int KB,
                        const int32_t* __restrict__ sorted_pairs, const int32_t* __restrict__ block_start, int E,
-                       int topk, int64_t cap, float* __restrict__ dst) {
+                       int topk, int64_t cap, bool ue8m0, float* __restrict__ dst) {
   const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= cap || r >= (int64_t)__ldg(block_start + E) * kBlockM) return;
   const int pair = __ldg(sorted_pairs + r);
   const float* s = pair >= 0 ? src + (int64_t)(pair / topk) * src_stride : nullptr;
-  for (int kb = 0; kb < KB; ++kb) dst[(int64_t)kb * cap + r] = s ? __ldg(s + kb) : 0.f;
+  if (ue8m0) {
+    const int64_t w = (r & ~int64_t(127)) + (r & 31) * 4 + ((r >> 5) & 3);
+    uint32_t* d = reinterpret_cast<uint32_t*>(dst);
+    for (int kb = 0; kb < KB; ++kb) d[(int64_t)kb * cap + w] = s ? ue8m0x4(__ldg(s + kb)) : 0u;
+  } else {
+    for (int kb = 0; kb < KB; ++kb) dst[(int64_t)kb * cap + r] = s ? __ldg(s + kb) : 0.f;
+  }
 }
 
 // [K blocks][rows_cap] fp32 scale table; box = 128 rows of one K block.
@@ -488,13 +708,13 @@ bool make_scale_map(CUtensorMap* m, const float* base, int64_t rows_cap, int kbl
   return make_f32_rows_map(m, base, dims, str, kBlockM);
 }
 
-template <int MODE, int STAGES>
+template <int MODE, int STAGES, bool MX>
 cudaError_t launch_f8_stages(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& msa,
                              const float* b_scale, const int32_t* block_start, int E, int k_red, int n_out, int NB,
                              int64_t rows_cap, void* out, float* out_scale, const int32_t* sorted_pairs, int* status,
                              int max_ctas, cudaStream_t st) {
-  auto kern = moe_gemm_fp8_kernel<MODE, STAGES>;
-  const int smem = F8Smem<STAGES>::bytes(E);
+  auto kern = moe_gemm_fp8_kernel<MODE, STAGES, MX>;
+  const int smem = F8Smem<STAGES, MX>::bytes(E);
   cudaFuncAttributes fa;
   cudaError_t err = cudaFuncGetAttributes(&fa, kern);
   if (err != cudaSuccess) return err;
@@ -511,18 +731,30 @@ cudaError_t launch_f8_stages(const CUtensorMap& ma, const CUtensorMap& mb, const
   return cudaGetLastError();
 }
 
+template <int MODE, bool MX>
+cudaError_t launch_f8_mx(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& msa, const float* b_scale,
+                         const int32_t* block_start, int E, int k_red, int n_out, int NB, int64_t rows_cap, void* out,
+                         float* out_scale, const int32_t* sorted_pairs, int* status, int max_ctas, cudaStream_t st) {
+  constexpr int kMaxSmem = 227 * 1024;
+  if (F8Smem<4, MX>::bytes(E) <= kMaxSmem)
+    return launch_f8_stages<MODE, 4, MX>(ma, mb, msa, b_scale, block_start, E, k_red, n_out, NB, rows_cap, out,
+                                         out_scale, sorted_pairs, status, max_ctas, st);
+  if (F8Smem<3, MX>::bytes(E) <= kMaxSmem)
+    return launch_f8_stages<MODE, 3, MX>(ma, mb, msa, b_scale, block_start, E, k_red, n_out, NB, rows_cap, out,
+                                         out_scale, sorted_pairs, status, max_ctas, st);
+  return cudaErrorInvalidValue;
+}
+
 template <int MODE>
 cudaError_t launch_f8(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& msa, const float* b_scale,
                       const int32_t* block_start, int E, int k_red, int n_out, int NB, int64_t rows_cap, void* out,
-                      float* out_scale, const int32_t* sorted_pairs, int* status, int max_ctas, cudaStream_t st) {
-  constexpr int kMaxSmem = 227 * 1024;
-  if (F8Smem<4>::bytes(E) <= kMaxSmem)
-    return launch_f8_stages<MODE, 4>(ma, mb, msa, b_scale, block_start, E, k_red, n_out, NB, rows_cap, out,
-                                     out_scale, sorted_pairs, status, max_ctas, st);
-  if (F8Smem<3>::bytes(E) <= kMaxSmem)
-    return launch_f8_stages<MODE, 3>(ma, mb, msa, b_scale, block_start, E, k_red, n_out, NB, rows_cap, out,
-                                     out_scale, sorted_pairs, status, max_ctas, st);
-  return cudaErrorInvalidValue;
+                      float* out_scale, const int32_t* sorted_pairs, bool ue8m0, int* status, int max_ctas,
+                      cudaStream_t st) {
+  if (ue8m0)
+    return launch_f8_mx<MODE, true>(ma, mb, msa, b_scale, block_start, E, k_red, n_out, NB, rows_cap, out, out_scale,
+                                    sorted_pairs, status, max_ctas, st);
+  return launch_f8_mx<MODE, false>(ma, mb, msa, b_scale, block_start, E, k_red, n_out, NB, rows_cap, out, out_scale,
+                                   sorted_pairs, status, max_ctas, st);
 }
 
 }  // namespace
@@ -537,17 +769,18 @@ cudaError_t launch_gather_rows(const void* src, int64_t src_stride, int64_t row_
 }
 
 cudaError_t launch_gather_scales_t(const float* src, int64_t src_stride, int KB, const int32_t* sorted_pairs,
-                                   const int32_t* block_start, int E, int topk, int64_t cap, float* dst,
+                                   const int32_t* block_start, int E, int topk, int64_t cap, bool ue8m0, float* dst,
                                    cudaStream_t st) {
   if (cap == 0) return cudaSuccess;
+  if (ue8m0 && cap % kBlockM != 0) return cudaErrorInvalidValue;  // atoms cover whole m-blocks
   gather_scales_t_kernel<<<(unsigned)ceil_div(cap, 256), 256, 0, st>>>(src, src_stride, KB, sorted_pairs, block_start,
-                                                                       E, topk, cap, dst);
+                                                                       E, topk, cap, ue8m0, dst);
   return cudaGetLastError();
 }
 
 cudaError_t launch_fp8_gemm1(const void* xq_sorted, const float* xs_sorted_t, int64_t rows_cap, const void* w1q,
                              const float* w1s, int E, int K, int N, const int32_t* block_start, void* actq,
-                             float* acts_t, int* status, int max_ctas, cudaStream_t st) {
+                             float* acts_t, bool ue8m0, int* status, int max_ctas, cudaStream_t st) {
   CUtensorMap ma, mbm, msa;
   const uint64_t a_dims[2] = {(uint64_t)K, (uint64_t)rows_cap};
   const uint64_t a_str[1] = {(uint64_t)K};
@@ -557,12 +790,13 @@ cudaError_t launch_fp8_gemm1(const void* xq_sorted, const float* xs_sorted_t, in
   if (!make_fp8_map(&mbm, w1q, 3, b_dims, b_str, 64)) return cudaErrorInvalidValue;
   if (!make_scale_map(&msa, xs_sorted_t, rows_cap, K / 128)) return cudaErrorInvalidValue;
   return launch_f8<F8_GEMM1>(ma, mbm, msa, w1s, block_start, E, K, N, N / 128, rows_cap, actq, acts_t, nullptr,
-                             status, max_ctas, st);
+                             ue8m0, status, max_ctas, st);
 }
 
 cudaError_t launch_fp8_gemm2(const void* actq, const float* acts_t, int64_t rows_cap, const void* w2q,
                              const float* w2s, int E, int K, int N, const int32_t* block_start,
-                             const int32_t* sorted_pairs, void* y_slots, int* status, int max_ctas, cudaStream_t st) {
+                             const int32_t* sorted_pairs, void* y_slots, bool ue8m0, int* status, int max_ctas,
+                             cudaStream_t st) {
   CUtensorMap ma, mbm, msa;
   const uint64_t a_dims[2] = {(uint64_t)N, (uint64_t)rows_cap};
   const uint64_t a_str[1] = {(uint64_t)N};
@@ -572,7 +806,7 @@ cudaError_t launch_fp8_gemm2(const void* actq, const float* acts_t, int64_t rows
   if (!make_fp8_map(&mbm, w2q, 3, b_dims, b_str, kF8BN)) return cudaErrorInvalidValue;
   if (!make_scale_map(&msa, acts_t, rows_cap, N / 128)) return cudaErrorInvalidValue;
   return launch_f8<F8_GEMM2>(ma, mbm, msa, w2s, block_start, E, N, K, (int)ceil_div(K, kF8BN), rows_cap, y_slots,
-                             nullptr, sorted_pairs, status, max_ctas, st);
+                             nullptr, sorted_pairs, ue8m0, status, max_ctas, st);
 }
 
 }  // namespace moe

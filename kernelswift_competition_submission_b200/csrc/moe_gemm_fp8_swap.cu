@@ -104,7 +104,7 @@ moe_gemm_fp8_swap_kernel(const __grid_constant__ CUtensorMap map_a, const __grid
                          const __grid_constant__ CUtensorMap map_s, const float* __restrict__ w_scale,
                          const int32_t* __restrict__ counts, const int32_t* __restrict__ block_start, int E,
                          int k_red, int n_w, int NB, void* __restrict__ out, float* __restrict__ out_scale,
-                         int64_t rows_cap, const int32_t* __restrict__ sorted_pairs, int* status) {
+                         int64_t rows_cap, const int32_t* __restrict__ sorted_pairs, bool pow2_act, int* status) {
   using C = SwCfg<MODE>;
   constexpr int S = C::kStages;
   constexpr uint32_t kIdesc = idesc_e4m3_sw(kSwRows, kSwTok);
@@ -323,7 +323,7 @@ moe_gemm_fp8_swap_kernel(const __grid_constant__ CUtensorMap map_a, const __grid
 #pragma unroll
         for (int j = 0; j < kSwTok; ++j) {
           const float a = fmaxf(fmaxf(s_amax[j], s_amax[kSwTok + j]), fmaxf(s_amax[2 * kSwTok + j], s_amax[3 * kSwTok + j]));
-          sc[j] = a > 0.f ? a / 448.0f : 1.0f;
+          sc[j] = fp8_block_scale(a, pow2_act);
         }
         // codes staged as [token][channel] bytes
 #pragma unroll
@@ -334,7 +334,7 @@ moe_gemm_fp8_swap_kernel(const __grid_constant__ CUtensorMap map_a, const __grid
         if (ew == 0 && lane < nvalid) {  // token `lane`'s scale, read from the amax table (no dynamic index)
           const float a = fmaxf(fmaxf(s_amax[lane], s_amax[kSwTok + lane]),
                                 fmaxf(s_amax[2 * kSwTok + lane], s_amax[3 * kSwTok + lane]));
-          out_scale[(int64_t)rb * rows_cap + row0 + lane] = a > 0.f ? a / 448.0f : 1.0f;
+          out_scale[(int64_t)rb * rows_cap + row0 + lane] = fp8_block_scale(a, pow2_act);
         }
         named_bar_sync(1, 128);
         // 32 token rows x 128 bytes -> act rows (row0 + j, channels rb * 128 ..)
@@ -385,7 +385,7 @@ template <int MODE>
 cudaError_t launch_sw(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& ms, const float* w_scale,
                       const int32_t* counts, const int32_t* block_start, int E, int k_red, int n_w, int NB,
                       int64_t rows_cap, int64_t num_pairs, void* out, float* out_scale, const int32_t* sorted_pairs,
-                      int* status, int max_ctas, cudaStream_t st) {
+                      bool pow2_act, int* status, int max_ctas, cudaStream_t st) {
   using C = SwCfg<MODE>;
   auto kern = moe_gemm_fp8_swap_kernel<MODE>;
   const int smem = C::bytes(E);
@@ -396,7 +396,7 @@ cudaError_t launch_sw(const CUtensorMap& ma, const CUtensorMap& mb, const CUtens
   const int ctas = (max_ctas > 0 && max_ctas < num_sms()) ? max_ctas : num_sms();
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(ctas, tiles_cap));
   kern<<<grid, kSwThreads, smem, st>>>(ma, mb, ms, w_scale, counts, block_start, E, k_red, n_w, NB, out, out_scale,
-                                       rows_cap, sorted_pairs, status);
+                                       rows_cap, sorted_pairs, pow2_act, status);
   return cudaGetLastError();
 }
 
@@ -414,7 +414,7 @@ bool fp8_use_swap(int64_t num_pairs, int E) { return num_pairs <= kFp8SwapMaxRow
 cudaError_t launch_fp8_swap_gemm1(const void* xq_sorted, const float* xs_sorted_t, int64_t rows_cap,
                                   int64_t num_pairs, const void* w1q, const float* w1s, int E, int K, int N,
                                   const int32_t* counts, const int32_t* block_start, void* actq, float* acts_t,
-                                  int* status, int max_ctas, cudaStream_t st) {
+                                  bool pow2_act, int* status, int max_ctas, cudaStream_t st) {
   CUtensorMap ma, mbm, ms;
   const uint64_t a_dims[3] = {(uint64_t)K, (uint64_t)N, (uint64_t)2 * E};
   const uint64_t a_str[2] = {(uint64_t)K, (uint64_t)N * K};
@@ -424,7 +424,7 @@ cudaError_t launch_fp8_swap_gemm1(const void* xq_sorted, const float* xs_sorted_
   if (!make_fp8_map(&mbm, xq_sorted, 2, b_dims, b_str, kSwTok)) return cudaErrorInvalidValue;
   if (!make_scale_map32(&ms, xs_sorted_t, rows_cap, K / 128)) return cudaErrorInvalidValue;
   return launch_sw<SW_GEMM1>(ma, mbm, ms, w1s, counts, block_start, E, K, N, N / 128, rows_cap, num_pairs, actq,
-                             acts_t, nullptr, status, max_ctas, st);
+                             acts_t, nullptr, pow2_act, status, max_ctas, st);
 }
 
 cudaError_t launch_fp8_swap_gemm2(const void* actq, const float* acts_t, int64_t rows_cap, int64_t num_pairs,
@@ -440,7 +440,7 @@ cudaError_t launch_fp8_swap_gemm2(const void* actq, const float* acts_t, int64_t
   if (!make_fp8_map(&mbm, actq, 2, b_dims, b_str, kSwTok)) return cudaErrorInvalidValue;
   if (!make_scale_map32(&ms, acts_t, rows_cap, N / 128)) return cudaErrorInvalidValue;
   return launch_sw<SW_GEMM2>(ma, mbm, ms, w2s, counts, block_start, E, N, K, K / 128, rows_cap, num_pairs, y_slots,
-                             nullptr, sorted_pairs, status, max_ctas, st);
+                             nullptr, sorted_pairs, false, status, max_ctas, st);
 }
 
 }  // namespace moe

@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "../../include/moe_b200.h"
+
 namespace moe {
 
 constexpr int kBlockM = 128;  // rows per m-block of the grouped GEMMs (one TMEM lane per row)
@@ -99,16 +101,24 @@ bool make_fp8_map(CUtensorMap* m, const void* base, int rank, const uint64_t* di
 bool make_f32_rows_map(CUtensorMap* m, const float* base, const uint64_t* dims, const uint64_t* strides_bytes,
                        uint32_t box_rows);
 // max_ctas: persistent grid size limit (0 = one CTA per SM).
+// With ue8m0 (every scale a power of two) the GEMMs run kind::mxf8f6f4.block_scale
+// instead: row scales are then UE8M0 atom tables (launch_gather_scales_t with ue8m0),
+// the weight scales' exponents become the B scale factors, and GEMM1 writes act's
+// scales as such a table too.
 cudaError_t launch_fp8_gemm1(const void* xq_sorted, const float* xs_sorted_t, int64_t rows_cap, const void* w1q,
                              const float* w1s, int E, int K, int N, const int32_t* block_start, void* actq,
-                             float* acts_t, int* status, int max_ctas, cudaStream_t st);
+                             float* acts_t, bool ue8m0, int* status, int max_ctas, cudaStream_t st);
 cudaError_t launch_fp8_gemm2(const void* actq, const float* acts_t, int64_t rows_cap, const void* w2q,
                              const float* w2s, int E, int K, int N, const int32_t* block_start,
-                             const int32_t* sorted_pairs, void* y_slots, int* status, int max_ctas, cudaStream_t st);
+                             const int32_t* sorted_pairs, void* y_slots, bool ue8m0, int* status, int max_ctas,
+                             cudaStream_t st);
 // dst[kb * cap + r] = src[(sorted_pairs[r] / topk) * src_stride + kb] for the rows the align
-// stage filled (src_stride in floats between token rows).
+// stage filled (src_stride in floats between token rows). With ue8m0 the 128 entries of an
+// m-block and K block form the scale-factor atom of tcgen05's block-scaled MMA instead: the
+// word of row r at (r / 128) * 128 + (r % 32) * 4 + (r % 128) / 32, holding the scale's UE8M0
+// code in all four bytes (one per 32-wide K chunk); 0 for padding rows.
 cudaError_t launch_gather_scales_t(const float* src, int64_t src_stride, int KB, const int32_t* sorted_pairs,
-                                   const int32_t* block_start, int E, int topk, int64_t cap, float* dst,
+                                   const int32_t* block_start, int E, int topk, int64_t cap, bool ue8m0, float* dst,
                                    cudaStream_t st);
 // dst[r] = row_bytes bytes of src at token row sorted_pairs[r] / topk (src_stride bytes apart),
 // for the rows the align stage filled; dst rows are row_bytes apart.
@@ -121,10 +131,11 @@ cudaError_t launch_gather_rows(const void* src, int64_t src_stride, int64_t row_
 // when the experts average no more than kFp8SwapMaxRowsPerExpert rows (fp8_use_swap).
 constexpr int64_t kFp8SwapMaxRowsPerExpert = 16;
 bool fp8_use_swap(int64_t num_pairs, int E);
+// pow2_act: act's scales rounded up to powers of two (the UE8M0 recipe).
 cudaError_t launch_fp8_swap_gemm1(const void* xq_sorted, const float* xs_sorted_t, int64_t rows_cap,
                                   int64_t num_pairs, const void* w1q, const float* w1s, int E, int K, int N,
                                   const int32_t* counts, const int32_t* block_start, void* actq, float* acts_t,
-                                  int* status, int max_ctas, cudaStream_t st);
+                                  bool pow2_act, int* status, int max_ctas, cudaStream_t st);
 cudaError_t launch_fp8_swap_gemm2(const void* actq, const float* acts_t, int64_t rows_cap, int64_t num_pairs,
                                   const void* w2q, const float* w2s, int E, int K, int N, const int32_t* counts,
                                   const int32_t* block_start, const int32_t* sorted_pairs, void* y_slots, int* status,
@@ -133,7 +144,8 @@ cudaError_t launch_fp8_swap_gemm2(const void* actq, const float* acts_t, int64_t
 // Per row, per 128 columns e4m3 quantisation (dtype bf16 / fp16 / fp32 input): row m's codes
 // at q + m * ldq (bytes), its K / 128 scales at s + m * lds (floats).
 cudaError_t launch_quantize_rows(int dtype, const void* x, int64_t M, int K, uint8_t* q, int64_t ldq, float* s,
-                                 int64_t lds, cudaStream_t st);
+                                 int64_t lds, bool pow2, cudaStream_t st);
+inline bool scale_fmt_ok(int f) { return f == MOE_FP8_SCALE_FP32 || f == MOE_FP8_SCALE_UE8M0; }
 
 // Packed e4m3 token row (MOE_DTYPE_E4M3_ROW): K codes, then K / 128 fp32 scales, padded to
 // a multiple of 16 bytes.

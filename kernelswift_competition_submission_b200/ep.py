@@ -112,8 +112,9 @@ class ExpertParallelMoE:
             raise ValueError("w1_local / w2_local must hold num_experts / world experts")
         self.fp8 = bool(use_fp8_w8a8)
         self.w1s = self.w2s = None
+        self.scale_format = None
         if self.fp8:
-            from .ops import _fp8_bytes
+            from .ops import _fp8_bytes, weights_scale_format
 
             if w1_scale is None or w2_scale is None:
                 raise ValueError("use_fp8_w8a8 needs w1_scale and w2_scale")
@@ -126,6 +127,8 @@ class ExpertParallelMoE:
             w1_local, w2_local = _fp8_bytes(w1_local.contiguous()), _fp8_bytes(w2_local.contiguous())
             self.w1s = w1_scale.to(torch.float32).contiguous()
             self.w2s = w2_scale.to(torch.float32).contiguous()
+            # power-of-two weight scales: the token rows are quantised with power-of-two scales too
+            self.scale_format = weights_scale_format(self.w1s, self.w2s)
         self.w1, self.w2 = w1_local, w2_local
         self.hidden = w2_local.shape[1]
         self.quant_fn = quant_fn or self._quant_cuda
@@ -257,7 +260,7 @@ class ExpertParallelMoE:
     def _quant_cuda(self, x):
         from .ops import quantize_rows_fp8_packed
 
-        return quantize_rows_fp8_packed(x)
+        return quantize_rows_fp8_packed(x, scale_format=self.scale_format)
 
     def _experts_cuda(self, x, w, ids, events=None, out=None, max_ctas=0):
         from .ops import fused_moe_staged, fused_moe_workspace_bytes
@@ -280,7 +283,7 @@ class ExpertParallelMoE:
             if events:  # one library call: the stage events bracket it (no per-GEMM split)
                 events[0].record()
             y = fused_moe_fp8_rows(x, self.hidden, self.w1, self.w1s, self.w2, self.w2s, w, ids, out=out,
-                                   workspace=self._ws, max_ctas=max_ctas)
+                                   workspace=self._ws, max_ctas=max_ctas, scale_format=self.scale_format)
             if events:
                 for e in events[1:]:
                     e.record()
@@ -700,8 +703,10 @@ class ExpertParallelMoE:
         if self.fp8:  # GEMMs straight from the received packed rows; the slot rows stay in ws
             _lib.check(lib.moe_fused_experts_fp8_rows(ctypes.c_void_p(rx), int(lib.moe_fp8_row_bytes(K)),
                                                       _ptr(self.w1), _ptr(self.w1s), _ptr(self.w2), _ptr(self.w2s),
-                                                      None, ctypes.c_void_p(rid), R, E_l, k, K, N, None, ws, wsn, 0,
-                                                      status, st), "moe_fused_experts_fp8_rows")
+                                                      None, ctypes.c_void_p(rid), R, E_l, k, K, N,
+                                                      _lib.MOE_FP8_SCALE_UE8M0 if self.scale_format == "ue8m0"
+                                                      else _lib.MOE_FP8_SCALE_FP32, None, ws, wsn, 0, status, st),
+                                   "moe_fused_experts_fp8_rows")
             self._mark("experts")
             # top-k combine of each valid received row, stored straight into its source's arena
             _lib.check(lib.moe_p2p_combine_experts_back(dt_rows, ws, E_l, K, N, k, W, self.rank, cap, pb, base, seq,

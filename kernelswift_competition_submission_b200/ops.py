@@ -219,6 +219,7 @@ def fused_moe(
     block_shape=(128, 128),
     out: torch.Tensor | None = None,
     workspace: torch.Tensor | None = None,
+    scale_format: str | None = None,
 ) -> torch.Tensor:
     """Expert path of the MoE layer for given routing.
 
@@ -228,7 +229,8 @@ def fused_moe(
 
     With ``use_fp8_w8a8`` the weights are e4m3 with fp32 ``w1_scale`` /
     ``w2_scale`` per 128 x 128 block (``quantize_weights_fp8``) and the token rows
-    are quantised per token per 128 on the fly (``fused_moe_fp8``).
+    are quantised per token per 128 on the fly (``fused_moe_fp8``; power-of-two
+    scales on both sides select the block-scaled tensor-core GEMMs).
     """
     if activation != "silu":
         raise ValueError(f"Unsupported activation: {activation}")
@@ -238,7 +240,7 @@ def fused_moe(
         if w1_scale is None or w2_scale is None:
             raise ValueError("use_fp8_w8a8 needs w1_scale and w2_scale")
         return fused_moe_fp8(hidden_states, w1, w1_scale, w2, w2_scale, topk_weights, topk_ids, out=out,
-                             workspace=workspace)
+                             workspace=workspace, scale_format=scale_format)
     a = _expert_args("fused_moe", hidden_states, w1, w2, topk_weights, topk_ids, out, workspace)
     _lib.check(
         a.lib.moe_fused_experts(a.dt, _ptr(a.x), _ptr(a.w1), _ptr(a.w2), _ptr(a.tw), _ptr(a.ti), a.M, a.E, a.k, a.K,
@@ -291,6 +293,42 @@ def _expert_args(name, hidden_states, w1, w2, topk_weights, topk_ids, out, works
     return a
 
 
+_SCALE_FMT = {"fp32": _lib.MOE_FP8_SCALE_FP32, "ue8m0": _lib.MOE_FP8_SCALE_UE8M0}
+
+
+def _fmt_code(name, scale_format):
+    if scale_format not in _SCALE_FMT:
+        raise ValueError(f"{name}: scale_format must be 'fp32' or 'ue8m0', got {scale_format!r}")
+    return _SCALE_FMT[scale_format]
+
+
+def is_ue8m0(*scales: torch.Tensor) -> bool:
+    """True when every scale is a positive power of two, i.e. exactly a UE8M0 code (the
+    block-scale format of tcgen05's kind::mxf8f6f4 MMA). One device-to-host read."""
+    ok = None
+    for s in scales:
+        b = s.detach().to(torch.float32).contiguous().view(torch.int32)
+        t = ((b & 0x7FFFFF) == 0).all() & (b > 0).all() & (b < 0x7F800000).all()
+        ok = t if ok is None else ok & t
+    return bool(ok.item()) if ok is not None else False
+
+
+_FMT_CACHE: dict = {}
+
+
+def weights_scale_format(w1_scale: torch.Tensor, w2_scale: torch.Tensor) -> str:
+    """'ue8m0' when both weight scale tensors hold only powers of two, else 'fp32'; cached
+    per (pointer, version, shape) of the two tensors, so the check runs once per weights."""
+    key = tuple((t.data_ptr(), t._version, tuple(t.shape), t.dtype) for t in (w1_scale, w2_scale))
+    fmt = _FMT_CACHE.get(key)
+    if fmt is None:
+        fmt = "ue8m0" if is_ue8m0(w1_scale, w2_scale) else "fp32"
+        if len(_FMT_CACHE) >= 64:
+            _FMT_CACHE.clear()
+        _FMT_CACHE[key] = fmt
+    return fmt
+
+
 def _fp8_bytes(t: torch.Tensor) -> torch.Tensor:
     if t.dtype == torch.float8_e4m3fn:
         return t.view(torch.uint8)
@@ -299,38 +337,47 @@ def _fp8_bytes(t: torch.Tensor) -> torch.Tensor:
     return t
 
 
-def quantize_rows_fp8(x: torch.Tensor):
-    """Per row, per 128 columns e4m3 quantisation: returns (q float8_e4m3fn [M, K], scales fp32 [M, K/128])."""
+def quantize_rows_fp8(x: torch.Tensor, scale_format: str = "ue8m0"):
+    """Per row, per 128 columns e4m3 quantisation: returns (q float8_e4m3fn [M, K], scales fp32 [M, K/128]).
+    scale_format 'ue8m0' rounds each scale up to a power of two, 'fp32' keeps amax / 448."""
     dev = _require_cuda("quantize_rows_fp8", x)
+    fmt = _fmt_code("quantize_rows_fp8", scale_format)
     dt = {torch.bfloat16: _lib.MOE_DTYPE_BF16, torch.float16: _lib.MOE_DTYPE_FP16,
           torch.float32: _lib.MOE_DTYPE_FP32}[x.dtype]
     x = x.contiguous()
     M, K = x.shape
     q = torch.empty(M, K, dtype=torch.uint8, device=dev)
     s = torch.empty(M, K // 128, dtype=torch.float32, device=dev)
-    _lib.check(_lib.load().moe_quantize_rows_fp8(dt, _ptr(x), M, K, _ptr(q), _ptr(s), _stream(dev)),
+    _lib.check(_lib.load().moe_quantize_rows_fp8(dt, _ptr(x), M, K, _ptr(q), _ptr(s), fmt, _stream(dev)),
                "moe_quantize_rows_fp8")
     return q.view(torch.float8_e4m3fn), s
 
 
-def quantize_weights_fp8(w: torch.Tensor):
-    """Per 128 x 128 block e4m3 quantisation of [E, R, C] weights: (q float8_e4m3fn, scales fp32 [E, R/128, C/128])."""
+def quantize_weights_fp8(w: torch.Tensor, scale_format: str = "ue8m0"):
+    """Per 128 x 128 block e4m3 quantisation of [E, R, C] weights: (q float8_e4m3fn, scales fp32 [E, R/128, C/128]).
+    scale_format 'ue8m0' (powers of two: the block-scaled GEMMs take them) or 'fp32' (amax / 448)."""
     dev = _require_cuda("quantize_weights_fp8", w)
+    fmt = _fmt_code("quantize_weights_fp8", scale_format)
     dt = {torch.bfloat16: _lib.MOE_DTYPE_BF16, torch.float16: _lib.MOE_DTYPE_FP16,
           torch.float32: _lib.MOE_DTYPE_FP32}[w.dtype]
     w = w.contiguous()
     E, R, C = w.shape
     q = torch.empty(E, R, C, dtype=torch.uint8, device=dev)
     s = torch.empty(E, R // 128, C // 128, dtype=torch.float32, device=dev)
-    _lib.check(_lib.load().moe_quantize_blocks_fp8(dt, _ptr(w), E, R, C, _ptr(q), _ptr(s), _stream(dev)),
+    _lib.check(_lib.load().moe_quantize_blocks_fp8(dt, _ptr(w), E, R, C, _ptr(q), _ptr(s), fmt, _stream(dev)),
                "moe_quantize_blocks_fp8")
     return q.view(torch.float8_e4m3fn), s
 
 
 def fused_moe_fp8(hidden_states, w1_q, w1_scale, w2_q, w2_scale, topk_weights, topk_ids, *, out=None,
-                  workspace=None):
+                  workspace=None, scale_format=None):
     """FP8 w8a8 expert path: bf16 tokens (quantised per token per 128 inside), e4m3 weights with
-    fp32 scales per 128 x 128 block (``quantize_weights_fp8``); returns bf16 [M, K]."""
+    fp32 scales per 128 x 128 block (``quantize_weights_fp8``); returns bf16 [M, K].
+
+    scale_format names the weights' scales: 'ue8m0' (every scale a power of two; the tokens
+    and the SiLU*mul rows are then quantised with power-of-two scales too, and prefill-sized
+    batches run the block-scaled GEMMs) or 'fp32' (any scales, fp32 promotion per K block).
+    None decides from the scales themselves (``weights_scale_format``, one check per weights)."""
     dev = _require_cuda("fused_moe_fp8", hidden_states, w1_q, w2_q, w1_scale, w2_scale, topk_weights, topk_ids)
     if hidden_states.dtype != torch.bfloat16:
         raise TypeError("fused_moe_fp8: hidden_states must be bf16")
@@ -347,6 +394,7 @@ def fused_moe_fp8(hidden_states, w1_q, w1_scale, w2_q, w2_scale, topk_weights, t
     ti = topk_ids.to(torch.int32).contiguous()
     s1 = w1_scale.to(torch.float32).contiguous()
     s2 = w2_scale.to(torch.float32).contiguous()
+    fmt = _fmt_code("fused_moe_fp8", scale_format or weights_scale_format(s1, s2))
     if out is None:
         out = torch.empty(M, K, dtype=torch.bfloat16, device=dev)
     lib = _lib.load()
@@ -355,7 +403,8 @@ def fused_moe_fp8(hidden_states, w1_q, w1_scale, w2_q, w2_scale, topk_weights, t
         workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=dev)
     _lib.check(
         lib.moe_fused_experts_fp8(_ptr(x), _ptr(w1b), _ptr(s1), _ptr(w2b), _ptr(s2), _ptr(tw), _ptr(ti), M, E, k, K, N,
-                                  _ptr(out), _ptr(workspace), workspace.numel(), _ptr(status_word(dev)), _stream(dev)),
+                                  fmt, _ptr(out), _ptr(workspace), workspace.numel(), _ptr(status_word(dev)),
+                                  _stream(dev)),
         "moe_fused_experts_fp8")
     return out
 
@@ -369,10 +418,12 @@ def fp8_row_bytes(hidden_size: int) -> int:
     return n
 
 
-def quantize_rows_fp8_packed(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+def quantize_rows_fp8_packed(x: torch.Tensor, out: torch.Tensor | None = None,
+                             scale_format: str = "ue8m0") -> torch.Tensor:
     """Per token per 128 e4m3 quantisation of x [M, K] into packed rows uint8
     [M, fp8_row_bytes(K)] (codes, then the K / 128 fp32 scales): the expert-parallel FP8 payload."""
     dev = _require_cuda("quantize_rows_fp8_packed", x)
+    fmt = _fmt_code("quantize_rows_fp8_packed", scale_format)
     dt = {torch.bfloat16: _lib.MOE_DTYPE_BF16, torch.float16: _lib.MOE_DTYPE_FP16,
           torch.float32: _lib.MOE_DTYPE_FP32}[x.dtype]
     x = x.contiguous()
@@ -382,16 +433,17 @@ def quantize_rows_fp8_packed(x: torch.Tensor, out: torch.Tensor | None = None) -
         out = torch.empty(M, rb, dtype=torch.uint8, device=dev)
     if out.dtype != torch.uint8 or out.shape[0] < M or out.shape[1] != rb or not out.is_contiguous():
         raise ValueError("quantize_rows_fp8_packed: out must be contiguous uint8 [M, fp8_row_bytes(K)]")
-    _lib.check(_lib.load().moe_quantize_rows_fp8_packed(dt, _ptr(x), M, K, _ptr(out), _stream(dev)),
+    _lib.check(_lib.load().moe_quantize_rows_fp8_packed(dt, _ptr(x), M, K, _ptr(out), fmt, _stream(dev)),
                "moe_quantize_rows_fp8_packed")
     return out[:M]
 
 
 def fused_moe_fp8_rows(rows, hidden_size, w1_q, w1_scale, w2_q, w2_scale, topk_weights, topk_ids, *, out=None,
-                       workspace=None, max_ctas=0):
+                       workspace=None, max_ctas=0, scale_format=None):
     """FP8 expert path from packed e4m3 rows (``quantize_rows_fp8_packed``; rows uint8 [M, >=
     fp8_row_bytes(K)], row pitch a multiple of 16): the result of ``fused_moe_fp8`` on the
-    tokens those rows were quantised from. Returns bf16 [M, K]."""
+    tokens those rows were quantised from. Returns bf16 [M, K]. scale_format as for
+    ``fused_moe_fp8``; with 'ue8m0' the rows must carry power-of-two scales as well."""
     dev = _require_cuda("fused_moe_fp8_rows", rows, w1_q, w2_q, w1_scale, w2_scale, topk_weights, topk_ids)
     K = int(hidden_size)
     if rows.dtype != torch.uint8 or rows.dim() != 2 or rows.stride(1) != 1:
@@ -408,6 +460,7 @@ def fused_moe_fp8_rows(rows, hidden_size, w1_q, w1_scale, w2_q, w2_scale, topk_w
     ti = topk_ids.to(torch.int32).contiguous()
     s1 = w1_scale.to(torch.float32).contiguous()
     s2 = w2_scale.to(torch.float32).contiguous()
+    fmt = _fmt_code("fused_moe_fp8_rows", scale_format or weights_scale_format(s1, s2))
     if out is None:
         out = torch.empty(M, K, dtype=torch.bfloat16, device=dev)
     lib = _lib.load()
@@ -418,7 +471,7 @@ def fused_moe_fp8_rows(rows, hidden_size, w1_q, w1_scale, w2_q, w2_scale, topk_w
         return out
     _lib.check(
         lib.moe_fused_experts_fp8_rows(_ptr(rows), rows.stride(0), _ptr(w1b), _ptr(s1), _ptr(w2b), _ptr(s2), _ptr(tw),
-                                       _ptr(ti), M, E, k, K, N, _ptr(out), _ptr(workspace), workspace.numel(),
+                                       _ptr(ti), M, E, k, K, N, fmt, _ptr(out), _ptr(workspace), workspace.numel(),
                                        int(max_ctas), _ptr(status_word(dev)), _stream(dev)),
         "moe_fused_experts_fp8_rows")
     return out

@@ -1,8 +1,9 @@
 """fused_moe drop-in with FP8 w8a8 experts: ``ModelNew`` with the reference's constructor,
 parameters and forward signature (``fused_moe/v0/fused_moe.py:99-124,126-167``), running the
-DeepSeek-V3 FP8 recipe: the expert weights are quantised to e4m3 with one fp32 scale per
-128 x 128 block, the token rows per token per 128, and the expert GEMMs run
-tcgen05.mma.kind::f8f6f4 with fp32 block-scale promotion.
+DeepSeek FP8 recipe with Blackwell's UE8M0 scales: the expert weights are quantised to e4m3
+with one power-of-two scale per 128 x 128 block, the token rows per token per 128 the same
+way, and the expert GEMMs apply the scales in the tensor cores (tcgen05.mma.kind::mxf8f6f4.
+block_scale) at prefill sizes, with fp32 promotion per K block at decode sizes.
 
 The quantised weights are cached and re-made only when a parameter's ``_version`` or
 storage changes (the caching idea of ``fused_moe/v1/fused_moe.py:285-303``, here for the
@@ -56,8 +57,8 @@ class ModelNew(nn.Module):
         key = (self.w1.device, self.w1.data_ptr(), self.w1._version, self.w2.data_ptr(), self.w2._version)
         if self._cache is None or self._cache[0] != key:
             with torch.no_grad():
-                w1q, w1s = self._ops.quantize_weights_fp8(self.w1.detach().to(torch.bfloat16).contiguous())
-                w2q, w2s = self._ops.quantize_weights_fp8(self.w2.detach().to(torch.bfloat16).contiguous())
+                w1q, w1s = self._ops.quantize_weights_fp8(self.w1.detach().to(torch.bfloat16).contiguous(), "ue8m0")
+                w2q, w2s = self._ops.quantize_weights_fp8(self.w2.detach().to(torch.bfloat16).contiguous(), "ue8m0")
             self._cache = (key, w1q, w1s, w2q, w2s)
             self.quantizations += 1
         return self._cache[1:]
@@ -66,7 +67,7 @@ class ModelNew(nn.Module):
         w1q, w1s, w2q, w2s = self._fp8_weights()
         w, ids = self._ops.softmax_topk(router_logits, self.top_k, self.renormalize)
         out = self._ops.fused_moe(hidden_states.to(torch.bfloat16), w1q, w2q, w, ids, use_fp8_w8a8=True,
-                                  w1_scale=w1s, w2_scale=w2s)
+                                  w1_scale=w1s, w2_scale=w2s, scale_format="ue8m0")
         return out.to(hidden_states.dtype)
 
 

@@ -16,12 +16,14 @@ tensors and ``torch.compile`` graphs see the operators without running them:
         -> out [M, K] in the hidden dtype; the launches of fused_moe/v1/fused_moe.py:305-341,
         math of fused_moe/v0/fused_moe.py:141-167
     torch.ops.moe_b200.fused_moe_fp8(hidden_states, w1_q, w1_scale, w2_q, w2_scale,
-                                     topk_weights, topk_ids) -> out bf16 [M, K]
+                                     topk_weights, topk_ids, scale_format="") -> out bf16 [M, K]
+        (scale_format "" decides from the weight scales: "ue8m0" when all are powers of two)
     torch.ops.moe_b200.moe_align(topk_ids, num_experts, block_m)
         -> (counts, block_start, sorted_pairs)  (sorted_pairs' length depends on the
         capacity rule; the fake uses the same formula)
-    torch.ops.moe_b200.quantize_rows_fp8(x) -> (q e4m3 [M, K], scales fp32 [M, K / 128])
-    torch.ops.moe_b200.quantize_weights_fp8(w) -> (q e4m3 [E, R, C], scales fp32 [E, R / 128, C / 128])
+    torch.ops.moe_b200.quantize_rows_fp8(x, scale_format="ue8m0") -> (q e4m3 [M, K], scales fp32 [M, K / 128])
+    torch.ops.moe_b200.quantize_weights_fp8(w, scale_format="ue8m0")
+        -> (q e4m3 [E, R, C], scales fp32 [E, R / 128, C / 128])
 
 Every operator returns new tensors and writes none of its inputs (``mutates_args=()``).
 """
@@ -65,12 +67,13 @@ def _fused_moe_fake(hidden_states, w1, w2, topk_weights, topk_ids):
 
 @torch.library.custom_op(f"{_NS}::fused_moe_fp8", mutates_args=())
 def fused_moe_fp8_op(hidden_states: Tensor, w1_q: Tensor, w1_scale: Tensor, w2_q: Tensor, w2_scale: Tensor,
-                     topk_weights: Tensor, topk_ids: Tensor) -> Tensor:
-    return ops.fused_moe_fp8(hidden_states, w1_q, w1_scale, w2_q, w2_scale, topk_weights, topk_ids)
+                     topk_weights: Tensor, topk_ids: Tensor, scale_format: str = "") -> Tensor:
+    return ops.fused_moe_fp8(hidden_states, w1_q, w1_scale, w2_q, w2_scale, topk_weights, topk_ids,
+                             scale_format=scale_format or None)
 
 
 @fused_moe_fp8_op.register_fake
-def _fused_moe_fp8_fake(hidden_states, w1_q, w1_scale, w2_q, w2_scale, topk_weights, topk_ids):
+def _fused_moe_fp8_fake(hidden_states, w1_q, w1_scale, w2_q, w2_scale, topk_weights, topk_ids, scale_format=""):
     return hidden_states.new_empty(hidden_states.shape, dtype=torch.bfloat16)
 
 
@@ -94,22 +97,22 @@ def _moe_align_fake(topk_ids, num_experts, block_m=128):
 
 
 @torch.library.custom_op(f"{_NS}::quantize_rows_fp8", mutates_args=())
-def quantize_rows_fp8_op(x: Tensor) -> tuple[Tensor, Tensor]:
-    return ops.quantize_rows_fp8(x)
+def quantize_rows_fp8_op(x: Tensor, scale_format: str = "ue8m0") -> tuple[Tensor, Tensor]:
+    return ops.quantize_rows_fp8(x, scale_format)
 
 
 @quantize_rows_fp8_op.register_fake
-def _quantize_rows_fp8_fake(x):
+def _quantize_rows_fp8_fake(x, scale_format="ue8m0"):
     M, K = x.shape
     return x.new_empty(M, K, dtype=torch.float8_e4m3fn), x.new_empty(M, K // 128, dtype=torch.float32)
 
 
 @torch.library.custom_op(f"{_NS}::quantize_weights_fp8", mutates_args=())
-def quantize_weights_fp8_op(w: Tensor) -> tuple[Tensor, Tensor]:
-    return ops.quantize_weights_fp8(w)
+def quantize_weights_fp8_op(w: Tensor, scale_format: str = "ue8m0") -> tuple[Tensor, Tensor]:
+    return ops.quantize_weights_fp8(w, scale_format)
 
 
 @quantize_weights_fp8_op.register_fake
-def _quantize_weights_fp8_fake(w):
+def _quantize_weights_fp8_fake(w, scale_format="ue8m0"):
     E, R, C = w.shape
     return w.new_empty(E, R, C, dtype=torch.float8_e4m3fn), w.new_empty(E, R // 128, C // 128, dtype=torch.float32)

@@ -138,18 +138,20 @@ def test_fp8_packed_row_format(lib):
 def test_fp8_rows_argument_validation(lib):
     f = lib.moe_fused_experts_fp8_rows
     rb = lib.moe_fp8_row_bytes(512)
-    args = lambda M, stride, K, mc=0: f(None, stride, None, None, None, None, None, None, M, 8, 2, K, 256, None, None,
-                                        0, mc, None, None)
+    args = lambda M, stride, K, mc=0, fmt=0: f(None, stride, None, None, None, None, None, None, M, 8, 2, K, 256, fmt,
+                                               None, None, 0, mc, None, None)
     assert args(4, rb - 16, 512) == _lib.MOE_ERR_INVALID_ARG     # pitch shorter than a packed row
     assert args(4, rb + 8, 512) == _lib.MOE_ERR_INVALID_ARG      # pitch not a multiple of 16
     assert args(4, rb, 500) == _lib.MOE_ERR_BAD_SHAPE            # K % 128 != 0
     assert args(4, rb, 512, -1) == _lib.MOE_ERR_INVALID_ARG      # negative grid limit
     assert args(0, rb, 512) == _lib.MOE_OK                       # no rows: nothing to do
     assert args(4, rb, 512) == _lib.MOE_ERR_INVALID_ARG          # null pointers
+    assert args(4, rb, 512, 0, 2) == _lib.MOE_ERR_INVALID_ARG    # unknown scale format
     q = lib.moe_quantize_rows_fp8_packed
-    assert q(0, None, 4, 500, None, None) == _lib.MOE_ERR_BAD_SHAPE
-    assert q(7, None, 4, 512, None, None) == _lib.MOE_ERR_UNSUPPORTED
-    assert q(0, None, 4, 512, None, None) == _lib.MOE_ERR_INVALID_ARG
+    assert q(0, None, 4, 500, None, 0, None) == _lib.MOE_ERR_BAD_SHAPE
+    assert q(7, None, 4, 512, None, 0, None) == _lib.MOE_ERR_UNSUPPORTED
+    assert q(0, None, 4, 512, None, 0, None) == _lib.MOE_ERR_INVALID_ARG
+    assert q(0, None, 4, 512, None, 5, None) == _lib.MOE_ERR_INVALID_ARG  # unknown scale format
     # the EP pack and p2p dispatch take the packed rows only with K % 128 == 0
     pack = lib.moe_ep_pack
     assert pack(_lib.MOE_DTYPE_E4M3_ROW, None, None, None, 4, 520, 2, 4, 2, None, None, None, None, None,

@@ -1,6 +1,8 @@
 """GPU parity of the FP8 w8a8 path: e4m3 quantisers (bit-exact against the oracle) and the
 fused FP8 expert path (atol = rtol = 5e-2 elementwise against the oracle's fp32 expert path on
-the exact dequantised operands, and 1e-2 on the aggregate relative error).
+the exact dequantised operands, and 1e-2 on the aggregate relative error), with fp32 block
+scales (promotion GEMMs) and with power-of-two UE8M0 scales (block-scaled GEMMs at prefill
+sizes, the promotion kernels for decode-sized batches).
 
 The kernel multiplies the e4m3 values themselves and applies the fp32 block scales to fp32
 partial sums, so it differs from the oracle only in summation order; the bound is set by the
@@ -19,42 +21,51 @@ pytestmark = pytest.mark.gpu
 TOL8 = 5e-2
 
 
+FMTS = ["fp32", "ue8m0"]
+
+
+@pytest.mark.parametrize("fmt", FMTS)
 @pytest.mark.parametrize("M,K,dtype", [(1, 128, torch.bfloat16), (37, 512, torch.bfloat16), (64, 7168, torch.bfloat16),
                                        (9, 256, torch.float32), (5, 384, torch.float16)])
-def test_quantize_rows_bit_exact(cuda_device, M, K, dtype):
+def test_quantize_rows_bit_exact(cuda_device, M, K, dtype, fmt):
     gen = torch.Generator().manual_seed(M * K)
     x = (torch.randn(M, K, generator=gen) * torch.logspace(-3, 2, M)[:, None]).to(dtype)
     x[0, :128] = 0  # an all-zero block keeps scale 1
-    q, s = quantize_rows_fp8(x.to(cuda_device))
-    rq, rs = quantize_rows_128(x.float().numpy())
+    q, s = quantize_rows_fp8(x.to(cuda_device), scale_format=fmt)
+    rq, rs = quantize_rows_128(x.float().numpy(), pow2=fmt == "ue8m0")
     np.testing.assert_array_equal(s.cpu().numpy(), rs)
     np.testing.assert_array_equal(q.float().cpu().numpy(), rq)
 
 
+@pytest.mark.parametrize("fmt", FMTS)
 @pytest.mark.parametrize("E,R,C", [(1, 128, 128), (3, 256, 384), (2, 512, 1024)])
-def test_quantize_weights_bit_exact(cuda_device, E, R, C):
+def test_quantize_weights_bit_exact(cuda_device, E, R, C, fmt):
     gen = torch.Generator().manual_seed(E + R + C)
     w = (torch.randn(E, R, C, generator=gen) / C ** 0.5).to(torch.bfloat16)
-    q, s = quantize_weights_fp8(w.to(cuda_device))
-    rq, rs = quantize_blocks_128(w.float().numpy())
+    q, s = quantize_weights_fp8(w.to(cuda_device), scale_format=fmt)
+    rq, rs = quantize_blocks_128(w.float().numpy(), pow2=fmt == "ue8m0")
     np.testing.assert_array_equal(s.cpu().numpy(), rs)
     np.testing.assert_array_equal(q.float().cpu().numpy(), rq)
 
 
-def _fp8_weights(E, K, N, dev, seed):
+def _fp8_weights(E, K, N, dev, seed, fmt="ue8m0"):
     gen = torch.Generator(device=dev).manual_seed(seed)
     w1 = (torch.randn(E, 2 * N, K, generator=gen, device=dev) / K ** 0.5).to(torch.bfloat16)
     w2 = (torch.randn(E, K, N, generator=gen, device=dev) / N ** 0.5).to(torch.bfloat16)
-    w1q, w1s = quantize_weights_fp8(w1)
-    w2q, w2s = quantize_weights_fp8(w2)
+    w1q, w1s = quantize_weights_fp8(w1, scale_format=fmt)
+    w2q, w2s = quantize_weights_fp8(w2, scale_format=fmt)
     return w1q, w1s, w2q, w2s
 
 
+# (M, E, k): 1 and 37 take the decode kernels (at most 16 pairs per expert), 300, 129 and
+# 1024 the prefill GEMMs (block-scaled with ue8m0); 1024 x 4 over 16 experts fills whole
+# m-blocks and runs several tiles per CTA
+@pytest.mark.parametrize("fmt", FMTS)
 @pytest.mark.parametrize("M,E,k,K,N", [(1, 8, 2, 256, 128), (37, 16, 4, 512, 256), (300, 8, 2, 384, 128),
-                                       (129, 4, 1, 256, 384)])
-def test_fused_fp8_oracle(cuda_device, M, E, k, K, N):
+                                       (129, 4, 1, 256, 384), (1024, 16, 4, 1024, 512)])
+def test_fused_fp8_oracle(cuda_device, M, E, k, K, N, fmt):
     dev = cuda_device
-    w1q, w1s, w2q, w2s = _fp8_weights(E, K, N, dev, seed=M + E)
+    w1q, w1s, w2q, w2s = _fp8_weights(E, K, N, dev, seed=M + E, fmt=fmt)
     gen = torch.Generator(device=dev).manual_seed(M)
     x = torch.randn(M, K, generator=gen, device=dev).to(torch.bfloat16)
     w, ids = softmax_topk(torch.randn(M, E, generator=gen, device=dev), k)
@@ -62,7 +73,7 @@ def test_fused_fp8_oracle(cuda_device, M, E, k, K, N):
     args = (x.float().cpu().numpy(), w1q.float().cpu().numpy(), w1s.cpu().numpy(), w2q.float().cpu().numpy(),
             w2s.cpu().numpy(), w.cpu().numpy(), ids.cpu().numpy())
     got = out.float().cpu().numpy()
-    exact = moe_experts_fp8_ref(*args)
+    exact = moe_experts_fp8_ref(*args, pow2=fmt == "ue8m0")
     np.testing.assert_allclose(got, exact, atol=TOL8, rtol=TOL8)
     rel = np.linalg.norm(got - exact) / np.linalg.norm(exact)
     assert rel < 1e-2, rel
@@ -79,7 +90,7 @@ def test_functional_flag_routes_to_fp8(cuda_device):
     assert torch.equal(a, b)
 
 
-@pytest.mark.parametrize("M", [1, 8, 32, 128])
+@pytest.mark.parametrize("M", [1, 8, 32, 128, 4096])
 def test_dsv3_fp8_config(cuda_device, M, dsv3_fp8_weights):
     """DeepSeek-V3 FP8 layer: grouped_topk (sigmoid + bias, top-2 group sum, x2.5) feeding the FP8 expert path."""
     dev = cuda_device
@@ -124,9 +135,9 @@ def test_dsv3_fp8_bench_workload(cuda_device, dsv3_fp8_weights):
     assert torch.isfinite(out).all()
 
 
-@pytest.fixture(scope="module")
-def dsv3_fp8_weights(cuda_device):
-    w = _fp8_weights(256, 7168, 2048, cuda_device, seed=43)
+@pytest.fixture(scope="module", params=FMTS)
+def dsv3_fp8_weights(cuda_device, request):
+    w = _fp8_weights(256, 7168, 2048, cuda_device, seed=43, fmt=request.param)
     torch.cuda.empty_cache()
     yield w
     del w
