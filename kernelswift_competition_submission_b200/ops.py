@@ -313,20 +313,25 @@ def is_ue8m0(*scales: torch.Tensor) -> bool:
     return bool(ok.item()) if ok is not None else False
 
 
-_FMT_CACHE: dict = {}
+def _scale_fmt_of(t: torch.Tensor) -> bool:
+    # remembered on the tensor object with its _version: a new tensor at a reused address
+    # carries no stale answer, and an in-place change of the scales is seen
+    memo = getattr(t, "_moe_b200_ue8m0", None)
+    if memo is not None and memo[0] == t._version:
+        return memo[1]
+    ok = is_ue8m0(t)
+    try:
+        t._moe_b200_ue8m0 = (t._version, ok)
+    except (AttributeError, RuntimeError):
+        pass
+    return ok
 
 
 def weights_scale_format(w1_scale: torch.Tensor, w2_scale: torch.Tensor) -> str:
-    """'ue8m0' when both weight scale tensors hold only powers of two, else 'fp32'; cached
-    per (pointer, version, shape) of the two tensors, so the check runs once per weights."""
-    key = tuple((t.data_ptr(), t._version, tuple(t.shape), t.dtype) for t in (w1_scale, w2_scale))
-    fmt = _FMT_CACHE.get(key)
-    if fmt is None:
-        fmt = "ue8m0" if is_ue8m0(w1_scale, w2_scale) else "fp32"
-        if len(_FMT_CACHE) >= 64:
-            _FMT_CACHE.clear()
-        _FMT_CACHE[key] = fmt
-    return fmt
+    """'ue8m0' when both weight scale tensors hold only powers of two, else 'fp32'. The
+    answer is remembered on each tensor with its ``_version``, so the check (one
+    device-to-host read) runs once per weights."""
+    return "ue8m0" if _scale_fmt_of(w1_scale) and _scale_fmt_of(w2_scale) else "fp32"
 
 
 def _fp8_bytes(t: torch.Tensor) -> torch.Tensor:
@@ -394,7 +399,7 @@ def fused_moe_fp8(hidden_states, w1_q, w1_scale, w2_q, w2_scale, topk_weights, t
     ti = topk_ids.to(torch.int32).contiguous()
     s1 = w1_scale.to(torch.float32).contiguous()
     s2 = w2_scale.to(torch.float32).contiguous()
-    fmt = _fmt_code("fused_moe_fp8", scale_format or weights_scale_format(s1, s2))
+    fmt = _fmt_code("fused_moe_fp8", scale_format or weights_scale_format(w1_scale, w2_scale))
     if out is None:
         out = torch.empty(M, K, dtype=torch.bfloat16, device=dev)
     lib = _lib.load()
@@ -460,7 +465,7 @@ def fused_moe_fp8_rows(rows, hidden_size, w1_q, w1_scale, w2_q, w2_scale, topk_w
     ti = topk_ids.to(torch.int32).contiguous()
     s1 = w1_scale.to(torch.float32).contiguous()
     s2 = w2_scale.to(torch.float32).contiguous()
-    fmt = _fmt_code("fused_moe_fp8_rows", scale_format or weights_scale_format(s1, s2))
+    fmt = _fmt_code("fused_moe_fp8_rows", scale_format or weights_scale_format(w1_scale, w2_scale))
     if out is None:
         out = torch.empty(M, K, dtype=torch.bfloat16, device=dev)
     lib = _lib.load()

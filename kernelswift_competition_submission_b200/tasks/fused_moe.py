@@ -55,12 +55,15 @@ class ModelNew(nn.Module):
         self._graph = GraphCache(self._forward_eager)
 
     def _prepared_weights(self, dtype):
+        # the parameter objects themselves are part of the key (held by the cache, so a new
+        # parameter can never be mistaken for the old one at a reused address)
         key = (dtype, self.w1.device, self.w1.data_ptr(), self.w1._version, self.w2.data_ptr(), self.w2._version)
-        if self._cache is None or self._cache[0] != key:
+        if self._cache is None or self._cache[0] != key or self._cache[3] is not self.w1 or \
+                self._cache[4] is not self.w2:
             with torch.no_grad():
                 w1 = self.w1.detach().to(dtype).contiguous()
                 w2 = self.w2.detach().to(dtype).contiguous()
-            self._cache = (key, w1, w2)
+            self._cache = (key, w1, w2, self.w1, self.w2)
         return self._cache[1], self._cache[2]
 
     def _forward_eager(self, hidden_states, router_logits, w1, w2):

@@ -54,14 +54,17 @@ class ModelNew(nn.Module):
         self.quantizations = 0  # how many times the FP8 weights were (re)made
 
     def _fp8_weights(self):
+        # the parameter objects are part of the key (held by the cache: a new parameter at a
+        # reused address is never taken for the old one)
         key = (self.w1.device, self.w1.data_ptr(), self.w1._version, self.w2.data_ptr(), self.w2._version)
-        if self._cache is None or self._cache[0] != key:
+        if self._cache is None or self._cache[0] != key or self._cache[5] is not self.w1 or \
+                self._cache[6] is not self.w2:
             with torch.no_grad():
                 w1q, w1s = self._ops.quantize_weights_fp8(self.w1.detach().to(torch.bfloat16).contiguous(), "ue8m0")
                 w2q, w2s = self._ops.quantize_weights_fp8(self.w2.detach().to(torch.bfloat16).contiguous(), "ue8m0")
-            self._cache = (key, w1q, w1s, w2q, w2s)
+            self._cache = (key, w1q, w1s, w2q, w2s, self.w1, self.w2)
             self.quantizations += 1
-        return self._cache[1:]
+        return self._cache[1:5]
 
     def forward(self, hidden_states: torch.Tensor, router_logits: torch.Tensor) -> torch.Tensor:
         w1q, w1s, w2q, w2s = self._fp8_weights()

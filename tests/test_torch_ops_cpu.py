@@ -32,3 +32,21 @@ def test_fake_shapes():
         counts, block_start, pairs = torch.ops.moe_b200.moe_align(ids, 16, 128)
         assert counts.shape == (16,) and block_start.shape == (17,)
         assert pairs.shape == ((37 * 4 + 16 * 127 + 127) // 128 * 128,)
+
+
+def test_weights_scale_format_follows_tensor_not_address():
+    """The power-of-two check is remembered on each scale tensor with its _version: an in-place
+    change is seen, and a new tensor (even at a reused address) is checked afresh."""
+    from kernelswift_competition_submission_b200 import weights_scale_format
+
+    a = torch.full((2, 4, 3), 0.25)
+    assert weights_scale_format(a, a) == "ue8m0"
+    a.mul_(1.5)
+    assert weights_scale_format(a, a) == "fp32"
+    for _ in range(20):  # fresh tensors, which the allocator may place where freed ones were
+        b = torch.full((2, 4, 3), 0.3)
+        assert weights_scale_format(b, b) == "fp32"
+        del b
+        c = torch.full((2, 4, 3), 0.125)
+        assert weights_scale_format(c, c) == "ue8m0"
+        del c
