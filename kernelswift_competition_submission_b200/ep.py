@@ -100,7 +100,7 @@ class ExpertParallelMoE:
                  scoring_func="softmax", routed_scaling_factor=1.0, e_score_correction_bias=None,
                  renormalize=True, group=None, route_fn=None, expert_fn=None, chunks=None, reserve_sms=8,
                  transport="nccl", max_tokens=None, use_fp8_w8a8=False, w1_scale=None, w2_scale=None,
-                 quant_fn=None):
+                 quant_fn=None, p2p_fused_return=None):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -165,6 +165,13 @@ class ExpertParallelMoE:
             raise ValueError(f"transport must be 'nccl' or 'p2p', not {transport!r}")
         self.transport = transport
         self.max_tokens = max_tokens  # p2p arena size in tokens per rank (default: the first batch, max over ranks)
+        # bf16 p2p return: True = the down GEMM's epilogue stores each finished row into its
+        # source's arena; False = scatter GEMM, then a combine-and-return kernel (same bits);
+        # None = the fused return up to 4096 received rows per rank (world * max_tokens), where
+        # it hides the return under the GEMM, the separate kernels above it, where a row's last
+        # slot lands late in the GEMM and the returns would bunch up at its end. The choice
+        # depends only on the arena size, so every rank makes the same one.
+        self.p2p_fused_return = p2p_fused_return
         self._p2p = None
         # p2p failure detection: each forward ends with an asynchronous copy of the device
         # status word to pinned host memory; a later forward reads it once that copy is done
@@ -716,12 +723,21 @@ class ExpertParallelMoE:
                                                    ws, wsn, st), "moe_expert_align_gather")
             _lib.check(lib.moe_expert_gemm1(dt, _ptr(self.w1), R, E_l, k, K, N, ws, wsn, status, 0, st),
                        "moe_expert_gemm1")
-            # the down GEMM's epilogue sums each received row's slots and stores the sum into its
-            # source rank's arena over NVLink while the GEMM still runs (one kernel)
-            _lib.check(lib.moe_p2p_expert_gemm2_return(dt, _ptr(self.w2), ws, wsn, E_l, K, N, k, W, self.rank, cap,
-                                                       pb, base, seq, _ptr(p["scr_c"]), status, 0, st),
-                       "moe_p2p_expert_gemm2_return")
-            self._mark("experts")
+            fused = self.p2p_fused_return if self.p2p_fused_return is not None else R <= 4096
+            if fused:
+                # the down GEMM's epilogue sums each received row's slots and stores the sum into
+                # its source rank's arena over NVLink while the GEMM still runs (one kernel)
+                _lib.check(lib.moe_p2p_expert_gemm2_return(dt, _ptr(self.w2), ws, wsn, E_l, K, N, k, W, self.rank,
+                                                           cap, pb, base, seq, _ptr(p["scr_c"]), status, 0, st),
+                           "moe_p2p_expert_gemm2_return")
+                self._mark("experts")
+            else:
+                _lib.check(lib.moe_expert_gemm2(dt, _ptr(self.w2), R, E_l, k, K, N, ws, wsn, status, 0, st),
+                           "moe_expert_gemm2")
+                self._mark("experts")
+                _lib.check(lib.moe_p2p_combine_experts_back(dt, ws, E_l, K, N, k, W, self.rank, cap, pb, base, seq,
+                                                            _ptr(p["scr_c"]), status, st),
+                           "moe_p2p_combine_experts_back")
         _lib.check(lib.moe_p2p_wait(base, W, 2, cap, K, k, seq, status, st), "moe_p2p_wait")
         self._mark("combine_back")
         out = torch.empty(M, K, dtype=x.dtype, device=dev)

@@ -56,8 +56,9 @@ def _worker(rank, world, port, q, mode):
         sl = slice(rank * el, (rank + 1) * el)
         kw = dict(num_experts=E, topk=K_TOP, num_expert_group=8, topk_group=4, scoring_func="sigmoid",
                   routed_scaling_factor=2.5, e_score_correction_bias=bias, chunks=2 if how == "overlap" else 1)
-        if how == "p2p":
-            kw.update(transport="p2p", max_tokens=400)
+        if how in ("p2p", "p2psep"):
+            # p2psep: the scatter GEMM and a separate combine-and-return kernel (the prefill-sized choice)
+            kw.update(transport="p2p", max_tokens=400, p2p_fused_return=False if how == "p2psep" else None)
         if fp8:
             w1q, w1s = pkg.quantize_weights_fp8(w1)
             w2q, w2s = pkg.quantize_weights_fp8(w2)
@@ -79,7 +80,7 @@ def _worker(rank, world, port, q, mode):
             assert hot == layer.replicated
         # p2p: three steps, batch sizes changing per step and rank (rows a rank stops using
         # must be cleared in the destination's arena)
-        sizes = (m, 120 - 50 * rank, 390) if how == "p2p" else (m,)
+        sizes = (m, 120 - 50 * rank, 390) if how.startswith("p2p") else (m,)
         ok, err = True, 0.0
         for mm in sizes:
             xs = x[:mm] if mm <= m else torch.randn(mm, HID, generator=tg, device=dev).to(torch.bfloat16)
@@ -101,7 +102,7 @@ def _worker(rank, world, port, q, mode):
         q.put((rank, "error", traceback.format_exc()))
 
 
-MODES = ["plain", "overlap", "replicate", "p2p", "fp8_plain", "fp8_overlap", "fp8_replicate", "fp8_p2p"]
+MODES = ["plain", "overlap", "replicate", "p2p", "p2psep", "fp8_plain", "fp8_overlap", "fp8_replicate", "fp8_p2p"]
 
 
 @pytest.mark.parametrize("world", [1, 2])
@@ -109,7 +110,8 @@ MODES = ["plain", "overlap", "replicate", "p2p", "fp8_plain", "fp8_overlap", "fp
 def test_ep_matches_single_gpu(cuda_device, mode, world):
     """plain: one all-to-all each way; overlap: 2 token chunks on a side stream;
     replicate: the 5 busiest experts replicated on every rank (their pairs stay home);
-    p2p: dispatch and combine by NVLink stores into the peers' arenas, three steps;
+    p2p: dispatch and combine by NVLink stores into the peers' arenas, three steps (p2psep:
+    with the down GEMM and the return as separate kernels);
     fp8_*: the same with e4m3 weights, the packed e4m3 token rows as the payload."""
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
