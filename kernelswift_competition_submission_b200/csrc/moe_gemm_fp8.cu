@@ -48,8 +48,9 @@
 //   warp 0      all 32 lanes write the stage's B scale-factor atoms (the UE8M0
 //               codes of the tile's weight blocks) into shared memory; lane 0
 //               loads A, B and the A scale-factor atom (512 B) by TMA.
-//   warp 1      per stage: tcgen05.cp of the A atom (TMEM columns 256-259) and
-//               the two B atoms (260-267), then 4 x tcgen05.mma.kind::mxf8f6f4.
+//   warp 1      per stage: tcgen05.cp of the A atom (TMEM columns 256 + 16 s ..
+//               + 3 for stage s) and the two B atoms (the next 8 columns), then
+//               4 x tcgen05.mma.kind::mxf8f6f4.
 //               block_scale (M=128, N=256, K=32), K chunk k reading scale byte k.
 //   warps 4-11  wait for the tile's accumulator, read it (128 columns per thread),
 //               hand it back and run the same tile epilogue (act scales are
@@ -207,6 +208,7 @@ constexpr int kF8RegsLaunch = 168;  // 65536 / 384 rounded down to a multiple of
 constexpr int kF8RegsLow = 40;
 constexpr int kF8RegsHigh = 232;
 static_assert(128 * kF8RegsLow + 256 * kF8RegsHigh <= kF8Threads * kF8RegsLaunch, "register split exceeds the launch");
+static_assert(kF8BN + 4 * 16 <= 512, "accumulator and four scale-factor slots fit the TMEM allocation");
 
 template <int R> __device__ __forceinline__ void setmaxnreg_dec() {
   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(R));
@@ -379,7 +381,9 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
       int stage = 0;
       uint32_t phase = 0, aphase = 0;
       bool ok = true;
-      const uint32_t sfa_t = tmem_base + (uint32_t)kF8BN, sfb_t = sfa_t + 4;
+      // one 16-column scale-factor slot per stage (A: 4 columns, B: 8), so a stage's copies
+      // never overwrite the factors the previous stage's MMAs are still reading
+      const uint32_t sf_base = tmem_base + (uint32_t)kF8BN;
       for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
         if (!mbar_wait(&pempty[0], aphase ^ 1, status, s_abort)) break;  // previous tile read out
         tc_fence_after();
@@ -391,6 +395,7 @@ moe_gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
           const uint64_t b_desc = smem_desc_sw128(a_src + kF8ATile);
           const uint8_t* sfb = smem + L::kSfbOffset + stage * 1024;
           // issued by this thread ahead of the MMAs, which then read them in order
+          const uint32_t sfa_t = sf_base + (uint32_t)(stage * 16), sfb_t = sfa_t + 4;
           tmem_cp_sf(sfa_t, smem_desc_sf(smem + L::kAScaleOffset + stage * kBlockM * 4));
           tmem_cp_sf(sfb_t, smem_desc_sf(sfb));
           tmem_cp_sf(sfb_t + 4, smem_desc_sf(sfb + 512));

@@ -183,8 +183,9 @@ class ExpertParallelMoE:
         """This library's kernels launched by one CUDA forward."""
         if self.transport == "p2p":
             # routing, signal, dispatch, wait, align count, align scatter, GEMM1, then bf16: set-up of
-            # the fused return + GEMM2 with the combine and return in its epilogue; FP8: GEMM2 +
-            # fused combine-and-return (+ quantise, row gather, scale gather); then wait, reduce
+            # the fused return + GEMM2 with the combine and return in its epilogue, or GEMM2 + the
+            # combine-and-return kernel; FP8: GEMM2 + fused combine-and-return (+ quantise, row
+            # gather, scale gather); then wait, reduce
             return 14 if self.fp8 else 11
         # routing, then per chunk: EP count, EP pack, align count, align scatter, GEMM1, GEMM2,
         # combine, EP combine (FP8: + quantise once, row and scale gathers per chunk)

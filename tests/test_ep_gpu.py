@@ -137,3 +137,72 @@ def test_ep_matches_single_gpu(cuda_device, mode, world):
     assert len(res) == world, res
     for r, (s, v) in res.items():
         assert s == "ok", (r, s, v)
+
+
+def _launch_worker(port, q):
+    """One rank: count this library's kernels (demangled names in namespace moe::) that one
+    forward launches, measured by torch.profiler, against kernel_launches_per_step."""
+    try:
+        import torch.distributed as dist
+        from datetime import timedelta
+
+        from torch.profiler import ProfilerActivity, profile
+
+        import kernelswift_competition_submission_b200 as pkg
+        from kernelswift_competition_submission_b200.ep import ExpertParallelMoE
+
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        dev = torch.device("cuda", 0)
+        torch.cuda.set_device(dev)
+        dist.init_process_group("nccl", rank=0, world_size=1, device_id=dev, timeout=timedelta(seconds=60))
+        gen = torch.Generator(device=dev).manual_seed(9)
+        w1 = (torch.randn(E, 2 * INTER, HID, generator=gen, device=dev) / HID ** 0.5).to(torch.bfloat16)
+        w2 = (torch.randn(E, HID, INTER, generator=gen, device=dev) / INTER ** 0.5).to(torch.bfloat16)
+        w1q, w1s = pkg.quantize_weights_fp8(w1)
+        w2q, w2s = pkg.quantize_weights_fp8(w2)
+        x = torch.randn(200, HID, generator=gen, device=dev).to(torch.bfloat16)
+        g = torch.randn(200, E, generator=gen, device=dev)
+        base = dict(num_experts=E, topk=K_TOP, num_expert_group=8, topk_group=4, scoring_func="sigmoid",
+                    routed_scaling_factor=2.5)
+        cases = {"nccl": dict(chunks=1), "nccl_2chunks": dict(chunks=2), "p2p": dict(transport="p2p", max_tokens=256),
+                 "p2p_separate_return": dict(transport="p2p", max_tokens=256, p2p_fused_return=False),
+                 "fp8_nccl": dict(chunks=1, use_fp8_w8a8=True), "fp8_p2p": dict(transport="p2p", max_tokens=256,
+                                                                                 use_fp8_w8a8=True)}
+        out = {}
+        for name, kw in cases.items():
+            fp8 = kw.get("use_fp8_w8a8", False)
+            if fp8:
+                kw = dict(kw, w1_scale=w1s, w2_scale=w2s)
+            layer = ExpertParallelMoE(w1q if fp8 else w1, w2q if fp8 else w2, **base, **kw)
+            for _ in range(2):
+                layer.forward(x, g)
+            torch.cuda.synchronize()
+            with profile(activities=[ProfilerActivity.CUDA]) as prof:
+                layer.forward(x, g)
+                torch.cuda.synchronize()
+            names = [e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
+            ours = [n for n in names if "moe::" in n]
+            out[name] = (layer.kernel_launches_per_step, len(ours))
+            layer.close()
+        q.put((0, "ok", out))
+        dist.destroy_process_group()
+    except Exception:
+        q.put((0, "error", traceback.format_exc()))
+
+
+def test_kernel_launches_match_profiler(cuda_device):
+    """kernel_launches_per_step (what bench.py reports as gpu_launches) against the kernels a
+    forward really launches, per transport and dtype, counted by torch.profiler."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_launch_worker, args=(_free_port(), q))
+    p.start()
+    try:
+        r, s, v = q.get(timeout=240)
+    finally:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    assert s == "ok", v
+    for name, (claimed, measured) in v.items():
+        assert claimed == measured, (name, claimed, measured)
