@@ -74,12 +74,15 @@ def parse():
     ap.add_argument("--replicate-hot", type=int, default=0,
                     help="expert-parallel: replicate the N busiest experts (from the first batch's routing) on "
                          "every rank")
+    ap.add_argument("--routing-only", action="store_true",
+                    help="time grouped_topk alone over --tokens rows (DeepSeek-V3 rule, E = 256) and print its row; "
+                         "a few MB on the device, the command the routing kernel's ncu capture runs")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-configs", action="store_true",
                     help="skip the per-configuration rows (DeepSeek-V3 bf16 / FP8 token sweeps, Mixtral, routing, "
                          "task shapes) that a 1-GPU run adds under \"configs\"")
     ap.add_argument("--config-iters", type=int, default=20, help="timed calls per configuration row")
-    ap.add_argument("--e2e-steps", type=int, default=20,
+    ap.add_argument("--e2e-steps", type=int, default=40,
                     help="batches streamed through HostPipeline for the end-to-end figure (fill and drain amortised)")
     return ap.parse_args()
 
@@ -799,8 +802,30 @@ def run_native(args):
         print(json.dumps(result), flush=True)
 
 
+def run_routing_only(args):
+    """grouped_topk alone (sigmoid + bias, top-2 group sum, 4 of 8 groups, top-8, x2.5) over
+    --tokens rows of fp32 logits, one GPU; L2 flushed before each timed call."""
+    import torch
+
+    from kernelswift_competition_submission_b200 import ops
+
+    dev = torch.device("cuda", 0)
+    peaks = measured_peaks()
+    M, E, k = args.tokens, 256, DSV3["topk"]
+    _, g, b_ = _dsv3_inputs(1, dev)
+    g = torch.randn(M, E, generator=torch.Generator(device=dev).manual_seed(M), device=dev)
+    timer = _CallTimer(dev)
+    ms = timer.median_ms(lambda: ops.grouped_topk(None, g, k, True, 8, 4, "sigmoid", 2.5, e_score_correction_bias=b_),
+                         args.steps, warmup=args.warmup)
+    row = _row("grouped_topk", M, ms, 0, M * E * 4 + E * 4 + M * k * 8, peaks, peaks["bf16_tflops"])
+    print(json.dumps(dict(row, peak_source=f"{peaks['source']} hbm_gbs", steps=args.steps, warmup=args.warmup)))
+
+
 def main():
     args = parse()
+    if args.routing_only:
+        run_routing_only(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

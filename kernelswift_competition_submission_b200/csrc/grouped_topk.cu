@@ -184,10 +184,12 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
 grouped_topk_lanes_kernel(const float* __restrict__ gating, const float* __restrict__ bias, int64_t M, int topk,
                           int renormalize, int n_group, int topk_group, int scoring, int gmode, float scale,
                           float* __restrict__ out_w, int32_t* __restrict__ out_ids) {
+  __shared__ RouteScratch s_scr[kWarpsPerBlock];
   const int64_t tok = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
   if (tok >= M) return;  // whole warp exits together
   route_token_lanes<VPL, LPG, false>(gating + tok * (int64_t)(32 * VPL), bias, tok, topk, renormalize, n_group,
-                                     topk_group, scoring, gmode, scale, out_w, out_ids);
+                                     topk_group, scoring, gmode, scale, out_w, out_ids,
+                                     &s_scr[threadIdx.x >> 5]);
 }
 
 template <int VPL>

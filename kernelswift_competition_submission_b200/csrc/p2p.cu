@@ -131,7 +131,9 @@ p2p_dispatch_kernel(const uint4* __restrict__ x, const int32_t* __restrict__ ids
       }
       const int my_e = lane < topk ? __ldg(ids + t * topk + lane) : -1;
       const float my_w = lane < topk ? __ldg(w + t * topk + lane) : 0.f;
-      for (int d = 0; d < world; ++d) {
+      // destinations in the order me, me + 1, ...: the ranks do not all start on rank 0
+      for (int i = 0; i < world; ++i) {
+        const int d = me + i < world ? me + i : me + i - world;
         int r = -1;
         if ((mask >> d) & 1ull) {
           if (lane == 0) r = atomicAdd(claimed + d, 1);
@@ -140,7 +142,17 @@ p2p_dispatch_kernel(const uint4* __restrict__ x, const int32_t* __restrict__ ids
           char* base = reinterpret_cast<char*>(peer_base[d]);
           uint4* dst = reinterpret_cast<uint4*>(base + lay.recv_x) + row * row_vecs;
           const uint4* src = x + t * row_vecs;
-          for (int64_t v = lane; v < row_vecs; v += 32) dst[v] = __ldg(src + v);
+          // four 16-byte loads in flight per lane before their stores
+          int64_t v = lane;
+          for (; v + 96 < row_vecs; v += 128) {
+            const uint4 a0 = __ldg(src + v), a1 = __ldg(src + v + 32), a2 = __ldg(src + v + 64),
+                        a3 = __ldg(src + v + 96);
+            dst[v] = a0;
+            dst[v + 32] = a1;
+            dst[v + 64] = a2;
+            dst[v + 96] = a3;
+          }
+          for (; v < row_vecs; v += 32) dst[v] = __ldg(src + v);
           if (lane < topk) {
             const bool own = my_e >= 0 && my_e < epr * world && my_e / epr == d;
             reinterpret_cast<int32_t*>(base + lay.recv_id)[row * topk + lane] = own ? my_e - d * epr : -1;

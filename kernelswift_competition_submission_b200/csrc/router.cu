@@ -184,10 +184,13 @@ router_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
   if (*s_last) {
     __threadfence();
     const int64_t t_end = M < (int64_t)(mb + 1) * kBlockM ? M : (int64_t)(mb + 1) * kBlockM;
+    // the stage buffers are idle now (every load was consumed by a finished MMA): one
+    // routing scratch per warp at their start
+    RouteScratch* scr = reinterpret_cast<RouteScratch*>(smem) + warp;
     for (int64_t tok = (int64_t)mb * kBlockM + sp + (int64_t)warp * splits; tok < t_end;
          tok += (int64_t)(kRThreads / 32) * splits)
       route_token_lanes<8, LPG, true>(logits + tok * kRN, bias, tok, topk, renormalize, n_group, topk_group,
-                                      scoring, gmode, scale, out_w, out_ids);
+                                      scoring, gmode, scale, out_w, out_ids, scr);
   }
   __syncthreads();
   if (warp == 2) {

@@ -91,6 +91,74 @@ __device__ __forceinline__ void route_select_sorted8(const float (&c)[8], const 
   }
 }
 
+// Per-warp shared memory of route_select_threshold8.
+struct RouteScratch {
+  uint64_t key[32];   // compacted candidates, one per lane
+  float s[32];        // their scores
+  float sel_s[32];    // the chosen experts' scores, in rank order
+  int32_t sel_id[32]; // the chosen experts, in rank order
+};
+
+// Top-k selection by threshold for E = 256 with group masking. Every kept group's two best
+// values are >= tkey's value (the smallest second-best of the kept groups), and those are
+// 2 * topk_group >= topk values, so the k-th best kept value is >= it and nothing below it
+// can be chosen. The candidates at or above it (about 8-16 per token for Gaussian logits)
+// are compacted one per lane in shared memory; each lane's rank is the number of
+// candidates with a larger key (the strict order: value descending, index ascending), and
+// ranks 0..topk-1 are the result, in order. Output bits equal route_select_sorted8's: the
+// same chosen experts in the same order, the same scores, the same butterfly sum.
+// Returns false (nothing written) when more than 32 candidates pass; the caller then runs
+// route_select_sorted8.
+__device__ __forceinline__ bool route_select_threshold8(const float (&c)[8], const float (&s)[8], int e0, int lane,
+                                                        bool kept, uint32_t tkey, int64_t tok, int topk,
+                                                        int renormalize, float scale, float* __restrict__ out_w,
+                                                        int32_t* __restrict__ out_ids, RouteScratch* scr) {
+  uint32_t m = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m |= (kept && ordered_key(c[i]) >= tkey) ? (1u << i) : 0u;
+  const int cnt = __popc(m);
+  const int n = (int)__reduce_add_sync(0xffffffffu, (unsigned)cnt);
+  if (n > 32) return false;
+  int pre = cnt;  // inclusive prefix over the lanes
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, pre, off);
+    if (lane >= off) pre += v;
+  }
+  pre -= cnt;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    if ((m >> i) & 1u) {
+      scr->key[pre] = route_key(c[i], e0 + i);
+      scr->s[pre] = s[i];
+      ++pre;
+    }
+  }
+  __syncwarp();
+  const uint64_t key = lane < n ? scr->key[lane] : 0ull;
+  const float sv = lane < n ? scr->s[lane] : 0.f;
+  int rank = 0;
+  for (int j = 0; j < n; ++j) rank += scr->key[j] > key ? 1 : 0;
+  if (lane < n && rank < topk) {
+    scr->sel_s[rank] = sv;
+    scr->sel_id[rank] = (int32_t)(~(uint32_t)key);
+  }
+  __syncwarp();
+  float my_w = lane < topk ? scr->sel_s[lane] : 0.f;
+  const int my_id = lane < topk ? scr->sel_id[lane] : 0;
+  __syncwarp();  // the scratch may be reused by this warp's next token
+  if (renormalize) {
+    const float tot = route_warp_sum(lane < topk ? my_w : 0.f);
+    my_w = my_w / tot;
+  }
+  if (scale != 1.0f) my_w *= scale;
+  if (lane < topk) {
+    out_w[tok * topk + lane] = my_w;
+    out_ids[tok * topk + lane] = my_id;
+  }
+  return true;
+}
+
 // Top-k selection for any VPL: per-lane insertion sort of the candidates (value descending,
 // equal values in index order), then per round a warp arg-max of the heads.
 template <int VPL>
@@ -151,23 +219,18 @@ __device__ __forceinline__ void route_select_insertion(float (&c)[VPL], float (&
 // round is one warp arg-max over the lanes' current heads (two redux.sync reductions);
 // the winner pops its head.
 // The scores (weights before renormalisation) travel with the sorted candidates.
-// One token's routing by one warp (all 32 lanes): `row` holds its E = 32 * VPL
-// logits. kCoherent reads them through L2 (rows that other CTAs of the same
-// launch wrote), otherwise through the read-only path.
-template <int VPL, int LPG, bool kCoherent>
-__device__ __forceinline__ void route_token_lanes(const float* row, const float* __restrict__ bias, int64_t tok,
-                                                  int topk, int renormalize, int n_group, int topk_group,
-                                                  int scoring, int gmode, float scale, float* __restrict__ out_w,
-                                                  int32_t* __restrict__ out_ids) {
+// With VPL = 8, group masking, 2 * topk_group >= topk and a per-warp `scr`, the top-k
+// is taken by route_select_threshold8 instead (same result, fewer instructions).
+// One token's routing by one warp (all 32 lanes); this lane holds the logits x (and the
+// bias values bv, when has_bias) of experts [lane * VPL, lane * VPL + VPL).
+template <int VPL, int LPG>
+__device__ __forceinline__ void route_token_values(const float (&x)[VPL], const float (&bv)[VPL], bool has_bias,
+                                                   int64_t tok, int topk, int renormalize, int n_group,
+                                                   int topk_group, int scoring, int gmode, float scale,
+                                                   float* __restrict__ out_w, int32_t* __restrict__ out_ids,
+                                                   RouteScratch* scr) {
   const int lane = threadIdx.x & 31;
   const int e0 = lane * VPL;
-  float x[VPL];
-#pragma unroll
-  for (int i = 0; i < VPL; i += 4) {
-    const float4 v = kCoherent ? __ldcg(reinterpret_cast<const float4*>(row + e0 + i))
-                               : __ldg(reinterpret_cast<const float4*>(row + e0 + i));
-    x[i] = v.x; x[i + 1] = v.y; x[i + 2] = v.z; x[i + 3] = v.w;
-  }
   float s[VPL];
   if (scoring == MOE_SCORING_SOFTMAX) {
     float m = -INFINITY;
@@ -188,12 +251,9 @@ __device__ __forceinline__ void route_token_lanes(const float* row, const float*
     for (int i = 0; i < VPL; ++i) s[i] = 1.0f / (1.0f + expf(-x[i]));
   }
   float c[VPL];
-  if (bias) {
+  if (has_bias) {
 #pragma unroll
-    for (int i = 0; i < VPL; i += 4) {
-      const float4 b = __ldg(reinterpret_cast<const float4*>(bias + e0 + i));
-      c[i] = s[i] + b.x; c[i + 1] = s[i + 1] + b.y; c[i + 2] = s[i + 2] + b.z; c[i + 3] = s[i + 3] + b.w;
-    }
+    for (int i = 0; i < VPL; ++i) c[i] = s[i] + bv[i];
   } else {
 #pragma unroll
     for (int i = 0; i < VPL; ++i) c[i] = s[i];
@@ -225,7 +285,16 @@ __device__ __forceinline__ void route_token_lanes(const float* row, const float*
       const float o = __shfl_sync(0xffffffffu, gs, h * LPG);
       rank += (o > gs) || (o == gs && h < my_g);
     }
-    if (rank >= topk_group) {
+    const bool kept = rank < topk_group;
+    if constexpr (VPL == 8) {
+      if (scr != nullptr && 2 * topk_group >= topk) {
+        const uint32_t tkey = __reduce_min_sync(0xffffffffu, kept ? ordered_key(b2) : 0xffffffffu);
+        if (route_select_threshold8(c, s, e0, lane, kept, tkey, tok, topk, renormalize, scale, out_w, out_ids,
+                                    scr))
+          return;
+      }
+    }
+    if (!kept) {
 #pragma unroll
       for (int i = 0; i < VPL; ++i) c[i] = -INFINITY;
     }
@@ -236,6 +305,40 @@ __device__ __forceinline__ void route_token_lanes(const float* row, const float*
   } else {
     route_select_insertion<VPL>(c, s, e0, lane, tok, topk, renormalize, scale, out_w, out_ids);
   }
+}
+
+// Loads the logits of one token (`row`, E = 32 * VPL floats) and the bias, then applies the
+// rule. kCoherent reads the logits through L2 (rows that other CTAs of the same launch
+// wrote), otherwise through the read-only path.
+template <int VPL>
+__device__ __forceinline__ void route_load_row(const float* row, float (&x)[VPL], bool coherent) {
+  const int e0 = (threadIdx.x & 31) * VPL;
+#pragma unroll
+  for (int i = 0; i < VPL; i += 4) {
+    const float4 v = coherent ? __ldcg(reinterpret_cast<const float4*>(row + e0 + i))
+                              : __ldg(reinterpret_cast<const float4*>(row + e0 + i));
+    x[i] = v.x; x[i + 1] = v.y; x[i + 2] = v.z; x[i + 3] = v.w;
+  }
+}
+template <int VPL>
+__device__ __forceinline__ void route_load_bias(const float* __restrict__ bias, float (&bv)[VPL]) {
+  const int e0 = (threadIdx.x & 31) * VPL;
+#pragma unroll
+  for (int i = 0; i < VPL; i += 4) {
+    const float4 b = bias ? __ldg(reinterpret_cast<const float4*>(bias + e0 + i)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    bv[i] = b.x; bv[i + 1] = b.y; bv[i + 2] = b.z; bv[i + 3] = b.w;
+  }
+}
+template <int VPL, int LPG, bool kCoherent>
+__device__ __forceinline__ void route_token_lanes(const float* row, const float* __restrict__ bias, int64_t tok,
+                                                  int topk, int renormalize, int n_group, int topk_group,
+                                                  int scoring, int gmode, float scale, float* __restrict__ out_w,
+                                                  int32_t* __restrict__ out_ids, RouteScratch* scr = nullptr) {
+  float x[VPL], bv[VPL];
+  route_load_row<VPL>(row, x, kCoherent);
+  route_load_bias<VPL>(bias, bv);
+  route_token_values<VPL, LPG>(x, bv, bias != nullptr, tok, topk, renormalize, n_group, topk_group, scoring, gmode,
+                               scale, out_w, out_ids, scr);
 }
 
 }  // namespace moe

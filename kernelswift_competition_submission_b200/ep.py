@@ -100,7 +100,7 @@ class ExpertParallelMoE:
                  scoring_func="softmax", routed_scaling_factor=1.0, e_score_correction_bias=None,
                  renormalize=True, group=None, route_fn=None, expert_fn=None, chunks=None, reserve_sms=8,
                  transport="nccl", max_tokens=None, use_fp8_w8a8=False, w1_scale=None, w2_scale=None,
-                 quant_fn=None, p2p_fused_return=None):
+                 quant_fn=None, p2p_fused_return=None, p2p_chunk_tokens=512):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -150,8 +150,11 @@ class ExpertParallelMoE:
         # chunks from 4 ranks up, none below. Measured on B200 (DeepSeek-V3 layer, 32768 tokens):
         # 8 GPUs 6.88 M tokens/s without, 7.16 M with 2 chunks / 16 SMs, 7.69 M with 2 chunks /
         # 8 SMs; 2 GPUs 2.57 M without, 2.27 M with 2 chunks / 16 SMs (all-to-alls small there).
+        # With transport="p2p", chunks > 1 is opt-in: measured on 2 GPUs (32768 tokens) the chunked
+        # peer-memory layer took 13.1-13.8 ms against 11.1 ms in one piece (each chunk re-reads
+        # every local expert's weights and halves the rows per expert).
         if chunks is None:
-            chunks = 2 if self.world >= 4 else 1
+            chunks = 2 if self.world >= 4 and transport == "nccl" else 1
         self.chunks = max(1, int(chunks))
         self.reserve_sms = max(0, int(reserve_sms))
         self._comm = None
@@ -172,7 +175,13 @@ class ExpertParallelMoE:
         # slot lands late in the GEMM and the returns would bunch up at its end. The choice
         # depends only on the arena size, so every rank makes the same one.
         self.p2p_fused_return = p2p_fused_return
+        # p2p with chunks > 1: one arena per chunk when every chunk holds at least this many
+        # tokens per rank (prefill); smaller batches keep one arena (decode)
+        self.p2p_chunk_tokens = max(1, int(p2p_chunk_tokens))
         self._p2p = None
+        self._p2p_cap = 0
+        self._last_recv_ids = None
+        self._ws_chunks = []  # expert-path workspaces of the chunked peer-memory forward
         # p2p failure detection: each forward ends with an asynchronous copy of the device
         # status word to pinned host memory; a later forward reads it once that copy is done
         self._p2p_status = None      # (pinned host int32 [1], event) of the last forward
@@ -182,11 +191,13 @@ class ExpertParallelMoE:
     def kernel_launches_per_step(self):
         """This library's kernels launched by one CUDA forward."""
         if self.transport == "p2p":
-            # routing, signal, dispatch, wait, align count, align scatter, GEMM1, then bf16: set-up of
-            # the fused return + GEMM2 with the combine and return in its epilogue, or GEMM2 + the
-            # combine-and-return kernel; FP8: GEMM2 + fused combine-and-return (+ quantise, row
-            # gather, scale gather); then wait, reduce
-            return 14 if self.fp8 else 11
+            # routing, then per arena (one, or one per token chunk): signal, dispatch, wait, align
+            # count, align scatter, GEMM1, then bf16: set-up of the fused return + GEMM2 with the
+            # combine and return in its epilogue, or GEMM2 + the combine-and-return kernel; FP8:
+            # GEMM2 + fused combine-and-return (+ row gather, scale gather, and the quantiser
+            # once per step); then wait, reduce
+            n = len(self._p2p) if self._p2p else 1
+            return 2 + 12 * n if self.fp8 else 1 + 10 * n
         # routing, then per chunk: EP count, EP pack, align count, align scatter, GEMM1, GEMM2,
         # combine, EP combine (FP8: + quantise once, row and scale gathers per chunk)
         return (2 + 10 * self.chunks) if self.fp8 else (1 + 8 * self.chunks)
@@ -558,20 +569,33 @@ class ExpertParallelMoE:
     def local_work(self):
         """(valid local pairs, distinct local experts) of the last forward (synchronises)."""
         ids = self._last_recv_ids
+        if ids is None:
+            return 0, 0
         valid = ids[ids >= 0]
         return int(valid.numel()), int(torch.unique(valid).numel())
 
     # ------------------------------------------------------------------ NVLink peer-memory transport
     def _p2p_setup(self, M, K, dtype, dev):
-        """Collective: every rank allocates an arena for `cap` tokens per rank (the largest
-        local batch over the ranks), exchanges CUDA IPC handles and opens the others'."""
-        from . import _lib
-
-        lib = _lib.load()
+        """Collective: the arenas of this layer for `cap` tokens per rank (the largest local
+        batch over the ranks): one arena, or with chunks > 1 one per chunk of ceil(cap / chunks)
+        tokens, each with its own flags and sequence numbers."""
         self._p2p_release()
         m = torch.tensor([M], dtype=torch.int64, device=dev)
         dist.all_reduce(m, op=dist.ReduceOp.MAX, group=self.group)
         cap = max(1, int(m.item()))
+        C = self.chunks if cap // max(1, self.chunks) >= self.p2p_chunk_tokens else 1
+        self._p2p_cap = cap
+        capc = cap if C == 1 else -(-cap // C)
+        self._p2p = [self._p2p_arena(capc, K, dtype, dev) for _ in range(C)]
+        torch.cuda.synchronize(dev)
+        dist.barrier(group=self.group)
+
+    def _p2p_arena(self, cap, K, dtype, dev):
+        """Collective: allocate this rank's arena for `cap` tokens per source rank, exchange
+        the CUDA IPC handles and open the other ranks' arenas."""
+        from . import _lib
+
+        lib = _lib.load()
         nbytes = int(lib.moe_p2p_arena_bytes(self.world, cap, K, self.topk))
         if nbytes <= 0:
             raise ValueError("p2p transport: unsupported shape")
@@ -592,14 +616,12 @@ class ExpertParallelMoE:
                 bases.append(pb.value)
         offs = (ctypes.c_int64 * 9)()
         _lib.check(lib.moe_p2p_arena_offsets(self.world, cap, K, self.topk, offs), "moe_p2p_arena_offsets")
-        self._p2p = {
+        return {
             "cap": cap, "K": K, "dtype": dtype, "base": base.value, "bases": bases, "offs": list(offs), "seq": 0,
             "peer_bases": torch.tensor(bases, dtype=torch.int64, device=dev),
             "scr_d": torch.zeros(2 * self.world + 1, dtype=torch.int32, device=dev),
             "scr_c": torch.zeros(max(1, self.world), dtype=torch.int32, device=dev),
         }
-        torch.cuda.synchronize(dev)
-        dist.barrier(group=self.group)
 
     def _p2p_release(self):
         if self._p2p is None:
@@ -609,11 +631,13 @@ class ExpertParallelMoE:
         lib = _lib.load()
         torch.cuda.synchronize()
         dist.barrier(group=self.group)  # no rank still writes into an arena being unmapped
-        for r, b in enumerate(self._p2p["bases"]):
-            if r != self.rank:
-                lib.moe_p2p_close(ctypes.c_void_p(b))
+        for a in self._p2p:
+            for r, b in enumerate(a["bases"]):
+                if r != self.rank:
+                    lib.moe_p2p_close(ctypes.c_void_p(b))
         dist.barrier(group=self.group)
-        lib.moe_p2p_free(ctypes.c_void_p(self._p2p["base"]))
+        for a in self._p2p:
+            lib.moe_p2p_free(ctypes.c_void_p(a["base"]))
         self._p2p = None
 
     # ------------------------------------------------------------------ p2p failure handling
@@ -661,13 +685,14 @@ class ExpertParallelMoE:
         self._p2p_raise_if_failed()
         M, K = x.shape
         dev = x.device
-        p = self._p2p
-        if p is None:  # collective: the first forward of every rank
+        if self._p2p is None:  # collective: the first forward of every rank
             self._p2p_setup(max(M, int(self.max_tokens or 0)), K, x.dtype, dev)
-            p = self._p2p
-        if M > p["cap"] or K != p["K"] or x.dtype != p["dtype"]:
+        p = self._p2p[0]
+        if M > self._p2p_cap or K != p["K"] or x.dtype != p["dtype"]:
             raise ValueError(f"p2p transport: batch [{M}, {K}] {x.dtype} does not fit the arena "
-                             f"(max_tokens {p['cap']}, hidden {p['K']}, {p['dtype']})")
+                             f"(max_tokens {self._p2p_cap}, hidden {p['K']}, {p['dtype']})")
+        if len(self._p2p) > 1:
+            return self._forward_p2p_chunked(x, gating)
         lib = _lib.load()
         st = _stream(dev)
         status = _ptr(status_word(dev))
@@ -747,6 +772,144 @@ class ExpertParallelMoE:
                        "moe_p2p_reduce")
         self._mark("reduce")
         # the status word, copied to the host behind this step (read by a later forward)
+        if self._p2p_status is None:
+            self._p2p_status = (torch.zeros(1, dtype=torch.int32).pin_memory(), torch.cuda.Event())
+        host, ev = self._p2p_status
+        host.copy_(status_word(dev), non_blocking=True)
+        ev.record()
+        if self.profile and self._marks:
+            self.phase_log.append(self._marks)
+        return out
+
+    def _forward_p2p_chunked(self, x, gating):
+        """Peer-memory transport in token chunks, one arena per chunk (own flags, own sequence
+        numbers). Chunk 0 is dispatched on the current stream and the others on a side stream,
+        under chunk 0's experts; each chunk's combine-and-return runs on the side stream under
+        the next chunk's experts; the sums per token come last. The expert GEMMs leave
+        `reserve_sms` SMs to the transport kernels. A wait kernel never spins on a flag that a
+        kernel of its own GPU has still to write: before it, its stream waits (CUDA event) for
+        this rank's own kernel of that phase, so only the other ranks' kernels are awaited."""
+        from . import _lib
+        from .ops import _DTYPES, _ptr, status_word
+
+        M, K = x.shape
+        dev = x.device
+        arenas = self._p2p
+        C = len(arenas)
+        lib = _lib.load()
+        main = torch.cuda.current_stream(dev)
+        if self._comm is None:
+            self._comm = torch.cuda.Stream(device=dev)
+        side = self._comm
+        status = _ptr(status_word(dev))
+        dt = _DTYPES[x.dtype]
+        W, k = self.world, self.topk
+        E_l, N = self.w1.shape[0], self.w2.shape[2]
+        for a in arenas:
+            a["seq"] = (a["seq"] + 1) & 0xFFFFFFFF or 1
+        self._on_cuda = True
+        self._marks = []
+        self._mark("start")
+        w, ids = self.route_fn(x, gating)
+        self._mark("route")
+        xc = self.quant_fn(x) if self.fp8 else x.contiguous()
+        dt_rows = _lib.MOE_DTYPE_E4M3_ROW if self.fp8 else dt
+        ids32 = ids.to(torch.int32).contiguous()
+        w32 = w.to(torch.float32).contiguous()
+        bounds = [(M * c) // C for c in range(C + 1)]
+        max_ctas = 0
+        if self.reserve_sms:
+            max_ctas = max(1, torch.cuda.get_device_properties(dev).multi_processor_count - self.reserve_sms)
+        ev_route = torch.cuda.Event()
+        ev_route.record(main)
+        tok_rows = [self._buf(f"p2p_tr{c}", max(bounds[c + 1] - bounds[c], 1), W, torch.int32, dev)
+                    for c in range(C)]
+        ev_disp = []
+        for c, a in enumerate(arenas):
+            s = main if c == 0 else side
+            t0, t1 = bounds[c], bounds[c + 1]
+            pb = _ptr(a["peer_bases"])
+            with torch.cuda.stream(s):
+                if c == 1:
+                    side.wait_event(ev_route)
+                sp = s.cuda_stream
+                _lib.check(lib.moe_p2p_signal(pb, W, self.rank, 0, a["cap"], K, k, a["seq"], status, sp),
+                           "moe_p2p_signal")
+                _lib.check(lib.moe_p2p_dispatch(dt_rows, _ptr(xc[t0:t1]), _ptr(ids32[t0:t1]), _ptr(w32[t0:t1]),
+                                                t1 - t0, K, k, E_l, W, self.rank, a["cap"], pb, a["base"], a["seq"],
+                                                _ptr(a["scr_d"]), _ptr(tok_rows[c]), status, sp), "moe_p2p_dispatch")
+                ev = torch.cuda.Event()
+                ev.record(s)
+                ev_disp.append(ev)
+        if len(self._ws_chunks) != C:
+            self._ws_chunks = [None] * C
+        ev_back = []
+        st_main, st_side = main.cuda_stream, side.cuda_stream
+        for c, a in enumerate(arenas):
+            base, cap, o = a["base"], a["cap"], a["offs"]
+            pb = _ptr(a["peer_bases"])
+            main.wait_event(ev_disp[c])
+            _lib.check(lib.moe_p2p_wait(base, W, 1, cap, K, k, a["seq"], status, st_main), "moe_p2p_wait")
+            if c == 0:
+                self._mark("dispatch")
+                recv_ids = []
+            if self.profile:  # received ids, for local_work() statistics
+                rids = torch.empty(W * cap, k, dtype=torch.int32, device=dev)
+                _lib.check(lib.moe_p2p_copy_recv_ids(base, W, cap, K, k, _ptr(rids), st_main),
+                           "moe_p2p_copy_recv_ids")
+                recv_ids.append(rids)
+            R = W * cap
+            need = int(lib.moe_fused_workspace_bytes_fp8(R, E_l, k, K, N) if self.fp8 else
+                       lib.moe_fused_workspace_bytes(R, E_l, k, K, N))
+            if self._ws_chunks[c] is None or self._ws_chunks[c].numel() < need:
+                self._ws_chunks[c] = torch.empty(int(need * 1.25) + 256, dtype=torch.uint8, device=dev)
+            ws, wsn = _ptr(self._ws_chunks[c]), self._ws_chunks[c].numel()
+            rx, rid = base + o[4], base + o[5]
+            fused = False
+            if self.fp8:
+                _lib.check(lib.moe_fused_experts_fp8_rows(ctypes.c_void_p(rx), int(lib.moe_fp8_row_bytes(K)),
+                                                          _ptr(self.w1), _ptr(self.w1s), _ptr(self.w2),
+                                                          _ptr(self.w2s), None, ctypes.c_void_p(rid), R, E_l, k, K, N,
+                                                          _lib.MOE_FP8_SCALE_UE8M0 if self.scale_format == "ue8m0"
+                                                          else _lib.MOE_FP8_SCALE_FP32, None, ws, wsn, max_ctas,
+                                                          status, st_main), "moe_fused_experts_fp8_rows")
+            else:
+                _lib.check(lib.moe_expert_align_gather(dt, ctypes.c_void_p(rx), ctypes.c_void_p(rid), R, E_l, k, K,
+                                                       N, ws, wsn, st_main), "moe_expert_align_gather")
+                _lib.check(lib.moe_expert_gemm1(dt, _ptr(self.w1), R, E_l, k, K, N, ws, wsn, status, max_ctas,
+                                                st_main), "moe_expert_gemm1")
+                fused = self.p2p_fused_return if self.p2p_fused_return is not None else R <= 4096
+                if fused:
+                    _lib.check(lib.moe_p2p_expert_gemm2_return(dt, _ptr(self.w2), ws, wsn, E_l, K, N, k, W,
+                                                               self.rank, cap, pb, base, a["seq"], _ptr(a["scr_c"]),
+                                                               status, max_ctas, st_main),
+                               "moe_p2p_expert_gemm2_return")
+                else:
+                    _lib.check(lib.moe_expert_gemm2(dt, _ptr(self.w2), R, E_l, k, K, N, ws, wsn, status, max_ctas,
+                                                    st_main), "moe_expert_gemm2")
+            ev = torch.cuda.Event()
+            ev.record(main)
+            if not fused:  # the return of chunk c under the experts of chunk c + 1
+                with torch.cuda.stream(side):
+                    side.wait_event(ev)
+                    _lib.check(lib.moe_p2p_combine_experts_back(dt_rows, ws, E_l, K, N, k, W, self.rank, cap, pb,
+                                                                base, a["seq"], _ptr(a["scr_c"]), status, st_side),
+                               "moe_p2p_combine_experts_back")
+                    ev = torch.cuda.Event()
+                    ev.record(side)
+            ev_back.append(ev)
+        self._mark("experts")
+        if self.profile:
+            self._last_recv_ids = torch.cat(recv_ids)
+        out = torch.empty(M, K, dtype=x.dtype, device=dev)
+        for c, a in enumerate(arenas):
+            t0, t1 = bounds[c], bounds[c + 1]
+            main.wait_event(ev_back[c])
+            _lib.check(lib.moe_p2p_wait(a["base"], W, 2, a["cap"], K, k, a["seq"], status, st_main), "moe_p2p_wait")
+            if t1 > t0:  # NaN rows if any wait of this step gave up
+                _lib.check(lib.moe_p2p_reduce(dt, a["base"], _ptr(tok_rows[c]), t1 - t0, K, k, W, a["cap"],
+                                              _ptr(out[t0:t1]), status, st_main), "moe_p2p_reduce")
+        self._mark("combine_back")
         if self._p2p_status is None:
             self._p2p_status = (torch.zeros(1, dtype=torch.int32).pin_memory(), torch.cuda.Event())
         host, ev = self._p2p_status

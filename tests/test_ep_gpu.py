@@ -59,6 +59,11 @@ def _worker(rank, world, port, q, mode):
         if how in ("p2p", "p2psep"):
             # p2psep: the scatter GEMM and a separate combine-and-return kernel (the prefill-sized choice)
             kw.update(transport="p2p", max_tokens=400, p2p_fused_return=False if how == "p2psep" else None)
+        if how.startswith("p2pchunk"):
+            # two token chunks, one arena each: dispatch of chunk 1 and return of chunk 0 on a side
+            # stream under the experts (p2pchunk: separate return kernel, the prefill choice)
+            kw.update(transport="p2p", max_tokens=400, chunks=2, p2p_chunk_tokens=64,
+                      p2p_fused_return=how == "p2pchunkfused")
         if fp8:
             w1q, w1s = pkg.quantize_weights_fp8(w1)
             w2q, w2s = pkg.quantize_weights_fp8(w2)
@@ -102,7 +107,8 @@ def _worker(rank, world, port, q, mode):
         q.put((rank, "error", traceback.format_exc()))
 
 
-MODES = ["plain", "overlap", "replicate", "p2p", "p2psep", "fp8_plain", "fp8_overlap", "fp8_replicate", "fp8_p2p"]
+MODES = ["plain", "overlap", "replicate", "p2p", "p2psep", "p2pchunk", "p2pchunkfused", "fp8_plain", "fp8_overlap",
+         "fp8_replicate", "fp8_p2p", "fp8_p2pchunk"]
 
 
 @pytest.mark.parametrize("world", [1, 2])
@@ -111,7 +117,8 @@ def test_ep_matches_single_gpu(cuda_device, mode, world):
     """plain: one all-to-all each way; overlap: 2 token chunks on a side stream;
     replicate: the 5 busiest experts replicated on every rank (their pairs stay home);
     p2p: dispatch and combine by NVLink stores into the peers' arenas, three steps (p2psep:
-    with the down GEMM and the return as separate kernels);
+    with the down GEMM and the return as separate kernels; p2pchunk*: two token chunks with
+    one arena each, transfers on a side stream under the other chunk's experts);
     fp8_*: the same with e4m3 weights, the packed e4m3 token rows as the payload."""
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
@@ -166,8 +173,12 @@ def _launch_worker(port, q):
                     routed_scaling_factor=2.5)
         cases = {"nccl": dict(chunks=1), "nccl_2chunks": dict(chunks=2), "p2p": dict(transport="p2p", max_tokens=256),
                  "p2p_separate_return": dict(transport="p2p", max_tokens=256, p2p_fused_return=False),
+                 "p2p_2chunks": dict(transport="p2p", max_tokens=256, chunks=2, p2p_chunk_tokens=64,
+                                     p2p_fused_return=False),
                  "fp8_nccl": dict(chunks=1, use_fp8_w8a8=True), "fp8_p2p": dict(transport="p2p", max_tokens=256,
-                                                                                 use_fp8_w8a8=True)}
+                                                                                 use_fp8_w8a8=True),
+                 "fp8_p2p_2chunks": dict(transport="p2p", max_tokens=256, chunks=2, p2p_chunk_tokens=64,
+                                         use_fp8_w8a8=True)}
         out = {}
         for name, kw in cases.items():
             fp8 = kw.get("use_fp8_w8a8", False)

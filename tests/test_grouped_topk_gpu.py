@@ -73,6 +73,48 @@ def test_shapes_and_rules(cuda_device, E, ng, tg, k, scoring, renorm):
     _compare(g.numpy(), ids, w, (k, renorm, ng, tg, scoring, 1.0))
 
 
+@pytest.mark.parametrize("M", [64, 4096])
+@pytest.mark.parametrize("with_bias", [True, False])
+def test_exact_ties_follow_strict_order(cuda_device, M, with_bias):
+    """Logits (and bias) from small sets: exact ties at the group and expert boundaries on
+    most rows, so the order (value descending, index ascending) alone decides, on every row.
+    Every 7th row is constant, so all 128 kept experts tie at the threshold (more candidates
+    than one per lane; the kernel's fallback selection)."""
+    gen = torch.Generator().manual_seed(7 + M)
+    g = torch.randint(-2, 3, (M, 256), generator=gen).float() / 2
+    g[::7] = 0.25
+    bias = (torch.randint(0, 2, (256,), generator=gen).float() * 0.01) if with_bias else None
+    w, ids = grouped_topk(None, g.to(cuda_device), 8, True, 8, 4, "sigmoid", 2.5,
+                          e_score_correction_bias=None if bias is None else bias.to(cuda_device))
+    rw, rids = grouped_topk_ref(g.numpy(), 8, True, 8, 4, "sigmoid", 2.5,
+                                e_score_correction_bias=None if bias is None else bias.numpy(),
+                                group_score="top2sum" if with_bias else "max")
+    np.testing.assert_array_equal(ids.cpu().numpy(), rids)
+    np.testing.assert_allclose(w.cpu().numpy(), rw, rtol=0, atol=W_ATOL)
+
+
+@pytest.mark.parametrize("quantised", [False, True])
+def test_register_kernel_matches_general_kernel(cuda_device, quantised):
+    """E = 256: the register kernel (threshold top-k selection) and the general kernel
+    (shared-memory group pass, arg-max rounds; taken when the logits are not 16-byte
+    aligned) give the same bits, with Gaussian logits and with tie-heavy ones."""
+    M = 4096
+    gen = torch.Generator().manual_seed(99)
+    g = (torch.randint(-2, 3, (M, 256), generator=gen).float() / 2) if quantised else torch.randn(M, 256, generator=gen)
+    bias = torch.randn(256, generator=gen) * 0.01
+    if quantised:
+        bias = (bias > 0).float() * 0.01
+    gd = g.to(cuda_device)
+    buf = torch.empty(M * 256 + 1, device=cuda_device)
+    mis = buf[1:].view(M, 256)  # 4-byte offset: not 16-byte aligned
+    mis.copy_(gd)
+    b = bias.to(cuda_device)
+    for tg in (4, 2):
+        w, ids = grouped_topk(None, gd, 8, True, 8, tg, "sigmoid", 2.5, e_score_correction_bias=b)
+        w2, ids2 = grouped_topk(None, mis, 8, True, 8, tg, "sigmoid", 2.5, e_score_correction_bias=b)
+        assert torch.equal(ids, ids2) and torch.equal(w, w2)
+
+
 def test_full_size_properties(cuda_device):
     """M = 32768 (the expert-parallel config): properties on all rows, oracle on a sample."""
     M = 32768

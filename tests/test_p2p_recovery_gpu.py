@@ -61,7 +61,7 @@ def _worker(port, q):
         torch.cuda.synchronize()
         assert torch.equal(good, ref)
         # a peer that never answers: wait for a disp flag value nothing will write
-        p = layer._p2p
+        p = layer._p2p[0]
         lib = _lib.load()
         st = _stream(dev)
         _lib.check(lib.moe_p2p_wait(ctypes.c_void_p(p["base"]), 1, 1, p["cap"], K, k, p["seq"] + 1000,
