@@ -93,14 +93,16 @@ __device__ __forceinline__ void route_select_sorted8(const float (&c)[8], const 
 
 // Per-warp shared memory of route_select_threshold8.
 struct RouteScratch {
-  uint64_t key[32];   // compacted candidates, one per lane
-  float s[32];        // their scores
+  uint64_t key[32];   // the compacted candidates' selection keys, one per lane
+  float c[32];        // compacted candidates: ranking value,
+  float s[32];        // score,
+  int32_t id[32];     // expert
   float sel_s[32];    // the chosen experts' scores, in rank order
   int32_t sel_id[32]; // the chosen experts, in rank order
 };
 
 // Top-k selection by threshold for E = 256 with group masking. Every kept group's two best
-// values are >= tkey's value (the smallest second-best of the kept groups), and those are
+// values are >= t (the smallest second-best of the kept groups), and those are
 // 2 * topk_group >= topk values, so the k-th best kept value is >= it and nothing below it
 // can be chosen. The candidates at or above it (about 8-16 per token for Gaussian logits)
 // are compacted one per lane in shared memory; each lane's rank is the number of
@@ -110,12 +112,13 @@ struct RouteScratch {
 // Returns false (nothing written) when more than 32 candidates pass; the caller then runs
 // route_select_sorted8.
 __device__ __forceinline__ bool route_select_threshold8(const float (&c)[8], const float (&s)[8], int e0, int lane,
-                                                        bool kept, uint32_t tkey, int64_t tok, int topk,
+                                                        bool kept, float t, int64_t tok, int topk,
                                                         int renormalize, float scale, float* __restrict__ out_w,
                                                         int32_t* __restrict__ out_ids, RouteScratch* scr) {
+  // !(c < t): c >= t, or c is NaN (NaN sorts above every number in the key order)
   uint32_t m = 0;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) m |= (kept && ordered_key(c[i]) >= tkey) ? (1u << i) : 0u;
+  for (int i = 0; i < 8; ++i) m |= (kept && !(c[i] < t)) ? (1u << i) : 0u;
   const int cnt = __popc(m);
   const int n = (int)__reduce_add_sync(0xffffffffu, (unsigned)cnt);
   if (n > 32) return false;
@@ -129,14 +132,17 @@ __device__ __forceinline__ bool route_select_threshold8(const float (&c)[8], con
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     if ((m >> i) & 1u) {
-      scr->key[pre] = route_key(c[i], e0 + i);
+      scr->c[pre] = c[i];
       scr->s[pre] = s[i];
+      scr->id[pre] = e0 + i;
       ++pre;
     }
   }
   __syncwarp();
-  const uint64_t key = lane < n ? scr->key[lane] : 0ull;
+  const uint64_t key = lane < n ? route_key(scr->c[lane], scr->id[lane]) : 0ull;
   const float sv = lane < n ? scr->s[lane] : 0.f;
+  scr->key[lane] = key;
+  __syncwarp();
   int rank = 0;
   for (int j = 0; j < n; ++j) rank += scr->key[j] > key ? 1 : 0;
   if (lane < n && rank < topk) {
@@ -280,17 +286,20 @@ __device__ __forceinline__ void route_token_values(const float (&x)[VPL], const 
     }
     const float gs = (gmode == MOE_GROUP_SCORE_MAX) ? b1 : b1 + b2;
     const int my_g = lane / LPG;
-    int rank = 0;
-    for (int h = 0; h < n_group; ++h) {
-      const float o = __shfl_sync(0xffffffffu, gs, h * LPG);
-      rank += (o > gs) || (o == gs && h < my_g);
+    // keep the topk_group best groups (score descending, group index ascending): per round
+    // the largest remaining score, then the lowest group holding it
+    const uint32_t gk = ordered_key(gs);
+    bool kept = false;
+    for (int r = 0; r < topk_group; ++r) {
+      const uint32_t hmax = __reduce_max_sync(0xffffffffu, kept ? 0u : gk);
+      const int gmin = (int)__reduce_min_sync(0xffffffffu, (!kept && gk == hmax) ? (unsigned)my_g : 0xffffffffu);
+      kept = kept || my_g == gmin;
     }
-    const bool kept = rank < topk_group;
     if constexpr (VPL == 8) {
       if (scr != nullptr && 2 * topk_group >= topk) {
         const uint32_t tkey = __reduce_min_sync(0xffffffffu, kept ? ordered_key(b2) : 0xffffffffu);
-        if (route_select_threshold8(c, s, e0, lane, kept, tkey, tok, topk, renormalize, scale, out_w, out_ids,
-                                    scr))
+        const float t = __uint_as_float((tkey & 0x80000000u) ? (tkey & 0x7fffffffu) : ~tkey);
+        if (route_select_threshold8(c, s, e0, lane, kept, t, tok, topk, renormalize, scale, out_w, out_ids, scr))
           return;
       }
     }
