@@ -225,15 +225,13 @@ p2p_combine_back_kernel(const uint4* __restrict__ partial, int K, int world, int
   if (threadIdx.x == 0) *done = 0;
 }
 
-constexpr int kSlotBatch = 8;
-
-// The expert path's top-k combine fused with the return trip: for received row t
-// (region src = t / cap, row r = t % cap, r < counts[src]) the weighted sum of its k slot
-// rows of y_slots is stored straight into rank src's back_x region `me`, row r. A
-// persistent grid (2 CTAs per SM, all resident) strides over the 16-byte vectors of all rows, so each
-// CTA issues its system-scope fence once (a fence per short-lived CTA costs an NVLink
-// round trip each);
-// the last CTA raises back[me] in every rank.
+// The expert path's top-k combine fused with the return trip, one warp per received row:
+// for row t (region src = t / cap, row r = t % cap, r < counts[src]) the lanes read the
+// row's k ids and weights once, then the weighted sum of its valid slot rows of y_slots
+// (slots in order, fmaf per slot: the bits of combine_kernel) is stored 16 bytes per lane
+// straight into rank src's back_x region `me`, row r, four vectors per lane at a time
+// with the loads of a slot issued before its FMAs. The grid strides over the rows; each
+// CTA issues its system-scope fence once; the last CTA raises back[me] in every rank.
 template <typename T>
 __global__ void __launch_bounds__(kP2PThreads)
 p2p_combine_experts_back_kernel(const uint4* __restrict__ y, const float* __restrict__ w,
@@ -245,49 +243,55 @@ p2p_combine_experts_back_kernel(const uint4* __restrict__ y, const float* __rest
   if (failed(status)) return;
   for (int i = threadIdx.x; i < world; i += blockDim.x) s_cnt[i] = __ldcg(own_counts + i);
   __syncthreads();
-  const int64_t total = (int64_t)world * cap * vpr;
-  for (int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; gid < total;
-       gid += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t t = gid / vpr;
-    const int v = (int)(gid - t * vpr);
+  const int lane = threadIdx.x & 31;
+  const int64_t rows = (int64_t)world * cap;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t t = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; t < rows; t += nwarps) {
     const int src = (int)(t / cap);
     const int64_t r = t - (int64_t)src * cap;
-    if (r >= s_cnt[src]) continue;
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    // slots in batches of kSlotBatch: every load of a batch is issued before the first FMA
-    // (the threads of a persistent grid get their memory parallelism from here); the FMAs
-    // then run in slot order, as in combine_kernel, so the sums are the same bits
-    for (int j0 = 0; j0 < topk; j0 += kSlotBatch) {
-      uint4 q[kSlotBatch];
-      float wj[kSlotBatch];
-      bool ok[kSlotBatch];
+    if (r >= s_cnt[src]) continue;  // warp-uniform
+    const int e = lane < topk ? __ldg(ids + t * topk + lane) : -1;
+    const float my_w = lane < topk ? __ldg(w + t * topk + lane) : 0.f;
+    const uint32_t valid = __ballot_sync(0xffffffffu, e >= 0 && e < E);
+    uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<char*>(peer_base[src]) + lay.back_x) +
+                 ((int64_t)me * cap + r) * vpr;
+    const uint4* yr = y + t * topk * (int64_t)vpr;
+    for (int v0 = lane; v0 < vpr; v0 += 128) {
+      float acc[4][8];
 #pragma unroll
-      for (int b = 0; b < kSlotBatch; ++b) {
-        const int j = j0 + b;
-        const int e = j < topk ? __ldg(ids + t * topk + j) : -1;
-        ok[b] = e >= 0 && e < E;
-        wj[b] = ok[b] ? __ldg(w + t * topk + j) : 0.f;
-        q[b] = ok[b] ? __ldg(y + (t * topk + j) * vpr + v) : make_uint4(0u, 0u, 0u, 0u);
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[u][i] = 0.f;
+      for (uint32_t m = valid; m; m &= m - 1) {  // slots in order
+        const int j = __ffs(m) - 1;
+        const float wj = __shfl_sync(0xffffffffu, my_w, j);
+        const uint4* ys = yr + (int64_t)j * vpr;
+        uint4 q[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) q[u] = v0 + 32 * u < vpr ? __ldg(ys + v0 + 32 * u) : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const uint32_t h[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = ElemTraits<T>::unpack2(h[i]);
+            acc[u][2 * i] = fmaf(wj, f.x, acc[u][2 * i]);
+            acc[u][2 * i + 1] = fmaf(wj, f.y, acc[u][2 * i + 1]);
+          }
+        }
       }
 #pragma unroll
-      for (int b = 0; b < kSlotBatch; ++b) {
-        if (!ok[b]) continue;
-        const uint32_t u[4] = {q[b].x, q[b].y, q[b].z, q[b].w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 f = ElemTraits<T>::unpack2(u[i]);
-          acc[2 * i] = fmaf(wj[b], f.x, acc[2 * i]);
-          acc[2 * i + 1] = fmaf(wj[b], f.y, acc[2 * i + 1]);
+      for (int u = 0; u < 4; ++u) {
+        if (v0 + 32 * u < vpr) {
+          uint4 o;
+          o.x = ElemTraits<T>::pack2(acc[u][0], acc[u][1]);
+          o.y = ElemTraits<T>::pack2(acc[u][2], acc[u][3]);
+          o.z = ElemTraits<T>::pack2(acc[u][4], acc[u][5]);
+          o.w = ElemTraits<T>::pack2(acc[u][6], acc[u][7]);
+          dst[v0 + 32 * u] = o;
         }
       }
     }
-    uint4 o;
-    o.x = ElemTraits<T>::pack2(acc[0], acc[1]);
-    o.y = ElemTraits<T>::pack2(acc[2], acc[3]);
-    o.z = ElemTraits<T>::pack2(acc[4], acc[5]);
-    o.w = ElemTraits<T>::pack2(acc[6], acc[7]);
-    uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<char*>(peer_base[src]) + lay.back_x);
-    dst[((int64_t)me * cap + r) * vpr + v] = o;
   }
   __threadfence_system();
   __syncthreads();
@@ -454,7 +458,8 @@ extern "C" int moe_p2p_combine_experts_back(int dtype, const void* workspace, in
   const uint4* y = reinterpret_cast<const uint4*>(static_cast<const char*>(workspace) + y_off);
   const char* ob = static_cast<const char*>(own_base);
   const int vpr = hidden_size / 8;
-  const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div(R * vpr, kP2PThreads), 2 * num_sms()));
+  // one warp per received row; up to 4 CTAs of 8 warps per SM (64 registers)
+  const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div(R * 32, kP2PThreads), 4 * num_sms()));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const float* w = reinterpret_cast<const float*>(ob + l.recv_w);
   const int32_t* ids = reinterpret_cast<const int32_t*>(ob + l.recv_id);
