@@ -922,3 +922,4 @@ class ExpertParallelMoE:
     def close(self):
         self._p2p_release()
         self._ws = None
+        self._ws_chunks = []
